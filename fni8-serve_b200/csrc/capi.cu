@@ -1,0 +1,216 @@
+// Library plumbing behind include/fni8_b200.h: status strings, thread-local error
+// messages, TMA descriptor encoding (through the runtime's driver entry point, so the
+// library does not link libcuda and loads on machines without a GPU), and the dense
+// GEMM / linear entry points that pick between the tile kernel (gemm_tile.cu) and the
+// skinny stream-K kernel (gemm_stream.cu).
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "fni8_common.cuh"
+#include "gemm_internal.h"
+
+namespace fni8h {
+
+static thread_local char g_msg[512] = "";
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  return fail(FNI8_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+int current_device() {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+
+int num_sms(int device) {
+  static int cache[kMaxDevices] = {};
+  if (device < 0 || device >= kMaxDevices) return 148;
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0) n = 148;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+static int encode(CUtensorMap* map, const void* base, cuuint32_t rank, const cuuint64_t* dims,
+                  const cuuint64_t* strides, const cuuint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(FNI8_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (no CUDA driver?)");
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return fail(FNI8_ERR_ALIGN, "TMA base must be 16-byte aligned");
+  for (cuuint32_t i = 0; i + 1 < rank; ++i)
+    if (strides[i] % 16 != 0) return fail(FNI8_ERR_ALIGN, "TMA stride %llu not a multiple of 16 bytes",
+                                          (unsigned long long)strides[i]);
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FNI8_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FNI8_OK;
+}
+
+int encode_tmap_2d_i8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                      uint32_t box_inner, uint32_t box_outer) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  return encode(map, base, 2, dims, strides, box);
+}
+
+int encode_tmap_3d_i8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
+                      uint64_t stride2, uint32_t box0, uint32_t box1) {
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {stride1, stride2};
+  const cuuint32_t box[3] = {box0, box1, 1};
+  return encode(map, base, 3, dims, strides, box);
+}
+
+// Shape/pointer checks shared by the dense GEMM entry points.
+static int check_gemm(const int8_t* a, const int8_t* w, const void* out, int64_t M, int64_t N, int64_t K) {
+  if (M < 0 || N <= 0 || K <= 0) return fail(FNI8_ERR_INVALID, "bad GEMM shape M=%lld N=%lld K=%lld", (long long)M,
+                                              (long long)N, (long long)K);
+  if (K % 16 != 0) return fail(FNI8_ERR_UNSUPPORTED, "K=%lld must be a multiple of 16", (long long)K);
+  if (M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31))
+    return fail(FNI8_ERR_UNSUPPORTED, "GEMM dimensions must be < 2^31");
+  if (M > 0 && (a == nullptr || w == nullptr || out == nullptr)) return fail(FNI8_ERR_INVALID, "null GEMM operand");
+  return FNI8_OK;
+}
+
+static int pick_path(int path, int64_t M, size_t ws_bytes, int64_t N, int64_t K) {
+  if (path == FNI8_PATH_TILE || path == FNI8_PATH_STREAM) return path;
+  if (M <= 64 && ws_bytes >= stream_workspace_bytes(M, N, K)) return FNI8_PATH_STREAM;
+  return FNI8_PATH_TILE;
+}
+
+static int pick_bn(int64_t M, int64_t N) {
+  const int64_t tiles256 = ((M + 127) / 128) * ((N + 255) / 256);
+  return tiles256 >= 2 * num_sms(current_device()) ? 256 : 128;
+}
+
+static int gemm_any(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
+                    const void* residual, void* out, int mode, int64_t M, int64_t N, int64_t K, int path, void* ws,
+                    size_t ws_bytes, cudaStream_t st) {
+  const int p = pick_path(path, M, ws_bytes, N, K);
+  if (p == FNI8_PATH_STREAM)
+    return stream_gemm(a, a_scale, w, w_scale, bias, residual, out, mode, M, N, K, ws, ws_bytes, st);
+  return tile_gemm(a, a_scale, w, w_scale, bias, residual, out, mode, M, N, K, pick_bn(M, N), st);
+}
+
+}  // namespace fni8h
+
+using namespace fni8h;
+
+extern "C" int fni8_abi_version(void) { return FNI8_ABI_VERSION; }
+
+extern "C" const char* fni8_status_string(int status) {
+  switch (status) {
+    case FNI8_OK: return "ok";
+    case FNI8_ERR_INVALID: return "invalid argument";
+    case FNI8_ERR_UNSUPPORTED: return "unsupported";
+    case FNI8_ERR_ALIGN: return "misaligned pointer or stride";
+    case FNI8_ERR_CUDA: return "CUDA error";
+    case FNI8_ERR_WORKSPACE: return "workspace missing or too small";
+    case FNI8_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+extern "C" const char* fni8_last_error_message(void) { return g_msg; }
+
+extern "C" int fni8_device_status(int* code_out) {
+  if (code_out == nullptr) return fail(FNI8_ERR_INVALID, "null code_out");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e, "cudaDeviceSynchronize");
+  int a = 0, b = 0;
+  if (int s = tile_status_read_and_clear(&a)) return s;
+  if (int s = stream_status_read_and_clear(&b)) return s;
+  *code_out = a != 0 ? a : b;
+  return *code_out == 0 ? FNI8_OK : fail(FNI8_ERR_DEVICE_TIMEOUT, "device watchdog code 0x%x", *code_out);
+}
+
+extern "C" size_t fni8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  return stream_workspace_bytes(M, N, K);
+}
+
+extern "C" int fni8_workspace_init(void* workspace, size_t bytes, void* stream) {
+  if (bytes == 0) return FNI8_OK;
+  if (workspace == nullptr) return fail(FNI8_ERR_INVALID, "null workspace");
+  cudaError_t e = cudaMemsetAsync(workspace, 0, bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_status(e, "cudaMemsetAsync(workspace)");
+  return FNI8_OK;
+}
+
+extern "C" int fni8_gemm_w8a8_ex(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                                 const void* bias, const void* residual, void* out, int out_dtype, int64_t M,
+                                 int64_t N, int64_t K, int path, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
+  if (int s = check_gemm(a, w, out, M, N, K)) return s;
+  if (out_dtype != FNI8_F16 && out_dtype != FNI8_BF16)
+    return fail(FNI8_ERR_INVALID, "out_dtype %d: expected F16 or BF16", out_dtype);
+  if (path < FNI8_PATH_AUTO || path > FNI8_PATH_STREAM) return fail(FNI8_ERR_INVALID, "unknown path %d", path);
+  if (M > 0 && (a_scale == nullptr || w_scale == nullptr)) return fail(FNI8_ERR_INVALID, "null scale");
+  if (path == FNI8_PATH_STREAM && M > kStreamMaxM)
+    return fail(FNI8_ERR_UNSUPPORTED, "stream path takes M <= %lld", (long long)kStreamMaxM);
+  if (M == 0) return FNI8_OK;
+  return gemm_any(a, a_scale, w, w_scale, bias, residual, out, out_dtype == FNI8_F16 ? 0 : 1, M, N, K, path,
+                  workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fni8_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                              const void* bias, const void* residual, void* out, int out_dtype, int64_t M, int64_t N,
+                              int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+  return fni8_gemm_w8a8_ex(a, a_scale, w, w_scale, bias, residual, out, out_dtype, M, N, K, FNI8_PATH_AUTO,
+                           workspace, workspace_bytes, stream);
+}
+
+extern "C" int fni8_gemm_w8a8_i32(const int8_t* a, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
+                                  int path, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int s = check_gemm(a, w, acc, M, N, K)) return s;
+  if (path < FNI8_PATH_AUTO || path > FNI8_PATH_STREAM) return fail(FNI8_ERR_INVALID, "unknown path %d", path);
+  if (path == FNI8_PATH_STREAM && M > kStreamMaxM)
+    return fail(FNI8_ERR_UNSUPPORTED, "stream path takes M <= %lld", (long long)kStreamMaxM);
+  if (M == 0) return FNI8_OK;
+  return gemm_any(a, nullptr, w, nullptr, nullptr, nullptr, acc, 2, M, N, K, path, workspace, workspace_bytes,
+                  static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fni8_linear_w8a8(const void* x, int dtype, const int8_t* w, const float* w_scale, const void* bias,
+                                void* out, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != FNI8_F16 && dtype != FNI8_BF16) return fail(FNI8_ERR_INVALID, "dtype %d: expected F16 or BF16", dtype);
+  if (int s = check_gemm(q_scratch, w, out, M, N, K)) return s;
+  if (M == 0) return FNI8_OK;
+  if (x == nullptr || w_scale == nullptr || s_scratch == nullptr) return fail(FNI8_ERR_INVALID, "null linear operand");
+  if (int st = fni8_quantize_rows_i8(x, dtype, M, K, q_scratch, s_scratch, stream)) return st;
+  return gemm_any(q_scratch, s_scratch, w, w_scale, bias, nullptr, out, dtype == FNI8_F16 ? 0 : 1, M, N, K,
+                  FNI8_PATH_AUTO, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,29 @@
+// Host-side functions shared between the translation units of libfni8_b200.so. Not part
+// of the public C ABI (include/fni8_b200.h).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fni8h {
+
+constexpr int kMaxDevices = 64;
+constexpr int kTileMaxSeg = 512;  // segments of one grouped launch
+
+// tcgen05 tile GEMM (gemm_tile.cu). out_mode: 0 fp16, 1 bf16, 2 int32 accumulators.
+int tile_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
+              const void* residual, void* out, int out_mode, int64_t M, int64_t N, int64_t K, int bn,
+              cudaStream_t st);
+int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w, const float* w_scale,
+                      int64_t E, int64_t N, int64_t K, const int32_t* seg_expert, const int32_t* seg_off,
+                      const int32_t* seg_cnt, int64_t S, void* out, int out_mode, int bn, cudaStream_t st);
+int tile_status_read_and_clear(int* code);
+
+// Swap-AB stream-K GEMM for skinny M (gemm_stream.cu).
+size_t stream_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int stream_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
+                const void* residual, void* out, int out_mode, int64_t M, int64_t N, int64_t K, void* ws,
+                size_t ws_bytes, cudaStream_t st);
+int stream_status_read_and_clear(int* code);
+constexpr int64_t kStreamMaxM = 256;
+
+}  // namespace fni8h

@@ -1,0 +1,482 @@
+// Dense and grouped W8A8 GEMM on the 5th-generation tensor cores (sm_100a).
+//
+//   out[m, n] = dtype((float(sum_k a[m,k] * w[n,k]) * a_scale[m]) * w_scale[n] (+ bias[n]) (+ res[m,n]))
+//
+// Design (one persistent CTA per SM, 6 warps, warp-specialised):
+//   warp 0      TMA producer: 128 x 128-byte tiles of A (activations) and BN x 128-byte
+//               tiles of W (weights), 128-byte swizzled, into a STAGES-deep smem ring.
+//   warp 1      allocates TMEM (2 x BN columns = a double-buffered int32 accumulator)
+//               and, from one thread, issues tcgen05.mma.kind::i8 (M=128, N=BN, K=32;
+//               4 per 128-byte stage); tcgen05.commit frees smem stages and publishes
+//               finished accumulators.
+//   warps 2-5   epilogue: tcgen05.ld of one accumulator row per thread, fp32 dequant
+//               (+bias, +residual), rounding to fp16/bf16 (or raw int32), global stores.
+//               The other accumulator buffer is being filled meanwhile.
+// Tiles are visited in bands of kGroupM m-tiles so a wave of 148 CTAs reuses the same
+// A rows and W columns out of the 126 MB L2.
+//
+// GROUPED: the A rows are split into segments (one per expert, or per (source rank,
+// expert) pair under expert parallelism); segment s multiplies rows
+// [off[s], off[s]+cnt[s]) by expert exp[s] of a [E, N, K] weight stack (3-D TMA map).
+// A tile may load rows past its segment's end (they belong to the next segment); the
+// epilogue simply does not store them.
+//
+// Every mbarrier wait is bounded (fni8_common.cuh); on a timeout the roles leave their
+// loops, drain in-flight TMA loads and MMAs (bounded), free TMEM and exit, and the host
+// sees FNI8_ERR_DEVICE_TIMEOUT from fni8_device_status().
+#include "fni8_common.cuh"
+#include "gemm_internal.h"
+
+namespace fni8b {
+namespace tile {
+
+constexpr int BM = 128;
+constexpr int BK = 128;  // bytes == int8 elements per stage along K
+constexpr int kThreads = 192;
+constexpr int kMaxSeg = fni8h::kTileMaxSeg;
+constexpr int kGroupM = 16;
+
+static __device__ int g_status;  // watchdog word of this file
+
+enum : int { kCodeProducer = 0x101, kCodeMma = 0x102, kCodeEpilogue = 0x103, kCodeDrain = 0x104 };
+enum : int { kOutF16 = 0, kOutBF16 = 1, kOutI32 = 2 };
+
+struct Epi {
+  const float* a_scale;  // [rows]
+  const float* w_scale;  // [N] or [E, N]
+  const void* bias;      // [N] (out dtype) or null
+  const void* residual;  // [rows, N] (out dtype) or null
+  void* out;             // [rows, N]
+  int mode;              // kOutF16 / kOutBF16 / kOutI32
+};
+struct Groups {
+  const int32_t* expert;
+  const int32_t* off;
+  const int32_t* cnt;
+  int S;
+};
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 512;
+  static constexpr int SEG_BYTES = (kMaxSeg + 1 + 3 * kMaxSeg) * 4;
+  static constexpr int SMEM = 1024 + STAGES * STAGE + BAR_BYTES + SEG_BYTES;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+};
+
+struct TileCoord {
+  int row0;        // first A row of the tile (TMA y)
+  int rows_valid;  // rows of this tile that belong to it (<= 128)
+  int n_blk;
+  int expert;
+};
+
+template <bool GROUPED>
+__device__ __forceinline__ TileCoord decode_tile(int t, int M, int m_tiles, int n_tiles, const int32_t* prefix,
+                                                 const int32_t* soff, const int32_t* scnt, const int32_t* sexp,
+                                                 int S) {
+  TileCoord tc;
+  if constexpr (GROUPED) {
+    const int mt = t / n_tiles;
+    tc.n_blk = t - mt * n_tiles;
+    int lo = 0, hi = S - 1;  // largest s with prefix[s] <= mt
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (prefix[mid] <= mt) lo = mid;
+      else hi = mid - 1;
+    }
+    const int ml = mt - prefix[lo];
+    tc.row0 = soff[lo] + ml * BM;
+    tc.rows_valid = min(BM, scnt[lo] - ml * BM);
+    tc.expert = sexp[lo];
+  } else {
+    const int band_tiles = kGroupM * n_tiles;
+    const int band = t / band_tiles;
+    const int first_m = band * kGroupM;
+    const int gm = min(kGroupM, m_tiles - first_m);
+    const int local = t - band * band_tiles;
+    const int m_blk = first_m + local % gm;
+    tc.n_blk = local / gm;
+    tc.row0 = m_blk * BM;
+    tc.rows_valid = min(BM, M - tc.row0);
+    tc.expert = 0;
+  }
+  return tc;
+}
+
+template <typename T>
+__device__ __forceinline__ void store_chunk(const Epi& epi, const uint32_t (&r)[32], int64_t row, int n0, int N,
+                                            float a_s, const float* wsc, bool vec_ok) {
+  T* out = static_cast<T*>(epi.out) + row * static_cast<int64_t>(N);
+  const T* bias = static_cast<const T*>(epi.bias);
+  const T* res = epi.residual ? static_cast<const T*>(epi.residual) + row * static_cast<int64_t>(N) : nullptr;
+  if (vec_ok && n0 + 32 <= N) {
+    float ws[32];
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(wsc + n0 + j));
+      ws[j] = f.x;
+      ws[j + 1] = f.y;
+      ws[j + 2] = f.z;
+      ws[j + 3] = f.w;
+    }
+#pragma unroll
+    for (int j8 = 0; j8 < 32; j8 += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j8 + j])), a_s), ws[j8 + j]);
+      if (bias != nullptr) {
+        const uint4 b = __ldg(reinterpret_cast<const uint4*>(bias + n0 + j8));
+        const T* bb = reinterpret_cast<const T*>(&b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], to_f32<T>(bb[j]));
+      }
+      if (res != nullptr) {
+        const uint4 b = __ldg(reinterpret_cast<const uint4*>(res + n0 + j8));
+        const T* bb = reinterpret_cast<const T*>(&b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], to_f32<T>(bb[j]));
+      }
+      uint4 o;
+      T* oo = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) oo[j] = from_f32<T>(v[j]);
+      *reinterpret_cast<uint4*>(out + n0 + j8) = o;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = n0 + j;
+      if (n < N) {
+        float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), a_s), __ldg(wsc + n));
+        if (bias != nullptr) v = __fadd_rn(v, to_f32<T>(bias[n]));
+        if (res != nullptr) v = __fadd_rn(v, to_f32<T>(res[n]));
+        out[n] = from_f32<T>(v);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void store_chunk_i32(const Epi& epi, const uint32_t (&r)[32], int64_t row, int n0, int N,
+                                                bool vec_ok) {
+  int32_t* out = static_cast<int32_t*>(epi.out) + row * static_cast<int64_t>(N);
+  if (vec_ok && n0 + 32 <= N) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      *reinterpret_cast<int4*>(out + n0 + j) = make_int4((int)r[j], (int)r[j + 1], (int)r[j + 2], (int)r[j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < N) out[n0 + j] = static_cast<int32_t>(r[j]);
+  }
+}
+
+template <int BN, bool GROUPED>
+__global__ void __launch_bounds__(kThreads, 1)
+    w8a8_tile_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Epi epi,
+                     Groups grp, int M, int N, int K, int vec_ok) {
+  using C = Cfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE);
+  uint64_t* full = bars;
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  int32_t* prefix = reinterpret_cast<int32_t*>(smem + C::STAGES * C::STAGE + C::BAR_BYTES);
+  int32_t* soff = prefix + kMaxSeg + 1;
+  int32_t* scnt = soff + kMaxSeg;
+  int32_t* sexp = scnt + kMaxSeg;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);  // one arrive per epilogue warp
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+
+  // Everything above touched only on-chip state; from here on we read upstream results.
+  pdl_wait();
+
+  const int n_tiles = (N + BN - 1) / BN;
+  const int m_tiles = (M + BM - 1) / BM;
+  const int kb = (K + BK - 1) / BK;
+  int S = 0;
+  if constexpr (GROUPED) {
+    S = grp.S;
+    for (int i = threadIdx.x; i < S; i += kThreads) {
+      soff[i] = grp.off[i];
+      scnt[i] = max(grp.cnt[i], 0);
+      sexp[i] = grp.expert[i];
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int carry = 0;
+      if (lane == 0) prefix[0] = 0;
+      for (int base = 0; base < S; base += 32) {
+        const int i = base + lane;
+        int v = (i < S) ? (scnt[i] + BM - 1) / BM : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int u = __shfl_up_sync(0xffffffffu, v, o);
+          if (lane >= o) v += u;
+        }
+        if (i < S) prefix[i + 1] = carry + v;
+        carry += __shfl_sync(0xffffffffu, v, 31);
+      }
+    }
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total = GROUPED ? prefix[S] * n_tiles : m_tiles * n_tiles;
+
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t ph = 0;
+      uint32_t armed = 0;  // parity each stage was last armed with (bit per stage)
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const TileCoord tc = decode_tile<GROUPED>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
+        for (int k = 0; k < kb; ++k) {
+          if (!mbar_wait(&empty[stage], ph ^ 1u, &g_status, kCodeProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * C::STAGE;
+          uint8_t* sb = sa + C::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], C::STAGE);
+          tma_load_2d(&tmA, &full[stage], sa, k * BK, tc.row0);
+          if constexpr (GROUPED) tma_load_3d(&tmB, &full[stage], sb, k * BK, tc.n_blk * BN, tc.expert);
+          else tma_load_2d(&tmB, &full[stage], sb, k * BK, tc.n_blk * BN);
+          armed = (armed & ~(1u << stage)) | (ph << stage);
+          ++issued;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Drain: the loads of the last min(issued, STAGES) stages must have landed before
+      // the CTA may exit (normally they have: the MMA consumed them).
+      const int pending = issued < C::STAGES ? issued : C::STAGES;
+      for (int i = 0; i < pending; ++i) {
+        const int s = (stage - 1 - i + 2 * C::STAGES) % C::STAGES;
+        mbar_wait(&full[s], (armed >> s) & 1u, &g_status, kCodeDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = idesc_i8(BM, BN);
+      int stage = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t aph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], aph ^ 1u, &g_status, kCodeMma)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int k = 0; k < kb; ++k) {
+          if (!mbar_wait(&full[stage], ph, &g_status, kCodeMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* sa = smem + stage * C::STAGE;
+          const uint64_t adesc = sw128_kmajor_desc(smem_u32(sa));
+          const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sa + C::A_BYTES));
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            // advance the start address by kk * 32 bytes inside the 128-byte swizzle atom
+            umma_i8(d, adesc + static_cast<uint64_t>(kk * 2), bdesc + static_cast<uint64_t>(kk * 2), kIdesc,
+                    (k | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) aph ^= 1u;
+      }
+      // All MMAs issued by this thread must retire before TMEM is freed.
+      umma_commit(drain);
+      mbar_wait(drain, 0, &g_status, kCodeDrain);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lanes [32q, 32q+32) are reachable from this warp
+    const int row_local = q * 32 + lane;
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const TileCoord tc = decode_tile<GROUPED>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
+      int ok = 0;
+      if (lane == 0) ok = mbar_wait(&tfull[acc], aph, &g_status, kCodeEpilogue) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      const bool valid = row_local < tc.rows_valid;
+      const int64_t row = static_cast<int64_t>(tc.row0) + row_local;
+      const float a_s = (valid && epi.mode != kOutI32) ? __ldg(epi.a_scale + row) : 0.0f;
+      const float* wsc = epi.w_scale + static_cast<int64_t>(tc.expert) * N;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tbase + static_cast<uint32_t>(c), r);
+        tmem_ld_wait();
+        const int n0 = tc.n_blk * BN + c;
+        if (valid && n0 < N) {
+          if (epi.mode == kOutF16) store_chunk<__half>(epi, r, row, n0, N, a_s, wsc, vec_ok != 0);
+          else if (epi.mode == kOutBF16) store_chunk<__nv_bfloat16>(epi, r, row, n0, N, a_s, wsc, vec_ok != 0);
+          else store_chunk_i32(epi, r, row, n0, N, vec_ok != 0);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) aph ^= 1u;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <int BN, bool GROUPED>
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Epi& epi, const Groups& grp, int M, int N, int K,
+           int grid, bool vec_ok, cudaStream_t st) {
+  using C = Cfg<BN>;
+  auto kern = w8a8_tile_kernel<BN, GROUPED>;
+  static bool configured[fni8h::kMaxDevices] = {};  // the attribute is set per device
+  const int dev = fni8h::current_device();
+  if (dev < 0 || dev >= fni8h::kMaxDevices) return fni8h::fail(FNI8_ERR_CUDA, "no current CUDA device");
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return fni8h::cuda_status(e, "cudaFuncSetAttribute(tile gemm)");
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, epi, grp, M, N, K, vec_ok ? 1 : 0);
+  if (e != cudaSuccess) return fni8h::cuda_status(e, "launch tile gemm");
+  return FNI8_OK;
+}
+
+}  // namespace tile
+}  // namespace fni8b
+
+// ------------------------------------------------------------------------------------
+// Internal host entry points (declared in gemm_internal.h, used by capi.cu / moe.cu)
+// ------------------------------------------------------------------------------------
+
+namespace fni8h {
+
+using namespace fni8b;
+
+int tile_status_read_and_clear(int* code) {
+  int v = 0, z = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, tile::g_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "read tile watchdog");
+  e = cudaMemcpyToSymbol(tile::g_status, &z, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "clear tile watchdog");
+  *code = v;
+  return FNI8_OK;
+}
+
+int tile_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
+              const void* residual, void* out, int out_mode, int64_t M, int64_t N, int64_t K, int bn,
+              cudaStream_t st) {
+  if (M <= 0 || N <= 0) return FNI8_OK;
+  if (bn != 128 && bn != 256) return fail(FNI8_ERR_INVALID, "tile BN must be 128 or 256");
+  CUtensorMap ta, tb;
+  if (int s = encode_tmap_2d_i8(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, 128, 128)) return s;
+  if (int s = encode_tmap_2d_i8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, 128, (uint32_t)bn)) return s;
+  tile::Epi epi{a_scale, w_scale, bias, residual, out, out_mode};
+  tile::Groups grp{nullptr, nullptr, nullptr, 0};
+  const int m_tiles = (int)((M + 127) / 128);
+  const int n_tiles = (int)((N + bn - 1) / bn);
+  const int64_t tiles = (int64_t)m_tiles * n_tiles;
+  const int sms = num_sms(current_device());
+  const int grid = (int)(tiles < sms ? tiles : sms);
+  const size_t esz = out_mode == tile::kOutI32 ? 4 : 2;
+  const bool vec_ok = ((N * (int64_t)esz) % 16 == 0) && (((uintptr_t)out & 15u) == 0) &&
+                      (((uintptr_t)w_scale & 15u) == 0) && (bias == nullptr || ((uintptr_t)bias & 15u) == 0) &&
+                      (residual == nullptr || ((uintptr_t)residual & 15u) == 0);
+  if (bn == 256)
+    return tile::launch<256, false>(ta, tb, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
+  return tile::launch<128, false>(ta, tb, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
+}
+
+int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w, const float* w_scale,
+                      int64_t E, int64_t N, int64_t K, const int32_t* seg_expert, const int32_t* seg_off,
+                      const int32_t* seg_cnt, int64_t S, void* out, int out_mode, int bn, cudaStream_t st) {
+  if (R <= 0 || N <= 0 || S <= 0) return FNI8_OK;
+  if (S > tile::kMaxSeg) return fail(FNI8_ERR_UNSUPPORTED, "at most %d segments (got %lld)", tile::kMaxSeg, (long long)S);
+  CUtensorMap ta, tb;
+  if (int s = encode_tmap_2d_i8(&ta, a, (uint64_t)K, (uint64_t)R, (uint64_t)K, 128, 128)) return s;
+  if (int s = encode_tmap_3d_i8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)E, (uint64_t)K, (uint64_t)(N * K), 128,
+                                (uint32_t)bn))
+    return s;
+  tile::Epi epi{a_scale, w_scale, nullptr, nullptr, out, out_mode};
+  tile::Groups grp{seg_expert, seg_off, seg_cnt, (int)S};
+  const int grid = num_sms(current_device());
+  const size_t esz = out_mode == tile::kOutI32 ? 4 : 2;
+  const bool vec_ok = ((N * (int64_t)esz) % 16 == 0) && (((uintptr_t)out & 15u) == 0) &&
+                      (((uintptr_t)w_scale & 15u) == 0) && ((N % 4) == 0);
+  if (bn == 256)
+    return tile::launch<256, true>(ta, tb, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
+  return tile::launch<128, true>(ta, tb, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
+}
+
+}  // namespace fni8h

@@ -1,0 +1,187 @@
+/*
+ * fni8_b200.h -- C ABI of the B200 (sm_100a) W8A8 matmul path for fni8-serve.
+ *
+ * fni8-serve (Python) reaches its kernels through the external `fni8` package:
+ *   fni8.linear(x, qt, bias=)           fni8serve/layers/linear.py:69
+ *   fni8.rmsnorm(x, w, eps, residual=, unit_offset=)   fni8serve/layers/norm.py:51
+ *   fni8.act_and_mul(x, "silu"|"gelu_tanh")            fni8serve/layers/activation.py:24,40
+ *   the per-expert GatedMLP loop of SparseMoE          fni8serve/models/moe.py:97-105
+ * This header is the native boundary underneath a drop-in `fni8` Python package: plain
+ * pointers, element counts and an opaque CUDA stream (`void* stream`, a cudaStream_t;
+ * NULL means the legacy default stream). No torch or C++ types cross it.
+ *
+ * Conventions
+ *  - Every function returns an int status (FNI8_OK == 0). On failure nothing has been
+ *    launched, and fni8_last_error_message() describes the problem (thread-local).
+ *  - All tensors are dense row-major with the innermost dimension contiguous.
+ *  - Activations: dtype FNI8_F16 or FNI8_BF16. Weights: int8 [N, K] (out_features x
+ *    in_features, K contiguous) with one fp32 scale per output row (`per_row_i8`).
+ *  - Per-token activation quantisation: scale[m] = absmax(x[m, :]) / 127 (fp32),
+ *    q = round_half_even(x / scale) clamped to [-127, 127]; an all-zero row gets
+ *    scale 0 and q = 0.
+ *  - Dequant epilogue (fp32, evaluated left to right, no fused multiply-add):
+ *    y = (float(acc) * a_scale[m]) * w_scale[n] (+ bias[n]) (+ residual[m, n]),
+ *    rounded once to the output dtype.
+ *  - K must be a multiple of 16 for the GEMMs (TMA row-stride rule); the quantisers
+ *    accept any K.
+ *  - Calls are asynchronous on `stream`, allocate nothing and never synchronise, so
+ *    they can be captured into a CUDA graph. Calls that share a workspace must not
+ *    overlap on the GPU.
+ */
+#ifndef FNI8_B200_H
+#define FNI8_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FNI8_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FNI8_API __attribute__((visibility("default")))
+#else
+#define FNI8_API
+#endif
+
+enum fni8_status {
+  FNI8_OK = 0,
+  FNI8_ERR_INVALID = 1,       /* bad pointer, shape, dtype or flag */
+  FNI8_ERR_UNSUPPORTED = 2,   /* valid request this build does not implement */
+  FNI8_ERR_ALIGN = 3,         /* pointer / stride alignment the kernels need */
+  FNI8_ERR_CUDA = 4,          /* a CUDA runtime call failed */
+  FNI8_ERR_WORKSPACE = 5,     /* workspace missing or too small */
+  FNI8_ERR_DEVICE_TIMEOUT = 6 /* a bounded device-side wait gave up (fni8_device_status) */
+};
+
+enum fni8_dtype { FNI8_F16 = 0, FNI8_BF16 = 1, FNI8_F32 = 2, FNI8_I32 = 3, FNI8_I8 = 4 };
+enum fni8_act { FNI8_ACT_SILU = 0, FNI8_ACT_GELU_TANH = 1 };
+enum fni8_scoring { FNI8_SCORE_SOFTMAX = 0, FNI8_SCORE_SIGMOID = 1 };
+/* GEMM kernel selection (fni8_gemm_w8a8_ex). AUTO picks by shape. */
+enum fni8_gemm_path { FNI8_PATH_AUTO = 0, FNI8_PATH_TILE = 1, FNI8_PATH_STREAM = 2 };
+
+/* ------------------------------------------------------------------ library */
+FNI8_API int fni8_abi_version(void);
+FNI8_API const char* fni8_status_string(int status);
+FNI8_API const char* fni8_last_error_message(void);
+/* Reads and clears the device-side watchdog words of the current device. *code_out
+ * receives 0 when no bounded wait has timed out since the last call. Synchronises. */
+FNI8_API int fni8_device_status(int* code_out);
+
+/* ------------------------------------------------------------------ quantisers */
+/* Per-token absmax int8 quantisation of x[M, K]: the activation stage inside
+ * fni8.linear (fni8serve/layers/linear.py:2-13,69). */
+FNI8_API int fni8_quantize_rows_i8(const void* x, int dtype, int64_t M, int64_t K, int8_t* q, float* scale,
+                          void* stream);
+
+/* RMSNorm over the last dim: replaces fni8.rmsnorm (fni8serve/layers/norm.py:38-58).
+ * y = dtype((x_f32 * (1/sqrt(mean(x_f32^2) + eps))) * g), g = w or (1 + w) when
+ * unit_offset. With residual != NULL the input is x + residual (rounded to dtype), which
+ * is also written to residual_out. */
+FNI8_API int fni8_rmsnorm(const void* x, const void* residual, const void* weight, int dtype, int64_t M, int64_t K,
+                 float eps, int unit_offset, void* out, void* residual_out, void* stream);
+
+/* Fused RMSNorm -> per-token int8 quantisation (one pass over HBM). Emits the int8 rows
+ * and scales exactly as fni8_quantize_rows_i8 would on the rounded RMSNorm output;
+ * `out` (the rounded normed rows) is optional (NULL skips the store). */
+FNI8_API int fni8_rmsnorm_quant_i8(const void* x, const void* residual, const void* weight, int dtype, int64_t M,
+                          int64_t K, float eps, int unit_offset, void* out, void* residual_out, int8_t* q,
+                          float* scale, void* stream);
+
+/* act(x[:, :I]) * x[:, I:] for x[M, 2I]: replaces fni8.act_and_mul
+ * (fni8serve/layers/activation.py:21-25,37-41): act(gate) in fp32 rounded to dtype, times
+ * up in fp32, rounded to dtype (the reference's F.silu(gate) * up on fp16 tensors). */
+FNI8_API int fni8_act_and_mul(const void* x, int dtype, int act, int64_t M, int64_t I, void* out, void* stream);
+
+/* Fused act_and_mul -> per-token int8 quantisation of the rounded result (the input of
+ * down_proj in GatedMLP.forward, fni8serve/layers/mlp.py:39-40). */
+FNI8_API int fni8_act_and_mul_quant_i8(const void* x, int dtype, int act, int64_t M, int64_t I, int8_t* q, float* scale,
+                              void* stream);
+
+/* ------------------------------------------------------------------ dense GEMM */
+/* Bytes of workspace fni8_gemm_w8a8* may use for an M x N x K problem (0 when none). */
+FNI8_API size_t fni8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
+/* Zero a workspace once before first use; the GEMM kernels leave it zeroed again. */
+FNI8_API int fni8_workspace_init(void* workspace, size_t bytes, void* stream);
+
+/* out[M, N] = dequant(a[M, K] . w[N, K]^T): the int8 GEMM + epilogue inside
+ * fni8.linear (fni8serve/layers/linear.py:67-69). bias [N] and residual [M, N] are
+ * optional and in out_dtype (F16 or BF16). */
+FNI8_API int fni8_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                   const void* bias, const void* residual, void* out, int out_dtype, int64_t M, int64_t N,
+                   int64_t K, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same with an explicit kernel choice (enum fni8_gemm_path). */
+FNI8_API int fni8_gemm_w8a8_ex(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                      const void* bias, const void* residual, void* out, int out_dtype, int64_t M, int64_t N,
+                      int64_t K, int path, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Raw int32 accumulators acc[M, N] = a . w^T (the int8 x int8 -> int32 matmul of the
+ * reference's gemm_w8a8; used for the bit-exact check). */
+FNI8_API int fni8_gemm_w8a8_i32(const int8_t* a, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K, int path,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Whole fni8.linear(x, qt, bias=) (fni8serve/layers/linear.py:67-69) for per_row_i8:
+ * quantise x[M, K] per token into q_scratch[M, K] / s_scratch[M], then the W8A8 GEMM
+ * with dequant epilogue into out[M, N] (dtype of x). `workspace` is the zero-maintained
+ * GEMM workspace (fni8_gemm_workspace_bytes). */
+FNI8_API int fni8_linear_w8a8(const void* x, int dtype, const int8_t* w, const float* w_scale, const void* bias,
+                              void* out, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ MoE */
+/* Router scores -> top-k (SparseMoE.forward routing, fni8serve/models/moe.py:65-95):
+ * softmax over all E (or sigmoid + optional selection bias added for the choice only),
+ * optional group-limited selection (n_groups > 0), top-k (ties -> lower expert id),
+ * optional renormalisation (sum clamped to >= 1e-9), times `scaling`, then rounded to
+ * weight_dtype (FNI8_F16 / FNI8_BF16, as the reference casts to x.dtype; FNI8_F32 keeps
+ * fp32). E <= 1024, top_k <= 32. */
+FNI8_API int fni8_moe_route(const float* logits, int64_t T, int64_t E, int64_t top_k, int scoring, const float* sel_bias,
+                   int64_t n_groups, int64_t topk_group, int norm_topk, float scaling, int weight_dtype,
+                   int32_t* topi, float* topw, void* stream);
+
+/* Stable grouping of the T*k (token, slot) pairs by expert: counts[E], offsets[E+1]
+ * (exclusive scan), row_of_slot[T*k] (slot = t*k + j -> grouped row; -1 for an expert id
+ * outside [0, E), which is dropped) and slot_of_row[offsets[E]]. Rows of one expert keep
+ * slot order, so the grouping is deterministic. Uses fni8_moe_plan_workspace_bytes(T*k, E)
+ * bytes of workspace (no zeroing needed). E <= 1024. */
+FNI8_API size_t fni8_moe_plan_workspace_bytes(int64_t n_slots, int64_t E);
+FNI8_API int fni8_moe_plan(const int32_t* topi, int64_t n_slots, int64_t E, int32_t* counts, int32_t* offsets,
+                  int32_t* row_of_slot, int32_t* slot_of_row, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* q_out[r] = q[slot_of_row[r] / top_k], scale_out likewise (int8 row gather). */
+FNI8_API int fni8_moe_gather_rows_i8(const int8_t* q, const float* scale, const int32_t* slot_of_row, int64_t R, int64_t K,
+                            int64_t top_k, int8_t* q_out, float* scale_out, void* stream);
+
+/* Grouped W8A8 GEMM over S row segments of a[R, K]: segment s covers rows
+ * [seg_off[s], seg_off[s] + seg_cnt[s]) and multiplies them by expert seg_expert[s] of
+ * w[E, N, K] (scales w_scale[E, N]); out[R, N] in out_dtype. The per-expert GEMMs of
+ * the SparseMoE loop (fni8serve/models/moe.py:99-105) in one persistent launch.
+ * The segment arrays live in device memory (S <= 512). */
+FNI8_API int fni8_grouped_gemm_w8a8(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w, const float* w_scale,
+                           int64_t E, int64_t N, int64_t K, const int32_t* seg_expert, const int32_t* seg_off,
+                           const int32_t* seg_cnt, int64_t S, void* out, int out_dtype, void* stream);
+
+/* out[t] = sum_j topw[t, j] * y[row_of_slot[t*k + j]] in fp32, rounded once: the
+ * weighted index_add_ combine (fni8serve/models/moe.py:97,105). */
+FNI8_API int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,
+                     int64_t top_k, int64_t H, void* out, void* stream);
+
+/* Routed-expert block of SparseMoE on one GPU (fni8serve/models/moe.py:97-105) given
+ * the routing: quantise x, group, gate_up grouped GEMM, act_and_mul + quant, down
+ * grouped GEMM, weighted combine. w_gu [E, 2I, H], w_dn [E, H, I] int8 with per-row
+ * fp32 scales s_gu [E, 2I], s_dn [E, H]. */
+FNI8_API size_t fni8_moe_experts_workspace_bytes(int64_t T, int64_t H, int64_t top_k, int64_t E, int64_t I);
+FNI8_API int fni8_moe_experts_w8a8(const void* x, int dtype, int64_t T, int64_t H, const int32_t* topi, const float* topw,
+                          int64_t top_k, const int8_t* w_gu, const float* s_gu, const int8_t* w_dn,
+                          const float* s_dn, int64_t E, int64_t I, int act, void* out, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FNI8_B200_H */

@@ -1,0 +1,227 @@
+"""Generate the golden fixtures in tests/golden/*.npz from the REFERENCE's own code.
+
+Runs only where the fni8-serve sources are available (pass --reference, default
+$FNI8_REFERENCE or /root/reference); the GPU box never runs it, it only reads the
+committed .npz files. fni8-serve cannot be imported normally here because its kernels
+package `fni8` is not installed, so this script:
+
+  * puts this repository's drop-in `fni8` package on sys.path (only QTensor and
+    quant.core.quantize_int8_rowwise are exercised: the reference's CPU paths never
+    call an fni8 kernel), and
+  * registers empty package objects for `fni8serve`, `fni8serve.layers` and
+    `fni8serve.models` so the individual modules below load without executing the
+    package __init__ files (which pull in the engine, loader and attention kernels).
+
+Every output below is computed by fni8-serve's own modules on CPU:
+    layers/norm.py RMSNorm (CPU path)          -> rmsnorm.npz
+    layers/activation.py SiluAndMul/GeluAndMul -> act.npz
+    layers/linear.py LinearW8A8 (fp16 fallback) -> linear.npz
+    models/weights.py to_qtensor/merge_qtensor -> weights.npz
+    models/moe.py SparseMoE (softmax and sigmoid+group-limited routing) -> moe_*.npz
+    tests/test_layers.py::_i8 and tests/test_smoke.py::_i8 (the reference tests' own
+        weight-quant fixtures)                  -> i8_fixture.npz
+Inputs are seeded; every fixture stores its inputs too, so the tests need nothing else.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import importlib.util
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+
+
+def _setup(ref: str):
+    sys.path.insert(0, os.path.join(REPO, "fni8-serve_b200"))
+    import fni8  # this repository's drop-in package
+
+    for name in ("fni8serve", "fni8serve.layers", "fni8serve.models"):
+        mod = types.ModuleType(name)
+        mod.__path__ = [os.path.join(ref, *name.split("."))]
+        sys.modules[name] = mod
+    L = types.SimpleNamespace()
+    L.fni8 = fni8
+    L.linear = importlib.import_module("fni8serve.layers.linear")
+    L.norm = importlib.import_module("fni8serve.layers.norm")
+    L.act = importlib.import_module("fni8serve.layers.activation")
+    L.mlp = importlib.import_module("fni8serve.layers.mlp")
+    L.weights = importlib.import_module("fni8serve.models.weights")
+    L.moe = importlib.import_module("fni8serve.models.moe")
+    return L
+
+
+def _load_test_module(ref: str, fname: str, L):
+    """Import one of the reference's test files to call its fixture helpers."""
+    layers_pkg = sys.modules["fni8serve.layers"]
+    for n in ("GatedMLP", "GeluAndMul", "RMSNorm", "SiluAndMul", "get_act_and_mul"):
+        setattr(layers_pkg, n, getattr(L.mlp, n, None) or getattr(L.act, n, None) or getattr(L.norm, n, None))
+    for n in ("LMHead", "RotaryEmbedding", "Sampler", "VocabEmbedding", "LinearW8A8"):
+        if not hasattr(layers_pkg, n):
+            setattr(layers_pkg, n, getattr(L.linear, n, None))
+    top = sys.modules["fni8serve"]
+    top.ServeConfig = None
+    top.load_fni8_checkpoint = None
+    if not hasattr(L.fni8, "save_fni8"):
+        L.fni8.save_fni8 = None  # only referenced at import time by test_smoke.py
+    spec = importlib.util.spec_from_file_location(f"_ref_{fname[:-3]}", os.path.join(ref, "tests", fname))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _np(t: torch.Tensor) -> np.ndarray:
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).numpy()
+    return t.detach().numpy()
+
+
+def gen_rmsnorm(L) -> dict:
+    g = torch.Generator().manual_seed(101)
+    out = {}
+    for tag, shape, dt in (("a", (4, 8, 512), torch.float16), ("b", (3, 1024), torch.float16),
+                           ("c", (5, 4096), torch.float16)):
+        K = shape[-1]
+        x = torch.randn(shape, generator=g).to(dt)
+        r = torch.randn(shape, generator=g).to(dt)
+        w = (1.0 + 0.1 * torch.randn(K, generator=g)).to(torch.float16)
+        eps = 1e-6
+        n = L.norm.RMSNorm(K, eps=eps, weight=w.clone())
+        y = n(x)
+        y_r, new_r = n(x, r)
+        nu = L.norm.RMSNorm(K, eps=eps, weight=(0.1 * torch.randn(K, generator=g)).to(torch.float16),
+                            add_unit_offset=True)
+        y_u = nu(x)
+        out.update({f"{tag}_x": _np(x), f"{tag}_r": _np(r), f"{tag}_w": _np(w), f"{tag}_wu": _np(nu.weight.data),
+                    f"{tag}_y": _np(y), f"{tag}_y_res": _np(y_r), f"{tag}_new_res": _np(new_r),
+                    f"{tag}_y_unit": _np(y_u)})
+    return out
+
+
+def gen_act(L) -> dict:
+    g = torch.Generator().manual_seed(202)
+    x = (2 * torch.randn(6, 2 * 768, generator=g)).to(torch.float16)
+    return {"x": _np(x), "silu": _np(L.act.SiluAndMul()(x)), "gelu_tanh": _np(L.act.GeluAndMul("tanh")(x))}
+
+
+def gen_linear(L) -> dict:
+    """LinearW8A8 on CPU = the reference's fp16 dequant fallback (linear.py:70-71)."""
+    g = torch.Generator().manual_seed(303)
+    out = {}
+    # the shape of tests/test_smoke.py:67-80 (N=256, K=512, M=16) and a BASELINE config-0
+    # slice (K=1024, 0.1% outlier channels x20)
+    for tag, (M, K, N, outl) in (("smoke", (16, 512, 256, False)), ("cfg0", (64, 1024, 256, True))):
+        w = (0.02 * torch.randn(N, K, generator=g)).to(torch.float16)
+        qt = L.weights.to_qtensor(w)
+        x = torch.randn(M, K, generator=g)
+        if outl:
+            ch = torch.randperm(K, generator=g)[: max(1, K // 1000)]
+            x[:, ch] *= 20
+        x = x.to(torch.float16)
+        bias = (0.1 * torch.randn(N, generator=g)).to(torch.float16)
+        y = L.linear.LinearW8A8(qt)(x)
+        yb = L.linear.LinearW8A8(qt, bias)(x)
+        out.update({f"{tag}_x": _np(x), f"{tag}_wq": _np(qt.data), f"{tag}_ws": _np(qt.scale),
+                    f"{tag}_bias": _np(bias), f"{tag}_y": _np(y), f"{tag}_y_bias": _np(yb)})
+    return out
+
+
+def gen_weights(L) -> dict:
+    g = torch.Generator().manual_seed(404)
+    sd = {f"p.{n}_proj.weight": (0.05 * torch.randn(*s, generator=g)).to(torch.float16)
+          for n, s in (("q", (64, 96)), ("k", (32, 96)), ("v", (32, 96)), ("gate", (80, 96)), ("up", (80, 96)))}
+    qkv = L.weights.qkv_weight(sd, "p")
+    gu = L.weights.gate_up_weight(sd, "p")
+    pre = L.weights.merge_qtensor([L.weights.to_qtensor(sd["p.gate_proj.weight"]),
+                                   L.weights.to_qtensor(sd["p.up_proj.weight"])])
+    out = {k.replace(".", "_"): _np(v) for k, v in sd.items()}
+    out.update({"qkv_q": _np(qkv.data), "qkv_s": _np(qkv.scale), "gu_q": _np(gu.data), "gu_s": _np(gu.scale),
+                "gu_pre_q": _np(pre.data), "gu_pre_s": _np(pre.scale)})
+    return out
+
+
+def gen_i8_fixture(ref: str, L) -> dict:
+    """The reference tests' own weight-quant helpers, called directly."""
+    tl = _load_test_module(ref, "test_layers.py", L)
+    ts = _load_test_module(ref, "test_smoke.py", L)
+    torch.manual_seed(505)
+    w_l = torch.randn(128, 256, dtype=torch.float16)
+    torch.manual_seed(505)
+    qt_l, deq_l = tl._i8(128, 256)
+    torch.manual_seed(506)
+    w_s = torch.randn(128, 256)
+    torch.manual_seed(506)
+    qt_s = ts._i8(128, 256)
+    return {"layers_w": _np(w_l), "layers_q": _np(qt_l.data), "layers_s": _np(qt_l.scale), "layers_deq": _np(deq_l),
+            "smoke_w": _np(w_s), "smoke_q": _np(qt_s.data), "smoke_s": _np(qt_s.scale)}
+
+
+def gen_moe(L, scoring: str) -> dict:
+    g = torch.Generator().manual_seed(606 if scoring == "softmax" else 607)
+    E, k, H, I = 8, 2, 256, 128
+    B, S = 2, 16
+    sd = {}
+    for e in range(E):
+        sd[f"e{e}.gate_proj.weight"] = (0.05 * torch.randn(I, H, generator=g)).to(torch.float16)
+        sd[f"e{e}.up_proj.weight"] = (0.05 * torch.randn(I, H, generator=g)).to(torch.float16)
+        sd[f"e{e}.down_proj.weight"] = (0.05 * torch.randn(H, I, generator=g)).to(torch.float16)
+    experts = [(L.weights.gate_up_weight(sd, f"e{e}"), L.weights.to_qtensor(sd[f"e{e}.down_proj.weight"]))
+               for e in range(E)]
+    gate = (0.05 * torch.randn(E, H, generator=g)).to(torch.float16)
+    kw = {}
+    bias = None
+    if scoring == "sigmoid":
+        bias = 0.1 * torch.randn(E, generator=g)
+        kw = dict(scoring_func="sigmoid", e_score_correction_bias=bias, num_expert_groups=2, topk_group=1)
+    moe = L.moe.SparseMoE(gate=gate, experts=experts, top_k=k, norm_topk_prob=True, **kw)
+    x = torch.randn(B, S, H, generator=g).to(torch.float16)
+    captured = {}
+    real_topk = torch.topk
+
+    def spy(inp, kk, *a, **kws):  # record the routing choice made inside moe.py
+        r = real_topk(inp, kk, *a, **kws)
+        if kk == k and inp.shape[-1] == E:
+            captured["topi"] = r[1].clone()
+        return r
+
+    torch.topk = spy
+    try:
+        y = moe(x)
+    finally:
+        torch.topk = real_topk
+    out = {"x": _np(x), "gate": _np(gate), "y": _np(y), "topi": _np(captured["topi"]),
+           "w_gu": np.stack([_np(gu.data) for gu, _ in experts]), "s_gu": np.stack([_np(gu.scale) for gu, _ in experts]),
+           "w_dn": np.stack([_np(dn.data) for _, dn in experts]), "s_dn": np.stack([_np(dn.scale) for _, dn in experts]),
+           "E": np.array(E), "k": np.array(k)}
+    if bias is not None:
+        out["bias"] = _np(bias)
+    return out
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--reference", default=os.environ.get("FNI8_REFERENCE", "/root/reference"))
+    a = ap.parse_args()
+    if not os.path.isdir(os.path.join(a.reference, "fni8serve")):
+        print(f"fni8-serve sources not found under {a.reference}", file=sys.stderr)
+        return 2
+    torch.set_num_threads(4)
+    L = _setup(a.reference)
+    jobs = {"rmsnorm": lambda: gen_rmsnorm(L), "act": lambda: gen_act(L), "linear": lambda: gen_linear(L),
+            "weights": lambda: gen_weights(L), "i8_fixture": lambda: gen_i8_fixture(a.reference, L),
+            "moe_softmax": lambda: gen_moe(L, "softmax"), "moe_sigmoid": lambda: gen_moe(L, "sigmoid")}
+    for name, fn in jobs.items():
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **fn())
+        print(f"wrote {path} ({os.path.getsize(path)} bytes)")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,163 @@
+"""fni8-serve's layer contracts on the sm_100a path: the fused RMSNorm -> int8 hand-off,
+CUDA-graph capture of the decode-path ops, and the grouped MoE pipeline against the
+oracle and against the reference SparseMoE's own outputs (tests/golden/moe_*.npz)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import w8a8_oracle as O
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a B200")]
+
+DEV = "cuda"
+
+
+def gen(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+def qweight(N, K, seed):
+    return O.quantize_weight_rowwise(0.02 * torch.randn(N, K, generator=gen(seed)))
+
+
+def test_norm_to_linear_sidecar_is_invisible():
+    """fni8.rmsnorm leaves int8 rows on its output; fni8.linear consumes them instead of
+    re-quantising. Results must equal the unfused chain exactly, and the side-car must be
+    ignored once the tensor is modified in place."""
+    import fni8
+
+    M, K, N = 64, 4096, 1024
+    g = gen(1)
+    x = torch.randn(M, K, generator=g).half().to(DEV)
+    r = torch.randn(M, K, generator=g).half().to(DEV)
+    w = (1 + 0.1 * torch.randn(K, generator=g)).half().to(DEV)
+    wq, ws = qweight(N, K, 2)
+    qt = fni8.QTensor(wq.to(DEV), ws.to(DEV))
+    h, _ = fni8.rmsnorm(x, w, 1e-6, residual=r)
+    assert getattr(h, "_fni8_q", None) is not None
+    fused = fni8.linear(h, qt)
+    plain = fni8.linear(h.clone(), qt)  # clone drops the side-car
+    assert torch.equal(fused, plain)
+    h.mul_(2)  # bumps the version counter: side-car must not be used
+    assert torch.equal(fni8.linear(h, qt), fni8.linear(h.clone(), qt))
+
+
+def test_decode_ops_capture_in_cuda_graph():
+    """The reference engine captures decode in a CUDA graph (engine/cuda_graph.py); the
+    ops must be capturable (no host sync, no allocation outside the caching allocator)."""
+    import fni8
+
+    K, N = 4096, 6144
+    wq, ws = qweight(N, K, 3)
+    qt = fni8.QTensor(wq.to(DEV), ws.to(DEV))
+    w = torch.ones(K, dtype=torch.float16, device=DEV)
+    static_x = torch.randn(8, K, generator=gen(4)).half().to(DEV)
+    fni8.linear(fni8.rmsnorm(static_x, w, 1e-6), qt)  # warm-up: workspace allocated outside capture
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static_y = fni8.linear(fni8.act_and_mul(torch.cat([static_x, static_x], -1)), qt)
+    for seed in (5, 6):
+        static_x.copy_(torch.randn(8, K, generator=gen(seed)).half())
+        graph.replay()
+        torch.cuda.synchronize()
+        ref = fni8.linear(fni8.act_and_mul(torch.cat([static_x, static_x], -1)), qt)
+        assert torch.equal(static_y, ref)
+
+
+# ------------------------------------------------------------------ MoE
+def _experts(E, H, I, seed):
+    g = gen(seed)
+    w_gu = torch.stack([qweight(2 * I, H, 100 * seed + e)[0] for e in range(E)])
+    s_gu = torch.stack([qweight(2 * I, H, 100 * seed + e)[1] for e in range(E)])
+    w_dn = torch.stack([qweight(H, I, 100 * seed + 50 + e)[0] for e in range(E)])
+    s_dn = torch.stack([qweight(H, I, 100 * seed + 50 + e)[1] for e in range(E)])
+    del g
+    return w_gu, s_gu, w_dn, s_dn
+
+
+@pytest.mark.parametrize("scoring", ["softmax", "sigmoid"])
+def test_route_matches_oracle(scoring):
+    import fni8.moe as M
+
+    T, E, k = 300, 128, 8
+    logits = torch.randn(T, E, generator=gen(7))
+    kw, okw = {}, {}
+    if scoring == "sigmoid":
+        b = 0.1 * torch.randn(E, generator=gen(8))
+        kw = dict(sel_bias=b.to(DEV), num_expert_groups=8, topk_group=4)
+        okw = dict(sel_bias=b, n_groups=8, topk_group=4)
+    topi, topw = M.route(logits.to(DEV), k, scoring=scoring, **kw)
+    ti, tw = O.moe_route(logits, k, scoring=scoring, **okw)
+    assert torch.equal(topi.cpu().long(), ti)
+    torch.testing.assert_close(topw.cpu(), tw.float(), rtol=2e-3, atol=1e-6)
+
+
+def test_plan_matches_oracle():
+    import fni8.moe as M
+
+    T, k, E = 4096, 8, 128
+    topi = torch.randint(0, E, (T, k), generator=gen(9), dtype=torch.int32)
+    topi[3, 2] = E + 4  # out-of-range id: dropped
+    counts, offsets, ros, sor = M.plan(topi.to(DEV), E)
+    c, o, r, s = O.moe_plan(topi, E)
+    assert torch.equal(counts.cpu().long(), c) and torch.equal(offsets.cpu().long(), o)
+    assert torch.equal(ros.cpu().long(), r) and torch.equal(sor.cpu()[: int(o[-1])].long(), s)
+
+
+def test_grouped_gemm_int32_exact():
+    import fni8.moe as M
+
+    E, N, K = 12, 768, 512
+    cnt = torch.tensor([0, 1, 130, 127, 128, 5, 0, 300, 17, 256, 3, 64], dtype=torch.int32)
+    off = torch.zeros(E, dtype=torch.int32)
+    off[1:] = torch.cumsum(cnt, 0)[:-1]
+    R = int(cnt.sum())
+    a = torch.randint(-127, 128, (R, K), generator=gen(10), dtype=torch.int8)
+    w = torch.randint(-127, 128, (E, N, K), generator=gen(11), dtype=torch.int8)
+    perm = torch.randperm(E, generator=gen(12)).int()  # segment s uses expert perm[s]
+    got = M.grouped_gemm(a.to(DEV), torch.ones(R, device=DEV), w.to(DEV), torch.ones(E, N, device=DEV),
+                         perm.to(DEV), off.to(DEV), cnt.to(DEV), out_dtype=torch.int32).cpu()
+    for s in range(E):
+        o, c = int(off[s]), int(cnt[s])
+        if c:
+            assert torch.equal(got[o:o + c], O.int_mm_fast(a[o:o + c], w[int(perm[s])])), s
+
+
+@pytest.mark.parametrize("T,E,k,H,I", [(64, 8, 2, 256, 128), (1024, 128, 8, 2048, 768), (3, 16, 4, 512, 256)])
+def test_moe_experts_vs_oracle(T, E, k, H, I):
+    import fni8.moe as M
+
+    x = torch.randn(T, H, generator=gen(T)).half()
+    w_gu, s_gu, w_dn, s_dn = _experts(E, H, I, 1)
+    logits = torch.randn(T, E, generator=gen(T + 1))
+    topi, topw = O.moe_route(logits, k)
+    stack = M.ExpertStack(w_gu.to(DEV), s_gu.to(DEV), w_dn.to(DEV), s_dn.to(DEV))
+    got = M.experts(x.to(DEV), topi.int().to(DEV), topw.float().to(DEV), stack).cpu()
+    ref = O.moe_experts_w8a8(x, topi, topw.float(), w_gu, s_gu, w_dn, s_dn, exact=False)
+    cos = F.cosine_similarity(got.flatten().float(), ref.flatten().float(), dim=0).item()
+    assert cos > 0.9999, cos
+    # identical except where the SiLU's expf flipped one fp16 rounding upstream
+    assert (got == ref).float().mean() > 0.98
+
+
+@pytest.mark.parametrize("scoring", ["softmax", "sigmoid"])
+def test_sparse_moe_dropin_matches_reference_golden(golden, scoring):
+    import fni8
+    import fni8.moe as M
+
+    g = golden(f"moe_{scoring}")
+    E, k = int(g["E"]), int(g["k"])
+    experts = [(fni8.QTensor(torch.from_numpy(g["w_gu"][e]), torch.from_numpy(g["s_gu"][e])),
+                fni8.QTensor(torch.from_numpy(g["w_dn"][e]), torch.from_numpy(g["s_dn"][e]))) for e in range(E)]
+    kw = {}
+    if scoring == "sigmoid":
+        kw = dict(scoring_func="sigmoid", e_score_correction_bias=torch.from_numpy(g["bias"]), num_expert_groups=2,
+                  topk_group=1)
+    moe = M.SparseMoE(gate=torch.from_numpy(g["gate"]), experts=experts, top_k=k, **kw).to(DEV)
+    x = torch.from_numpy(g["x"]).to(DEV)
+    y = moe(x).cpu()
+    ref = torch.from_numpy(g["y"])
+    cos = F.cosine_similarity(y.flatten().float(), ref.flatten().float(), dim=0).item()
+    assert y.shape == ref.shape and cos >= 0.99, cos

@@ -1,0 +1,508 @@
+"""Benchmark of the B200 W8A8 path on BASELINE.json's configurations.
+
+    python bench.py [--config 1] [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line (rank 0). The default workload is BASELINE config 1, the Qwen3-8B
+decode-step linear set: for each decode batch M in {1, 8, 32, 128, 256} the four
+fni8.linear calls QKV (4096->6144), O (4096->4096), gate_up (4096->24576) and
+down (12288->4096), each = per-token int8 quantisation + int8 GEMM + dequant epilogue.
+A step is that whole set (20 linears). Metric: algorithmic HBM bytes per second
+(weights + scales + activations in + outputs out). Every linear has its own weights
+(965 MB per step), so every weight read comes from HBM, not the 126 MB L2.
+
+Other configs (parity-test workloads, also benchable): 0 single linear, 2 prefill
+(fused RMSNorm+quant -> 4 GEMMs at M=8192, TOPS), 3 MoE expert layer (tokens/s,
+expert-parallel under torchrun), 4 column-parallel K=8192 N=28672 sweep.
+
+--impl reference times the reference's own CPU path for the same workload on the
+host cores: the oracle port (torch._int_mm + fp32 dequant, oracle/w8a8_oracle.py),
+because the reference's kernels package (fni8) is not available here.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "fni8-serve_b200"))
+sys.path.insert(0, ROOT)
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+INT8_DENSE_NOMINAL_TOPS = 4500.0  # B200 dense int8 tensor-core peak (vendor figure)
+
+QWEN3_8B = [("qkv", 4096, 6144), ("o", 4096, 4096), ("gate_up", 4096, 24576), ("down", 12288, 4096)]
+DECODE_M = [1, 8, 32, 128, 256]
+
+
+# ------------------------------------------------------------------ environment helpers
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return dict(FALLBACK_PEAKS, source="fallback")
+
+
+def committed_traffic(key):
+    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get(key)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.uuid = str(torch.cuda.get_device_properties(device).uuid)
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self):
+        self.f.flush()
+        rows = []
+        for ln in open(self.f.name):
+            c = [x.strip() for x in ln.split(",")]
+            if len(c) < 10:
+                continue
+            u = c[1][4:] if c[1].startswith("GPU-") else c[1]
+            if self.uuid.replace("GPU-", "") not in u and u not in self.uuid:
+                continue
+            rows.append(c)
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower().startswith("active")})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": float(rows[0][3]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world, local):
+    if world > 1 and not torch.distributed.is_initialized():
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def flush_l2(buf):
+    buf.add_(1)  # 256 MB written: evicts the 126 MB L2 between timed iterations
+
+
+# ------------------------------------------------------------------ workloads
+def make_weight(N, K, seed, device):
+    """int8 per-row weights + fp32 scales generated on the device (N(0, 0.02) quantised)."""
+    import fni8
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    w = torch.randn(N, K, generator=g, device=device, dtype=torch.float32) * 0.02
+    q, s = fni8.quant.core.quantize_int8_rowwise(w)
+    return fni8.QTensor(q.contiguous(), s.squeeze(-1).contiguous(), scheme="per_row_i8")
+
+
+def act(M, K, seed, device, outliers=True):
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(M, K, generator=g, device=device)
+    if outliers:
+        ch = torch.randperm(K, generator=g, device=device)[: max(1, K // 1000)]
+        x[:, ch] *= 20
+    return x.half()
+
+
+def decode_bytes(M, K, N):
+    # weights + per-row scales + fp16 activations in + fp16 outputs out
+    return N * K + 4 * N + 2 * M * K + 2 * M * N
+
+
+class DecodeSet:
+    """20 fni8.linear calls, distinct weights each."""
+
+    def __init__(self, device, ms=DECODE_M):
+        self.items = []
+        seed = 0
+        for M in ms:
+            for name, K, N in QWEN3_8B:
+                seed += 1
+                self.items.append((M, name, K, N, make_weight(N, K, seed, device), act(M, K, 1000 + seed, device)))
+        self.bytes = sum(decode_bytes(M, K, N) for M, _, K, N, _, _ in self.items)
+
+    def step(self):
+        import fni8
+
+        return [fni8.linear(x, qt) for (_, _, _, _, qt, x) in self.items]
+
+
+def time_graph(fn, steps, warmup, world, flush=None):
+    """Capture fn() in a CUDA graph; time `steps` replays with CUDA events (max over ranks)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()  # eager warm-up (allocates the GEMM workspace outside capture)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    times = []
+    for _ in range(steps):
+        if flush is not None:
+            flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        times.append((a, b))
+    torch.cuda.synchronize()
+    barrier(world)
+    total_ms = sum(a.elapsed_time(b) for a, b in times)
+    del graph
+    return max_over_ranks(total_ms, world)
+
+
+def per_launch_ms(fn, reps=20):
+    """Average device time of one fn() launch sequence, events on the launching stream."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ev = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        ev.append((a, b))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in ev) / reps
+
+
+# ------------------------------------------------------------------ configs (our arm)
+def run_config1(args, world, rank, dev):
+    import fni8
+    from fni8 import _native as nat
+    from fni8.ops import WORKSPACE
+
+    ds = DecodeSet(dev)
+    WORKSPACE.get(dev)
+    pk = peaks()
+    with ClockSampler(dev) as clk:
+        ms_total = time_graph(ds.step, args.steps, args.warmup, world)
+    clocks = clk.summary()
+    ms_step = ms_total / args.steps
+    value = world * ds.bytes / (ms_step * 1e-3) / 1e9
+
+    # dominant kernel: the weight-streaming W8A8 GEMM. The 20 GEMM launches alone (on
+    # int8 activations prepared beforehand) are captured in one graph per decode batch M
+    # and timed with CUDA events around the replays.
+    gemm_ms, gemm_bytes, per = 0.0, 0, {}
+    for M in DECODE_M:
+        rows = [it for it in ds.items if it[0] == M]
+        qs = [fni8.quantize_rows(x) for (*_, x) in rows]
+
+        def gemms(rows=rows, qs=qs):
+            for (_, _, _, _, qt, _), (q, s) in zip(rows, qs):
+                fni8.linear_q(q, s, qt)
+
+        t = time_graph(gemms, args.steps, args.warmup, world) / args.steps
+        b = sum(N * K + 4 * N + M * K + 4 * M + 2 * M * N for (_, _, K, N, _, _) in rows)
+        gemm_ms += t
+        gemm_bytes += b
+        per[f"M{M}"] = round(b / (t * 1e-3) / 1e9, 1)
+    achieved = gemm_bytes / (gemm_ms * 1e-3) / 1e9
+
+    # end to end through the public API with host buffers: H2D of each linear's input
+    # from pinned memory, fni8.linear, D2H of its output, every step
+    hx = [x.cpu().pin_memory() for (*_, x) in ds.items]
+    hy = [torch.empty(M, N, dtype=torch.float16).pin_memory() for (M, _, _, N, _, _) in ds.items]
+    h2d = sum(t.numel() * 2 for t in hx)
+    d2h = sum(t.numel() * 2 for t in hy)
+
+    def e2e_step():
+        for (M, _, K, N, qt, _), xh, yh in zip(ds.items, hx, hy):
+            xd = xh.to(dev, non_blocking=True)
+            yh.copy_(fni8.linear(xd, qt), non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        e2e_step()
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(a.elapsed_time(b), world) / args.steps
+    e2e = world * ds.bytes / (e2e_ms * 1e-3) / 1e9
+
+    line = {
+        "metric": "W8A8 decode GB/s (Qwen3-8B QKV/O/gate_up/down at M=1,8,32,128,256; % of HBM)",
+        "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "BASELINE config 1: Qwen3-8B decode-step linear set", "M": DECODE_M,
+                   "gemms": [f"{n}:K{k}xN{nn}" for n, k, nn in QWEN3_8B], "bytes_per_step": ds.bytes,
+                   "l2": "inputs larger than L2 (distinct weights per linear, 965 MB per step)",
+                   "parallelism": f"replicas{world}", "timing": "CUDA graph replay, CUDA events"},
+        "frac_of_hbm": round(value / world / pk["hbm_gbs"], 3),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 3), "traffic": committed_traffic("decode_gemm"),
+                     "kernel": "w8a8_stream_kernel (the 20 decode GEMMs, graph-replayed, per-M graphs)",
+                     "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs)",
+                     "gemm_gbs_per_M": per, "gemm_us_per_step": round(gemm_ms * 1e3, 2)},
+        "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms, 4), "api": "fni8.linear (eager, pinned host buffers)"},
+        "gpu_launches": 40 * args.steps,
+        "clocks": clocks,
+    }
+    return line, ds
+
+
+def run_config2(args, world, rank, dev):
+    """Prefill: fused RMSNorm+quant -> QKV, O, gate_up -> fused SiLU*up+quant -> down, M=8192."""
+    import fni8
+
+    M = 8192
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(M, 4096, generator=g, device=dev).half()
+    gamma = (1 + 0.1 * torch.randn(4096, generator=g, device=dev)).half()
+    W = {name: make_weight(N, K, 100 + i, dev) for i, (name, K, N) in enumerate(QWEN3_8B)}
+    ops = sum(2 * M * K * N for _, K, N in QWEN3_8B)
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        q, s = fni8.rmsnorm_quant(x, gamma, 1e-6)
+        fni8.linear_q(q, s, W["qkv"])
+        fni8.linear_q(q, s, W["o"])
+        h = fni8.linear_q(q, s, W["gate_up"])
+        hq, hs = fni8.act_and_mul_quant(h)
+        return fni8.linear_q(hq, hs, W["down"])
+
+    pk = peaks()
+    with ClockSampler(dev) as clk:
+        ms_total = time_graph(step, args.steps, args.warmup, world, flush=lambda: flush_l2(flush_buf))
+    clocks = clk.summary()
+    ms_step = ms_total / args.steps
+    value = world * ops / (ms_step * 1e-3) / 1e12
+    q, s = fni8.rmsnorm_quant(x, gamma, 1e-6)
+    t_gu = per_launch_ms(lambda: fni8.linear_q(q, s, W["gate_up"]), reps=10)
+    ach = 2 * M * 4096 * 24576 / (t_gu * 1e-3) / 1e12
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(M, 4096, dtype=torch.float16).pin_memory()
+
+    def e2e_step():
+        xd = xh.to(dev, non_blocking=True)
+        q, s = fni8.rmsnorm_quant(xd, gamma, 1e-6)
+        fni8.linear_q(q, s, W["qkv"])
+        fni8.linear_q(q, s, W["o"])
+        hq, hs = fni8.act_and_mul_quant(fni8.linear_q(q, s, W["gate_up"]))
+        yh.copy_(fni8.linear_q(hq, hs, W["down"]), non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        e2e_step()
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(a.elapsed_time(b), world) / args.steps
+    line = {
+        "metric": "W8A8 prefill TOPS (Qwen3-8B 4 GEMMs at M=8192, fused RMSNorm+quant; % int8 TC peak)",
+        "value": round(value, 1), "unit": "TOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "BASELINE config 2: Qwen3-8B prefill M=8192", "ops_per_step": ops,
+                   "l2": "flushed between steps (256 MB write)", "parallelism": f"replicas{world}"},
+        "frac_of_int8_nominal": round(value / world / INT8_DENSE_NOMINAL_TOPS, 3),
+        "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": INT8_DENSE_NOMINAL_TOPS,
+                     "unit": "TOP/s", "frac": round(ach / INT8_DENSE_NOMINAL_TOPS, 3),
+                     "traffic": committed_traffic("prefill_gate_up"), "kernel": "w8a8_tile_kernel (gate_up)",
+                     "peak_source": "nominal dense int8 (no measured int8 peak); 2x measured bf16 = "
+                                    f"{2 * pk['bf16_tflops']:.0f}"},
+        "e2e": {"value": round(world * ops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TOP/s",
+                "h2d_bytes_per_step": xh.numel() * 2, "d2h_bytes_per_step": yh.numel() * 2},
+        "gpu_launches": 6 * args.steps,
+        "clocks": clocks,
+    }
+    return line, None
+
+
+# ------------------------------------------------------------------ reference arm (CPU)
+def reference_arm(args, world, rank):
+    """The reference's CPU int8 path on the host cores (oracle port), same config."""
+    if rank != 0:
+        return None
+    from oracle import w8a8_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    if args.config == 1:
+        items = []
+        for M in DECODE_M:
+            for name, K, N in QWEN3_8B:
+                q, s = O.quantize_weight_rowwise(0.02 * torch.randn(N, K, generator=g))
+                items.append((M, K, N, q, s, torch.randn(M, K, generator=g).half()))
+        nbytes = sum(decode_bytes(M, K, N) for M, K, N, *_ in items)
+
+        def step():
+            for M, K, N, q, s, x in items:
+                O.linear_w8a8(x, q, s, exact=False)
+
+        unit, metric = "GB/s", "W8A8 decode GB/s (Qwen3-8B QKV/O/gate_up/down at M=1,8,32,128,256; % of HBM)"
+        work = nbytes
+        scale = 1e9
+    else:
+        raise SystemExit(f"--impl reference: config {args.config} not wired yet")
+    for _ in range(max(1, min(args.warmup, 1))):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    v = work / dt / scale
+    return {"metric": metric, "value": round(v, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
+            "config": {"workload": f"BASELINE config {args.config}", "parallelism": "host cores"},
+            "cpu_baseline": {"value": round(v, 3), "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"{args.steps} full steps of config {args.config} on the host "
+                                       "(torch._int_mm int8->int32 + fp32 dequant, oracle/w8a8_oracle.py)"},
+            "e2e": {"value": round(v, 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def cpu_baseline_sample(config, seconds=10.0):
+    """Bounded CPU sample of the same workload for the cpu_baseline key of our line."""
+    from oracle import w8a8_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    if config == 1:
+        items = []
+        for M in DECODE_M:
+            for name, K, N in QWEN3_8B:
+                q, s = O.quantize_weight_rowwise(0.02 * torch.randn(N, K, generator=g))
+                items.append((M, K, N, q, s, torch.randn(M, K, generator=g).half()))
+        nbytes = sum(decode_bytes(M, K, N) for M, K, N, *_ in items)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            for M, K, N, q, s, x in items:
+                O.linear_w8a8(x, q, s, exact=False)
+            n += 1
+            if time.perf_counter() - t0 > seconds:
+                break
+        dt = (time.perf_counter() - t0) / n
+        return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
+                "kind": "port", "sample": f"{n} full config-1 steps (20 linears) on the host, "
+                                          "torch._int_mm + fp32 dequant (oracle/w8a8_oracle.py)"}
+    if config == 2:
+        M = 512  # 1/16 of the M=8192 prefill, same K/N
+        x = torch.randn(M, 4096, generator=g).half()
+        ws = [(O.quantize_weight_rowwise(0.02 * torch.randn(N, K, generator=g)), K, N) for _, K, N in QWEN3_8B]
+        ops = sum(2 * M * K * N for _, K, N in QWEN3_8B)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            q, s = O.quantize_rows(O.rmsnorm(x, torch.ones(4096, dtype=torch.float16), 1e-6))
+            for (wq, wsc), K, N in ws:
+                a = q if K == 4096 else torch.randint(-127, 128, (M, K), dtype=torch.int8)
+                O.dequant(O.int_mm_fast(a, wq), s, wsc)
+            n += 1
+            if time.perf_counter() - t0 > seconds:
+                break
+        dt = (time.perf_counter() - t0) / n
+        return {"value": round(ops / dt / 1e12, 4), "unit": "TOP/s", "cores": torch.get_num_threads(),
+                "kind": "port", "sample": f"{n} steps of the config-2 chain at M=512 (1/16 of M=8192)"}
+    return None
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_env()
+
+    if args.impl == "reference":
+        line = reference_arm(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    init_dist(world, local)
+    runners = {1: run_config1, 2: run_config2}
+    if args.config not in runners:
+        raise SystemExit(f"config {args.config}: not wired into bench.py yet")
+    line, _ = runners[args.config](args, world, rank, dev)
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_sample(args.config)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

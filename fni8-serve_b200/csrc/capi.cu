@@ -7,6 +7,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <stdlib.h>
+
 #include <mutex>
 
 #include "fni8_common.cuh"
@@ -105,9 +107,19 @@ static int check_gemm(const int8_t* a, const int8_t* w, const void* out, int64_t
   return FNI8_OK;
 }
 
+// Largest M the AUTO choice sends to the stream-K kernel (tuning knob for measurements).
+static int64_t stream_auto_max_m() {
+  static int64_t m = [] {
+    const char* e = getenv("FNI8_STREAM_AUTO_MAX_M");
+    const long v = e ? atol(e) : 64;
+    return (int64_t)(v < 0 ? 0 : (v > kStreamMaxM ? kStreamMaxM : v));
+  }();
+  return m;
+}
+
 static int pick_path(int path, int64_t M, size_t ws_bytes, int64_t N, int64_t K) {
   if (path == FNI8_PATH_TILE || path == FNI8_PATH_STREAM) return path;
-  if (M <= 64 && ws_bytes >= stream_workspace_bytes(M, N, K)) return FNI8_PATH_STREAM;
+  if (M <= stream_auto_max_m() && ws_bytes >= stream_workspace_bytes(M, N, K)) return FNI8_PATH_STREAM;
   return FNI8_PATH_TILE;
 }
 

@@ -252,6 +252,28 @@ int encode_tmap_3d_i8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t 
                       uint64_t stride2, uint32_t box0, uint32_t box1);
 }  // namespace fni8h
 
+namespace fni8h {
+// Launch with programmatic dependent launch allowed: the kernel may be scheduled while
+// the previous kernel on the stream drains; it must execute griddepcontrol.wait before
+// touching that kernel's results. Also pins the shared-memory carveout to the maximum so
+// consecutive kernels of the library never force an L1/shared reconfiguration.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+}  // namespace fni8h
+
 #define FNI8_CHECK_LAUNCH(what)                                  \
   do {                                                           \
     cudaError_t _e = cudaGetLastError();                         \

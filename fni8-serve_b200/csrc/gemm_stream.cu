@@ -21,6 +21,8 @@
 #include "fni8_common.cuh"
 #include "gemm_internal.h"
 
+#include <stdlib.h>
+
 namespace fni8b {
 namespace strm {
 
@@ -41,12 +43,15 @@ struct Epi {
   int mode;
 };
 
-template <int NT>
+// BUDGET_KB bounds the stage ring: at ~100 KB two CTAs fit on an SM, so the next kernel
+// on the stream (launched early through PDL) can stream its first weight tiles while
+// this one drains.
+template <int NT, int BUDGET_KB>
 struct Cfg {
   static constexpr int W_BYTES = BNW * BK;
   static constexpr int X_BYTES = NT * BK;
   static constexpr int STAGE = W_BYTES + X_BYTES;
-  static constexpr int STAGES_FIT = (200 * 1024) / STAGE;
+  static constexpr int STAGES_FIT = (BUDGET_KB * 1024) / STAGE;
   static constexpr int STAGES = STAGES_FIT > 12 ? 12 : STAGES_FIT;
   static constexpr int TMEM_COLS = (2 * NT < 32) ? 32 : 2 * NT;
   static constexpr int SMEM = 1024 + STAGES * STAGE + 256;
@@ -122,11 +127,11 @@ __device__ __forceinline__ void epilogue_segment(const Epi& epi, uint32_t tbase,
   named_bar_sync(1, 128);  // s_flag is reused by the next segment
 }
 
-template <int NT>
+template <int NT, int BUDGET_KB>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a8_stream_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, Epi epi,
                        int M, int N, int K, int32_t* ws) {
-  using C = Cfg<NT>;
+  using C = Cfg<NT, BUDGET_KB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE);
@@ -171,17 +176,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int64_t u0 = static_cast<int64_t>(blockIdx.x) * U / G;
   const int64_t u1 = static_cast<int64_t>(blockIdx.x + 1) * U / G;
 
-  // The weights do not depend on the previous kernel: start streaming them while it
-  // finishes would be possible, but x does, so wait for the upstream grid here.
-  pdl_wait();
-  pdl_launch_dependents();
+  // The weights never depend on the previous kernel, the activations do. The producer
+  // therefore arms the first ring of stages and starts their weight loads before the
+  // grid-dependency wait, so the first HBM round trip overlaps the upstream kernel's tail.
+  pdl_launch_dependents();  // the next kernel may start its prologue; it waits for our completion
+  if (!(warp == 0 && lane == 0)) pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t ph = 0, armed = 0;
       int issued = 0;
-      for (int64_t u = u0; u < u1; ++u) {
+      const int64_t pre_end = u0 + ((u1 - u0) < C::STAGES ? (u1 - u0) : C::STAGES);
+      for (int64_t u = u0; u < pre_end; ++u, ++stage) {  // first use of each stage: no wait
+        const int tile = static_cast<int>(u / kb);
+        const int k = static_cast<int>(u - static_cast<int64_t>(tile) * kb);
+        uint8_t* sw = smem + stage * C::STAGE;
+        mbar_arrive_expect_tx(&full[stage], C::STAGE);
+        tma_load_2d(&tmW, &full[stage], sw, k * BK, tile * BNW);
+      }
+      pdl_wait();
+      stage = 0;
+      for (int64_t u = u0; u < pre_end; ++u, ++stage) {
+        const int k = static_cast<int>(u % kb);
+        tma_load_2d(&tmX, &full[stage], smem + stage * C::STAGE + C::W_BYTES, k * BK, 0);
+        ++issued;
+      }
+      if (stage == C::STAGES) {
+        stage = 0;
+        ph = 1;
+      }
+      for (int64_t u = pre_end; u < u1; ++u) {
         const int tile = static_cast<int>(u / kb);
         const int k = static_cast<int>(u - static_cast<int64_t>(tile) * kb);
         if (!mbar_wait(&empty[stage], ph ^ 1u, &g_status, kCodeProducer)) break;
@@ -324,11 +349,11 @@ size_t stream_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   return static_cast<size_t>(G) * (128 * static_cast<size_t>(stream_nt(M)) + 1) * sizeof(int32_t);
 }
 
-template <int NT>
-static int launch_stream(const CUtensorMap& tw, const CUtensorMap& tx, const strm::Epi& epi, int M, int N, int K,
-                         int grid, int32_t* ws, cudaStream_t st) {
-  using C = strm::Cfg<NT>;
-  auto kern = strm::w8a8_stream_kernel<NT>;
+template <int NT, int BUDGET_KB>
+static int launch_stream_cfg(const CUtensorMap& tw, const CUtensorMap& tx, const strm::Epi& epi, int M, int N, int K,
+                             int grid, int32_t* ws, cudaStream_t st) {
+  using C = strm::Cfg<NT, BUDGET_KB>;
+  auto kern = strm::w8a8_stream_kernel<NT, BUDGET_KB>;
   static bool configured[kMaxDevices] = {};
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) return fail(FNI8_ERR_CUDA, "no current CUDA device");
@@ -350,6 +375,21 @@ static int launch_stream(const CUtensorMap& tw, const CUtensorMap& tx, const str
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, epi, M, N, K, ws);
   if (e != cudaSuccess) return cuda_status(e, "launch stream gemm");
   return FNI8_OK;
+}
+
+static int stream_budget_kb() {
+  static int kb = [] {
+    const char* e = getenv("FNI8_STREAM_SMEM_KB");
+    return (e != nullptr && atoi(e) == 200) ? 200 : 100;
+  }();
+  return kb;
+}
+
+template <int NT>
+static int launch_stream(const CUtensorMap& tw, const CUtensorMap& tx, const strm::Epi& epi, int M, int N, int K,
+                         int grid, int32_t* ws, cudaStream_t st) {
+  if (stream_budget_kb() == 200) return launch_stream_cfg<NT, 200>(tw, tx, epi, M, N, K, grid, ws, st);
+  return launch_stream_cfg<NT, 100>(tw, tx, epi, M, N, K, grid, ws, st);
 }
 
 int stream_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
@@ -379,3 +419,4 @@ int stream_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const fl
 }
 
 }  // namespace fni8h
+

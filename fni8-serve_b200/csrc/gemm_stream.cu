@@ -420,3 +420,75 @@ int stream_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const fl
 
 }  // namespace fni8h
 
+// ------------------------------------------------------------------------------------
+// Allocation-free variant of the skinny GEMM (fni8_gemm_w8a8_noalloc).
+//
+// The stream-K kernel needs a zero-maintained int32 scratch area for its partial tiles.
+// Callers that cannot allocate device memory — an engine that has already reserved the
+// whole HBM for its KV cache and weights, or a host program reaching this library through
+// a thin FFI with no device allocator of its own — get that scratch from a fixed array
+// compiled into the library instead. Every GPU that loads the library holds the array
+// until the process exits.
+// ------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace fni8b {
+namespace strm {
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB per device
+constexpr int64_t kNoAllocMaxM = 32;                        // rows of activations per call
+static __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocScratchBytes / sizeof(int32_t)];
+}  // namespace strm
+}  // namespace fni8b
+
+namespace fni8h {
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[kMaxDevices];
+
+// Device address of the scratch array on the current device. The first call on a device
+// looks the address up (in host code the array's name is only a stand-in for it) and
+// zeroes the array on `st`; later calls reuse both.
+static int noalloc_scratch(int dev, cudaStream_t st, void** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, strm::g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    e = cudaMemsetAsync(p, 0, strm::kNoAllocScratchBytes, st);
+    if (e != cudaSuccess) return cuda_status(e, "clear no-alloc scratch");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return FNI8_OK;
+}
+
+}  // namespace fni8h
+
+extern "C" int fni8_gemm_w8a8_noalloc(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                                      const void* bias, const void* residual, void* out, int out_dtype, int64_t M,
+                                      int64_t N, int64_t K, void* stream) {
+  using namespace fni8h;
+  if (M < 0 || N <= 0 || K <= 0) return fail(FNI8_ERR_INVALID, "bad GEMM shape M=%lld N=%lld K=%lld", (long long)M,
+                                              (long long)N, (long long)K);
+  if (K % 16 != 0) return fail(FNI8_ERR_UNSUPPORTED, "K=%lld must be a multiple of 16", (long long)K);
+  if (N >= (1LL << 31) || K >= (1LL << 31)) return fail(FNI8_ERR_UNSUPPORTED, "GEMM dimensions must be < 2^31");
+  if (M > strm::kNoAllocMaxM)
+    return fail(FNI8_ERR_UNSUPPORTED, "the allocation-free GEMM takes at most %lld rows (got %lld)",
+                (long long)strm::kNoAllocMaxM, (long long)M);
+  if (out_dtype != FNI8_F16 && out_dtype != FNI8_BF16)
+    return fail(FNI8_ERR_INVALID, "out_dtype %d: expected F16 or BF16", out_dtype);
+  if (M == 0) return FNI8_OK;
+  if (a == nullptr || w == nullptr || out == nullptr || a_scale == nullptr || w_scale == nullptr)
+    return fail(FNI8_ERR_INVALID, "null GEMM operand");
+  const size_t need = stream_workspace_bytes(M, N, K);
+  if (need > strm::kNoAllocScratchBytes)
+    return fail(FNI8_ERR_UNSUPPORTED, "problem needs %zu scratch bytes, the built-in area holds %zu", need,
+                strm::kNoAllocScratchBytes);
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return fail(FNI8_ERR_CUDA, "no current CUDA device");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  void* scratch = nullptr;
+  if (int s = noalloc_scratch(dev, st, &scratch)) return s;
+  return stream_gemm(a, a_scale, w, w_scale, bias, residual, out, out_dtype == FNI8_F16 ? 0 : 1, M, N, K, scratch,
+                     strm::kNoAllocScratchBytes, st);
+}

@@ -118,6 +118,21 @@ FNI8_API int fni8_gemm_w8a8_ex(const int8_t* a, const float* a_scale, const int8
                       const void* bias, const void* residual, void* out, int out_dtype, int64_t M, int64_t N,
                       int64_t K, int path, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free form of fni8_gemm_w8a8 for decode-sized problems. No counterpart in
+ * the reference. For callers that cannot allocate device memory (an engine that has
+ * reserved all of HBM up front, or a host reaching this library through a bare FFI with
+ * no device allocator): instead of a caller-provided workspace it uses a 4 MiB scratch
+ * array built into the library, which every GPU that loads the library holds until the
+ * process exits. Takes M <= 32 rows (larger M, or an N/K split that would need more than
+ * 4 MiB, returns FNI8_ERR_UNSUPPORTED) and calls no allocator. The first call on a device
+ * looks up the array's address and zeroes it on `stream`; make that first call before
+ * any stream capture. All calls on a device share the array: calls that overlap on the
+ * GPU (other streams, other threads) race and must be serialised by the caller. The
+ * kernels leave the array zeroed after every completed call. */
+FNI8_API int fni8_gemm_w8a8_noalloc(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                                    const void* bias, const void* residual, void* out, int out_dtype, int64_t M,
+                                    int64_t N, int64_t K, void* stream);
+
 /* Raw int32 accumulators acc[M, N] = a . w^T (the int8 x int8 -> int32 matmul of the
  * reference's gemm_w8a8; used for the bit-exact check). */
 FNI8_API int fni8_gemm_w8a8_i32(const int8_t* a, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K, int path,

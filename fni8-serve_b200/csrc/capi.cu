@@ -65,7 +65,7 @@ static EncodeTiledFn encode_fn() {
 }
 
 static int encode(CUtensorMap* map, const void* base, cuuint32_t rank, const cuuint64_t* dims,
-                  const cuuint64_t* strides, const cuuint32_t* box) {
+                  const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapDataType dt, CUtensorMapSwizzle sw) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return fail(FNI8_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (no CUDA driver?)");
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return fail(FNI8_ERR_ALIGN, "TMA base must be 16-byte aligned");
@@ -73,9 +73,8 @@ static int encode(CUtensorMap* map, const void* base, cuuint32_t rank, const cuu
     if (strides[i] % 16 != 0) return fail(FNI8_ERR_ALIGN, "TMA stride %llu not a multiple of 16 bytes",
                                           (unsigned long long)strides[i]);
   const cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, dt, rank, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FNI8_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return FNI8_OK;
 }
@@ -85,7 +84,7 @@ int encode_tmap_2d_i8(CUtensorMap* map, const void* base, uint64_t inner, uint64
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {row_stride_bytes};
   const cuuint32_t box[2] = {box_inner, box_outer};
-  return encode(map, base, 2, dims, strides, box);
+  return encode(map, base, 2, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 int encode_tmap_3d_i8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
@@ -93,7 +92,16 @@ int encode_tmap_3d_i8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t 
   const cuuint64_t dims[3] = {d0, d1, d2};
   const cuuint64_t strides[2] = {stride1, stride2};
   const cuuint32_t box[3] = {box0, box1, 1};
-  return encode(map, base, 3, dims, strides, box);
+  return encode(map, base, 3, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int encode_tmap_2d_16(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64_t outer,
+                      uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  return encode(map, base, 2, dims, strides, box,
+                bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 // Shape/pointer checks shared by the dense GEMM entry points.
@@ -111,7 +119,7 @@ static int check_gemm(const int8_t* a, const int8_t* w, const void* out, int64_t
 static int64_t stream_auto_max_m() {
   static int64_t m = [] {
     const char* e = getenv("FNI8_STREAM_AUTO_MAX_M");
-    const long v = e ? atol(e) : 64;
+    const long v = e ? atol(e) : 16;
     return (int64_t)(v < 0 ? 0 : (v > kStreamMaxM ? kStreamMaxM : v));
   }();
   return m;
@@ -120,6 +128,7 @@ static int64_t stream_auto_max_m() {
 static int pick_path(int path, int64_t M, size_t ws_bytes, int64_t N, int64_t K) {
   if (path == FNI8_PATH_TILE || path == FNI8_PATH_STREAM) return path;
   if (M <= stream_auto_max_m() && ws_bytes >= stream_workspace_bytes(M, N, K)) return FNI8_PATH_STREAM;
+  if (path == FNI8_PATH_FUSED) return FNI8_PATH_TILE;
   return FNI8_PATH_TILE;
 }
 
@@ -162,10 +171,11 @@ extern "C" int fni8_device_status(int* code_out) {
   if (code_out == nullptr) return fail(FNI8_ERR_INVALID, "null code_out");
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_status(e, "cudaDeviceSynchronize");
-  int a = 0, b = 0;
+  int a = 0, b = 0, c = 0;
   if (int s = tile_status_read_and_clear(&a)) return s;
   if (int s = stream_status_read_and_clear(&b)) return s;
-  *code_out = a != 0 ? a : b;
+  if (int s = skinny_status_read_and_clear(&c)) return s;
+  *code_out = a != 0 ? a : (b != 0 ? b : c);
   return *code_out == 0 ? FNI8_OK : fail(FNI8_ERR_DEVICE_TIMEOUT, "device watchdog code 0x%x", *code_out);
 }
 
@@ -215,14 +225,38 @@ extern "C" int fni8_gemm_w8a8_i32(const int8_t* a, const int8_t* w, int32_t* acc
                   static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int fni8_linear_w8a8_ex(const void* x, int dtype, const int8_t* w, const float* w_scale, const void* bias,
+                                   void* out, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
+                                   int path, void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != FNI8_F16 && dtype != FNI8_BF16) return fail(FNI8_ERR_INVALID, "dtype %d: expected F16 or BF16", dtype);
+  if (path < FNI8_PATH_AUTO || path > FNI8_PATH_FUSED) return fail(FNI8_ERR_INVALID, "unknown path %d", path);
+  if (M < 0 || N <= 0 || K <= 0) return fail(FNI8_ERR_INVALID, "bad linear shape M=%lld N=%lld K=%lld", (long long)M,
+                                              (long long)N, (long long)K);
+  if (K % 16 != 0) return fail(FNI8_ERR_UNSUPPORTED, "K=%lld must be a multiple of 16", (long long)K);
+  if (M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31))
+    return fail(FNI8_ERR_UNSUPPORTED, "GEMM dimensions must be < 2^31");
+  if (M == 0) return FNI8_OK;
+  if (x == nullptr || w == nullptr || w_scale == nullptr || out == nullptr)
+    return fail(FNI8_ERR_INVALID, "null linear operand");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // decode sizes: per-token quantisation fused into the GEMM, one launch, no scratch
+  const bool fused_ok = skinny_supported(x, M, N, K);
+  if (path == FNI8_PATH_FUSED) {
+    if (!fused_ok) return fail(FNI8_ERR_UNSUPPORTED, "fused decode linear takes M <= %lld and 16-byte aligned x",
+                               (long long)kSkinnyMaxM);
+    return skinny_linear(x, dtype == FNI8_BF16, w, w_scale, bias, out, M, N, K, st);
+  }
+  if (path == FNI8_PATH_AUTO && fused_ok && M <= skinny_auto_max_m())
+    return skinny_linear(x, dtype == FNI8_BF16, w, w_scale, bias, out, M, N, K, st);
+  if (q_scratch == nullptr || s_scratch == nullptr) return fail(FNI8_ERR_INVALID, "null linear scratch");
+  if (int s = fni8_quantize_rows_i8(x, dtype, M, K, q_scratch, s_scratch, stream)) return s;
+  return gemm_any(q_scratch, s_scratch, w, w_scale, bias, nullptr, out, dtype == FNI8_F16 ? 0 : 1, M, N, K, path,
+                  workspace, workspace_bytes, st);
+}
+
 extern "C" int fni8_linear_w8a8(const void* x, int dtype, const int8_t* w, const float* w_scale, const void* bias,
                                 void* out, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
                                 void* workspace, size_t workspace_bytes, void* stream) {
-  if (dtype != FNI8_F16 && dtype != FNI8_BF16) return fail(FNI8_ERR_INVALID, "dtype %d: expected F16 or BF16", dtype);
-  if (int s = check_gemm(q_scratch, w, out, M, N, K)) return s;
-  if (M == 0) return FNI8_OK;
-  if (x == nullptr || w_scale == nullptr || s_scratch == nullptr) return fail(FNI8_ERR_INVALID, "null linear operand");
-  if (int st = fni8_quantize_rows_i8(x, dtype, M, K, q_scratch, s_scratch, stream)) return st;
-  return gemm_any(q_scratch, s_scratch, w, w_scale, bias, nullptr, out, dtype == FNI8_F16 ? 0 : 1, M, N, K,
-                  FNI8_PATH_AUTO, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+  return fni8_linear_w8a8_ex(x, dtype, w, w_scale, bias, out, M, N, K, q_scratch, s_scratch, FNI8_PATH_AUTO,
+                             workspace, workspace_bytes, stream);
 }

@@ -26,4 +26,12 @@ int stream_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const fl
 int stream_status_read_and_clear(int* code);
 constexpr int64_t kStreamMaxM = 256;
 
+// Fused quantise + GEMM for decode (gemm_skinny.cu): fp16/bf16 x[M, K] in, out[M, N].
+constexpr int64_t kSkinnyMaxM = 32;
+bool skinny_supported(const void* x, int64_t M, int64_t N, int64_t K);
+int64_t skinny_auto_max_m();
+int skinny_linear(const void* x, bool bf16, const int8_t* w, const float* w_scale, const void* bias, void* out,
+                  int64_t M, int64_t N, int64_t K, cudaStream_t st);
+int skinny_status_read_and_clear(int* code);
+
 }  // namespace fni8h

@@ -29,8 +29,26 @@ namespace strm {
 constexpr int kThreads = 192;
 constexpr int BNW = 128;  // weight rows per tile (MMA M)
 constexpr int BK = 128;
+constexpr int64_t kL2AheadUnits = 24;  // 384 KB of weights per CTA prefetched into L2
 
 static __device__ int g_status;
+
+// Timeline tracing, compiled in only for measurement builds (-DFNI8_TRACE): per CTA, the
+// globaltimer of a few pipeline events, in launch order.
+#ifdef FNI8_TRACE
+static __device__ unsigned long long g_trace[65536 * 8];
+static __device__ unsigned int g_trace_seq;
+#define FNI8_TRACE_SLOT                                                  \
+  __shared__ unsigned int s_trace_slot;                                  \
+  if (threadIdx.x == 0) s_trace_slot = atomicAdd(&g_trace_seq, 1u) % 65536u;
+#define FNI8_TRACE_AT(i) (g_trace[s_trace_slot * 8u + (i)] = globaltimer_ns())
+#define FNI8_TRACE_VAL(i, v) (g_trace[s_trace_slot * 8u + (i)] = (v))
+#else
+#define FNI8_TRACE_SLOT
+#define FNI8_TRACE_AT(i) ((void)0)
+#define FNI8_TRACE_VAL(i, v) ((void)0)
+#endif
+
 enum : int { kCodeProducer = 0x201, kCodeMma = 0x202, kCodeEpilogue = 0x203, kCodeDrain = 0x204 };
 enum : int { kOutF16 = 0, kOutBF16 = 1, kOutI32 = 2 };
 
@@ -144,7 +162,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* s_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  FNI8_TRACE_SLOT
   if (threadIdx.x == 0) {
+    FNI8_TRACE_AT(0);
+    FNI8_TRACE_VAL(7, (static_cast<unsigned long long>(N) << 32) | blockIdx.x);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -195,7 +216,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&full[stage], C::STAGE);
         tma_load_2d(&tmW, &full[stage], sw, k * BK, tile * BNW);
       }
+      // Pull the following weight tiles of this CTA into L2 as well, so HBM keeps
+      // streaming while the upstream kernel finishes (bounded so the prefetched set of
+      // all CTAs stays well inside the 126 MB L2).
+      {
+        const int64_t l2_end = (u1 - pre_end) < kL2AheadUnits ? u1 : pre_end + kL2AheadUnits;
+        for (int64_t u = pre_end; u < l2_end; ++u) {
+          const int tile = static_cast<int>(u / kb);
+          tma_prefetch_l2_2d(&tmW, static_cast<int>(u - static_cast<int64_t>(tile) * kb) * BK, tile * BNW);
+        }
+      }
       pdl_wait();
+      FNI8_TRACE_AT(1);
       stage = 0;
       for (int64_t u = u0; u < pre_end; ++u, ++stage) {
         const int k = static_cast<int>(u % kb);
@@ -247,6 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          if (u == u0 && k == kbeg) FNI8_TRACE_AT(2);
           const uint8_t* sw = smem + stage * C::STAGE;
           const uint64_t adesc = sw128_kmajor_desc(smem_u32(sw));
           const uint64_t bdesc = sw128_kmajor_desc(smem_u32(sw + C::W_BYTES));
@@ -268,6 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       umma_commit(drain);
       mbar_wait(drain, 0, &g_status, kCodeDrain);
+      FNI8_TRACE_AT(3);
     }
     __syncwarp();
   } else {
@@ -288,6 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // in one warp must not leave the others waiting at a named barrier
       const int all_ok = named_bar_and(1, 128, ok);
       if (!all_ok) break;
+      if (threadIdx.x == 64 && u == u0) FNI8_TRACE_AT(4);
       tc_fence_after();
       const int owner = owner_of(static_cast<int64_t>(tile) * kb, U, G);
       int32_t* slot = ws + static_cast<int64_t>(owner) * BNW * NT;
@@ -306,9 +341,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (acc == 0) aph ^= 1u;
       u += kend - kbeg;
     }
+    if (threadIdx.x == 64) FNI8_TRACE_AT(5);
   }
 
   __syncthreads();
+  if (threadIdx.x == 0) FNI8_TRACE_AT(6);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
@@ -321,6 +358,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 namespace fni8h {
 
 using namespace fni8b;
+
+#ifdef FNI8_TRACE
+extern "C" __attribute__((visibility("default"))) int fni8_trace_read(unsigned long long* dst, int n_records) {
+  const size_t bytes = static_cast<size_t>(n_records) * 8 * sizeof(unsigned long long);
+  if (cudaMemcpyFromSymbol(dst, strm::g_trace, bytes) != cudaSuccess) return FNI8_ERR_CUDA;
+  unsigned int z = 0;
+  if (cudaMemcpyToSymbol(strm::g_trace_seq, &z, sizeof(z)) != cudaSuccess) return FNI8_ERR_CUDA;
+  return FNI8_OK;
+}
+#endif
 
 int stream_status_read_and_clear(int* code) {
   int v = 0, z = 0;
@@ -360,6 +407,10 @@ static int launch_stream_cfg(const CUtensorMap& tw, const CUtensorMap& tx, const
   if (!configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(stream gemm)");
+    // whole unified L1/shared array as shared memory: the next kernel on the stream can
+    // then become resident next to this one (PDL) without an L1/shared reconfiguration
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return cuda_status(e, "carveout(stream gemm)");
     configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
@@ -369,7 +420,7 @@ static int launch_stream_cfg(const CUtensorMap& tw, const CUtensorMap& tx, const
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fni8h::pdl_enabled();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, epi, M, N, K, ws);

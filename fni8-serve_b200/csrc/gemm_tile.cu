@@ -35,6 +35,7 @@ constexpr int BK = 128;  // bytes == int8 elements per stage along K
 constexpr int kThreads = 192;
 constexpr int kMaxSeg = fni8h::kTileMaxSeg;
 constexpr int kGroupM = 16;
+constexpr int kL2AheadUnits = 16;  // weight k-blocks per CTA prefetched into L2 before the PDL wait
 
 static __device__ int g_status;  // watchdog word of this file
 
@@ -288,6 +289,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           pre_row[pre] = tc.row0;
           pre_k[pre] = k;
         }
+        {  // weight tiles of the next units into L2 while the upstream kernel drains
+          int tt = t, kk = k, nb = tc.n_blk;
+          for (int i = 0; i < kL2AheadUnits && tt < total; ++i) {
+            tma_prefetch_l2_2d(&tmB, kk * BK, nb * BN);
+            if (++kk == kb) {
+              kk = 0;
+              tt += gridDim.x;
+              if (tt < total) nb = decode_tile<GROUPED>(tt, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S).n_blk;
+            }
+          }
+        }
         pdl_wait();
         for (int i = 0; i < pre; ++i) tma_load_2d(&tmA, &full[i], smem + i * C::STAGE, pre_k[i] * BK, pre_row[i]);
         issued = pre;
@@ -420,6 +432,10 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Epi& epi, const G
   if (!configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return fni8h::cuda_status(e, "cudaFuncSetAttribute(tile gemm)");
+    // whole unified L1/shared array as shared memory: the next kernel on the stream can
+    // then become resident next to this one (PDL) without an L1/shared reconfiguration
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return fni8h::cuda_status(e, "carveout(tile gemm)");
     configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
@@ -429,7 +445,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Epi& epi, const G
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = fni8h::pdl_enabled();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, epi, grp, M, N, K, vec_ok ? 1 : 0);

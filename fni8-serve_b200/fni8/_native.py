@@ -17,7 +17,7 @@ OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_ALIGN, ERR_CUDA, ERR_WORKSPACE, ERR_DEVICE
 F16, BF16, F32, I32, I8 = range(5)
 ACT_SILU, ACT_GELU_TANH = 0, 1
 SCORE_SOFTMAX, SCORE_SIGMOID = 0, 1
-PATH_AUTO, PATH_TILE, PATH_STREAM = 0, 1, 2
+PATH_AUTO, PATH_TILE, PATH_STREAM, PATH_FUSED = 0, 1, 2, 3
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int
@@ -43,6 +43,7 @@ SIGNATURES: dict[str, tuple] = {
     "fni8_gemm_w8a8_i32": (_i, [_p, _p, _p, _i64, _i64, _i64, _i, _p, _sz, _p]),
     "fni8_gemm_w8a8_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i64, _i64, _i64, _p]),
     "fni8_linear_w8a8": (_i, [_p, _i, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _sz, _p]),
+    "fni8_linear_w8a8_ex": (_i, [_p, _i, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _i, _p, _sz, _p]),
     "fni8_moe_route": (_i, [_p, _i64, _i64, _i64, _i, _p, _i64, _i64, _i, _f, _i, _p, _p, _p]),
     "fni8_moe_plan_workspace_bytes": (_sz, [_i64, _i64]),
     "fni8_moe_plan": (_i, [_p, _i64, _i64, _p, _p, _p, _p, _p, _sz, _p]),

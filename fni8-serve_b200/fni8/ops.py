@@ -249,14 +249,16 @@ def linear_q(q: torch.Tensor, scale: torch.Tensor, qt: QTensor, bias: torch.Tens
     return out.reshape(*q.shape[:-1], N)
 
 
-def linear(x: torch.Tensor, qt: QTensor, bias: torch.Tensor | None = None) -> torch.Tensor:
-    """fni8.linear: per-token int8 quantisation of x, int8 GEMM, dequant epilogue (+bias)."""
+def linear(x: torch.Tensor, qt: QTensor, bias: torch.Tensor | None = None, path: int = nat.PATH_AUTO) -> torch.Tensor:
+    """fni8.linear: per-token int8 quantisation of x, int8 GEMM, dequant epilogue (+bias).
+
+    `path` (not in the reference signature) forces a kernel; the default picks by shape."""
     _need_cuda(x, "linear")
     dt = _act_dtype(x, "linear")
     K = x.shape[-1]
     _check_weight(qt, x.device, K, "linear")
     N = qt.data.shape[0]
-    sc = _sidecar(x)
+    sc = _sidecar(x) if path == nat.PATH_AUTO else None
     if sc is not None:
         return linear_q(sc[0], sc[1], qt, bias=bias, out_dtype=x.dtype)
     x2 = x.reshape(-1, K).contiguous()
@@ -266,8 +268,8 @@ def linear(x: torch.Tensor, qt: QTensor, bias: torch.Tensor | None = None) -> to
     s = torch.empty((M,), dtype=torch.float32, device=x.device)
     b = bias.to(x.dtype).contiguous() if bias is not None else None
     ws, wsb = _ws(x.device)
-    nat.call("fni8_linear_w8a8", _vp(x2), dt, _vp(qt.data), _vp(qt.scale), _vp(b), _vp(out), M, N, K, _vp(q), _vp(s),
-             ws, wsb, _stream(x.device))
+    nat.call("fni8_linear_w8a8_ex", _vp(x2), dt, _vp(qt.data), _vp(qt.scale), _vp(b), _vp(out), M, N, K, _vp(q),
+             _vp(s), path, ws, wsb, _stream(x.device))
     return out.reshape(*x.shape[:-1], N)
 
 

@@ -254,3 +254,27 @@ def test_zero_rows_and_errors():
         fni8.linear(torch.zeros(4, 64, dtype=torch.float16, device=DEV),
                     fni8.QTensor(qt.data, qt.scale, scheme="per_group_i4", group_size=32, codebook="int4"))
     assert fni8.device_status() == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (3, 6144, 4096), (16, 4096, 12288), (17, 24576, 4096),
+                                   (32, 1000, 2048), (5, 128, 16), (8, 640, 4112), (2, 300, 1024)])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_fused_decode_linear_bit_exact(M, N, K, dtype):
+    """fni8.linear at decode sizes runs one fused kernel (per-token quantisation inside
+    the GEMM, split-K over a thread-block cluster reduced through DSMEM). It must equal
+    the oracle and the unfused quantiser + GEMM path bit for bit, with and without bias."""
+    import fni8
+
+    x = act_input(M, K, 7 * M + N, dtype)
+    wq, ws = weight(N, K, K + 1)
+    qt = fni8.QTensor(wq.to(DEV), ws.to(DEV))
+    bias = (0.1 * torch.randn(N, generator=gen(9))).to(dtype)
+    from fni8 import _native as nat
+
+    for b in (None, bias):
+        got = fni8.linear(x.to(DEV), qt, bias=None if b is None else b.to(DEV), path=nat.PATH_FUSED).cpu()
+        assert torch.equal(got, O.linear_w8a8(x, wq, ws, bias=b, exact=False))
+        q, s = fni8.quantize_rows(x.to(DEV))
+        unfused = fni8.linear_q(q, s, qt, bias=None if b is None else b.to(DEV), out_dtype=dtype).cpu()
+        assert torch.equal(got, unfused)
+    assert fni8.device_status() == 0

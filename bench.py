@@ -229,6 +229,27 @@ def per_launch_ms(fn, reps=20):
     return sum(a.elapsed_time(b) for a, b in ev) / reps
 
 
+def time_eager(fn, steps, warmup, world, flush=None):
+    """Time `steps` eager calls of fn() with CUDA events (for steps that synchronise with
+    the host, e.g. expert-parallel all_to_all split sizes); max over ranks."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    total = 0.0
+    for _ in range(steps):
+        if flush is not None:
+            flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        total += a.elapsed_time(b)
+    barrier(world)
+    return max_over_ranks(total, world)
+
+
 # ------------------------------------------------------------------ configs (our arm)
 def run_config1(args, world, rank, dev):
     import fni8
@@ -382,91 +403,307 @@ def run_config2(args, world, rank, dev):
     return line, None
 
 
+def base_line(metric, value, unit, world, args, ms_step, config, dtype="int8", scaling="weak"):
+    return {"metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None, "dtype": dtype, "data": "synthetic", "config": config}
+
+
+def run_config0(args, world, rank, dev):
+    """one fni8.linear, M=256 K=1024 N=6144 (Qwen3-0.6B gate_up)."""
+    import fni8
+
+    M, K, N = 256, 1024, 6144
+    qt = make_weight(N, K, 1, dev)
+    x = act(M, K, 2, dev)
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    ops = 2 * M * N * K
+    with ClockSampler(dev) as clk:
+        ms = time_graph(lambda: fni8.linear(x, qt), args.steps, args.warmup, world,
+                        flush=lambda: flush_l2(flush_buf)) / args.steps
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(M, N, dtype=torch.float16).pin_memory()
+
+    def e2e_step():
+        yh.copy_(fni8.linear(xh.to(dev, non_blocking=True), qt), non_blocking=True)
+
+    e2e_ms = time_eager(e2e_step, args.steps, args.warmup, world) / args.steps
+    line = base_line("W8A8 linear TOP/s (M=256 K=1024 N=6144; % int8 TC peak)", world * ops / (ms * 1e-3) / 1e12,
+                     "TOP/s", world, args, ms,
+                     {"workload": "BASELINE config 0: single W8A8 linear", "M": M, "K": K, "N": N,
+                      "l2": "flushed between steps (256 MB write)", "parallelism": f"replicas{world}"})
+    line["roofline"] = {"bound": "tensor", "achieved": round(ops / (ms * 1e-3) / 1e12, 1),
+                        "peak": INT8_DENSE_NOMINAL_TOPS, "unit": "TOP/s",
+                        "frac": round(ops / (ms * 1e-3) / 1e12 / INT8_DENSE_NOMINAL_TOPS, 4),
+                        "traffic": committed_traffic("cfg0_linear"), "kernel": "quantise + w8a8_tile_kernel",
+                        "note": "3.2 GOP in one launch pair: launch-latency bound, not tensor bound"}
+    line["e2e"] = {"value": round(world * ops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOP/s",
+                   "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2}
+    line["gpu_launches"] = 2 * args.steps
+    line["clocks"] = clk.summary()
+    return line, None
+
+
+MOE = dict(T=4096, E=128, k=8, H=2048, I=768)
+
+
+def moe_inputs(dev, rank):
+    """BASELINE config 3 inputs: tokens N(0,1); router logits N(0,1) + a per-expert bias
+    -1.1*log(rank) over a seeded expert ranking (Zipf s=1.1 weights), shared by all ranks."""
+    T, E, H = MOE["T"], MOE["E"], MOE["H"]
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(T, H, generator=g, device=dev).half()
+    order = torch.randperm(E, generator=torch.Generator().manual_seed(7))
+    zipf = torch.empty(E)
+    zipf[order] = -1.1 * torch.log(torch.arange(1, E + 1, dtype=torch.float32))
+    logits = torch.randn(T, E, generator=g, device=dev) + zipf.to(dev)
+    return x, logits
+
+
+def moe_experts_on(dev, lo, hi):
+    """Experts [lo, hi) of the config-3 layer: the same seeded weights on every rank."""
+    from fni8.moe import ExpertStack
+
+    E, H, I = MOE["E"], MOE["H"], MOE["I"]
+    gu = [make_weight(2 * I, H, 5000 + e, dev) for e in range(lo, hi)]
+    dn = [make_weight(H, I, 9000 + e, dev) for e in range(lo, hi)]
+    return ExpertStack(torch.stack([w.data for w in gu]), torch.stack([w.scale for w in gu]),
+                       torch.stack([w.data for w in dn]), torch.stack([w.scale for w in dn]))
+
+
+def run_config3(args, world, rank, dev):
+    """Qwen3-30B-A3B-shaped MoE layer, expert-parallel over the ranks."""
+    import fni8.moe as moe
+    from fni8.parallel import ExpertParallelMoE, expert_shard
+
+    T, E, k, H, I = MOE["T"], MOE["E"], MOE["k"], MOE["H"], MOE["I"]
+    x, logits = moe_inputs(dev, rank)
+    lo, hi = expert_shard(E, world, rank)
+    stack = moe_experts_on(dev, lo, hi)
+    ops = 2 * T * k * (2 * I * H + H * I)
+    if world == 1:
+        def step():
+            topi, topw = moe.route(logits, k)
+            return moe.experts(x, topi, topw, stack)
+
+        with ClockSampler(dev) as clk:
+            ms = time_graph(step, args.steps, args.warmup, world) / args.steps
+        timing = "CUDA graph replay"
+    else:
+        ep = ExpertParallelMoE(stack, E)
+
+        def step():
+            topi, topw = moe.route(logits, k)
+            return ep(x, topi, topw)
+
+        with ClockSampler(dev) as clk:
+            ms = time_eager(step, args.steps, args.warmup, world) / args.steps
+        timing = "eager (all_to_all split sizes visit the host), CUDA events"
+    # grouped-GEMM share: the two grouped launches alone, on the routed inputs
+    topi, topw = moe.route(logits, k)
+    from fni8.moe import grouped_gemm, plan
+    from fni8.ops import act_and_mul_quant, quantize_rows
+
+    xq, xs = quantize_rows(x)
+    counts, offsets, ros, sor = plan(topi, E)
+    from fni8.parallel import gather_rows
+
+    n = int(offsets[-1].item())
+    aq, as_ = gather_rows(xq, xs, sor, n, k)
+    iota = torch.arange(E, dtype=torch.int32, device=dev)
+    full = moe_experts_on(dev, 0, E) if world > 1 else stack
+    h = grouped_gemm(aq, as_, full.w_gu, full.s_gu, iota, offsets[:E], counts)
+    hq, hs = act_and_mul_quant(h)
+    t_gu = per_launch_ms(lambda: grouped_gemm(aq, as_, full.w_gu, full.s_gu, iota, offsets[:E], counts), reps=10)
+    t_dn = per_launch_ms(lambda: grouped_gemm(hq, hs, full.w_dn, full.s_dn, iota, offsets[:E], counts), reps=10)
+    ach = ops / ((t_gu + t_dn) * 1e-3) / 1e12
+    wbytes = E * (2 * I * H + H * I)
+    line = base_line("MoE expert layer tokens/s (E=128 top-8 H=2048 I=768, W8A8 grouped GEMM, expert parallel)",
+                     world * T / (ms * 1e-3), "tokens/s", world, args, ms,
+                     {"workload": "BASELINE config 3: Qwen3-30B-A3B-shaped MoE layer", "tokens_per_rank": T,
+                      "experts": E, "top_k": k, "hidden": H, "intermediate": I, "router": "N(0,1)+Zipf(1.1) bias",
+                      "parallelism": f"ep{world}", "timing": timing,
+                      "l2": "inputs larger than L2 (604 MB of expert weights)"})
+    line["roofline"] = {"bound": "tensor", "achieved": round(ach, 1), "peak": INT8_DENSE_NOMINAL_TOPS,
+                        "unit": "TOP/s", "frac": round(ach / INT8_DENSE_NOMINAL_TOPS, 3),
+                        "traffic": committed_traffic("moe_grouped"),
+                        "kernel": "w8a8_tile_kernel<grouped> (gate_up + down, all 128 experts)",
+                        "weights_gbs": round(wbytes / ((t_gu + t_dn) * 1e-3) / 1e9, 1),
+                        "note": "309 GOP vs 604 MB of weights: tensor (69 us) and HBM (92 us) bounds are close"}
+    line["e2e"] = None
+    line["gpu_launches"] = 12 * args.steps
+    line["clocks"] = clk.summary()
+    return line, None
+
+
+def run_config4(args, world, rank, dev):
+    """K=8192 N=28672, M in {16, 512, 4096}, N sharded over the ranks."""
+    from fni8.parallel import ColumnParallelLinearW8A8, shard_rows
+
+    K, N = 8192, 28672
+    Ms = [16, 512, 4096]
+    full = make_weight(N, K, 77, dev)
+    shard = shard_rows(full, world, rank)
+    del full
+    xs = [act(M, K, 10 + M, dev) for M in Ms]
+    cp = ColumnParallelLinearW8A8(shard) if world > 1 else None
+    import fni8
+
+    def step():
+        for x in xs:
+            (cp(x) if cp is not None else fni8.linear(x, shard))
+
+    ops = sum(2 * M * N * K for M in Ms)
+    with ClockSampler(dev) as clk:
+        if world == 1:
+            ms = time_graph(step, args.steps, args.warmup, world) / args.steps
+        else:
+            ms = time_eager(step, args.steps, args.warmup, world) / args.steps
+    per = {}
+    for M, x in zip(Ms, xs):
+        t = per_launch_ms(lambda x=x: fni8.linear(x, shard), reps=10)
+        per[f"M{M}_shard"] = {"us": round(t * 1e3, 1), "TOP/s": round(2 * M * (N // world) * K / (t * 1e-3) / 1e12, 1),
+                              "GB/s": round(((N // world) * K + 2 * M * K + 2 * M * (N // world)) / (t * 1e-3) / 1e9, 1)}
+    line = base_line("Column-parallel W8A8 TOP/s (K=8192 N=28672, M=16/512/4096, N sharded, all-gather)",
+                     ops / (ms * 1e-3) / 1e12, "TOP/s", world, args, ms,
+                     {"workload": "BASELINE config 4: column-parallel dense sweep", "K": K, "N": N, "M": Ms,
+                      "parallelism": f"column{world}", "l2": "inputs larger than L2 (235 MB of weights)"},
+                     scaling="strong")
+    line["per_gpu"] = round(ops / (ms * 1e-3) / 1e12 / world, 1)
+    line["shard_kernels"] = per
+    line["roofline"] = {"bound": "tensor", "achieved": per["M4096_shard"]["TOP/s"], "peak": INT8_DENSE_NOMINAL_TOPS,
+                        "unit": "TOP/s", "frac": round(per["M4096_shard"]["TOP/s"] / INT8_DENSE_NOMINAL_TOPS, 3),
+                        "traffic": committed_traffic("sweep_m4096"), "kernel": "w8a8_tile_kernel (M=4096 shard)"}
+    line["e2e"] = None
+    line["gpu_launches"] = 6 * args.steps
+    line["clocks"] = clk.summary()
+    return line, None
+
+
 # ------------------------------------------------------------------ reference arm (CPU)
-def reference_arm(args, world, rank):
-    """The reference's CPU int8 path on the host cores (oracle port), same config."""
-    if rank != 0:
-        return None
+METRICS = {
+    0: ("W8A8 linear TOP/s (M=256 K=1024 N=6144; % int8 TC peak)", "TOP/s"),
+    1: ("W8A8 decode GB/s (Qwen3-8B QKV/O/gate_up/down at M=1,8,32,128,256; % of HBM)", "GB/s"),
+    2: ("W8A8 prefill TOPS (Qwen3-8B 4 GEMMs at M=8192, fused RMSNorm+quant; % int8 TC peak)", "TOP/s"),
+    3: ("MoE expert layer tokens/s (E=128 top-8 H=2048 I=768, W8A8 grouped GEMM, expert parallel)", "tokens/s"),
+    4: ("Column-parallel W8A8 TOP/s (K=8192 N=28672, M=16/512/4096, N sharded, all-gather)", "TOP/s"),
+}
+
+
+def cpu_workload(config):
+    """The reference's CPU int8 path for a config on the host cores (the oracle port:
+    torch._int_mm int8->int32 + fp32 dequant, oracle/w8a8_oracle.py), as
+    (step, work per step, scale to the metric's unit, sample description). Large configs
+    run a fixed fraction of the workload per step; the rate is what is reported."""
     from oracle import w8a8_oracle as O
 
-    torch.set_num_threads(os.cpu_count() or 1)
     g = torch.Generator().manual_seed(0)
-    if args.config == 1:
+
+    def qw(N, K):
+        return O.quantize_weight_rowwise(0.02 * torch.randn(N, K, generator=g))
+
+    if config == 0:
+        M, K, N = 256, 1024, 6144
+        wq, ws = qw(N, K)
+        x = torch.randn(M, K, generator=g).half()
+        return (lambda: O.linear_w8a8(x, wq, ws, exact=False)), 2 * M * N * K, 1e12, "the full config-0 linear"
+    if config == 1:
         items = []
         for M in DECODE_M:
             for name, K, N in QWEN3_8B:
-                q, s = O.quantize_weight_rowwise(0.02 * torch.randn(N, K, generator=g))
-                items.append((M, K, N, q, s, torch.randn(M, K, generator=g).half()))
-        nbytes = sum(decode_bytes(M, K, N) for M, K, N, *_ in items)
+                wq, ws = qw(N, K)
+                items.append((wq, ws, torch.randn(M, K, generator=g).half()))
+        nbytes = sum(decode_bytes(x.shape[0], w.shape[1], w.shape[0]) for w, _, x in items)
 
         def step():
-            for M, K, N, q, s, x in items:
-                O.linear_w8a8(x, q, s, exact=False)
+            for wq, ws, x in items:
+                O.linear_w8a8(x, wq, ws, exact=False)
 
-        unit, metric = "GB/s", "W8A8 decode GB/s (Qwen3-8B QKV/O/gate_up/down at M=1,8,32,128,256; % of HBM)"
-        work = nbytes
-        scale = 1e9
-    else:
-        raise SystemExit(f"--impl reference: config {args.config} not wired yet")
-    for _ in range(max(1, min(args.warmup, 1))):
+        return step, nbytes, 1e9, "the full config-1 step (20 linears)"
+    if config == 2:
+        M = 512
+        x = torch.randn(M, 4096, generator=g).half()
+        gamma = torch.ones(4096, dtype=torch.float16)
+        ws = {name: qw(N, K) for name, K, N in QWEN3_8B}
+
+        def step():
+            q, s = O.quantize_rows(O.rmsnorm(x, gamma, 1e-6))
+            O.dequant(O.int_mm_fast(q, ws["qkv"][0]), s, ws["qkv"][1])
+            O.dequant(O.int_mm_fast(q, ws["o"][0]), s, ws["o"][1])
+            h = O.dequant(O.int_mm_fast(q, ws["gate_up"][0]), s, ws["gate_up"][1])
+            hq, hs = O.quantize_rows(O.act_and_mul(h))
+            O.dequant(O.int_mm_fast(hq, ws["down"][0]), hs, ws["down"][1])
+
+        ops = sum(2 * M * K * N for _, K, N in QWEN3_8B)
+        return step, ops, 1e12, "the config-2 chain at M=512 tokens (1/16 of M=8192) per step"
+    if config == 3:
+        T, E, k, H, I = 256, MOE["E"], MOE["k"], MOE["H"], MOE["I"]
+        w_gu = torch.empty(E, 2 * I, H, dtype=torch.int8)
+        s_gu = torch.empty(E, 2 * I)
+        w_dn = torch.empty(E, H, I, dtype=torch.int8)
+        s_dn = torch.empty(E, H)
+        for e in range(E):
+            w_gu[e], s_gu[e] = qw(2 * I, H)
+            w_dn[e], s_dn[e] = qw(H, I)
+        x = torch.randn(T, H, generator=g).half()
+        zipf = -1.1 * torch.log(torch.arange(1, E + 1, dtype=torch.float32))[torch.randperm(E, generator=g)]
+        logits = torch.randn(T, E, generator=g) + zipf
+
+        def step():
+            topi, topw = O.moe_route(logits, k)
+            O.moe_experts_w8a8(x, topi, topw.float(), w_gu, s_gu, w_dn, s_dn, exact=False)
+
+        return step, T, 1.0, "256 of the 4096 tokens per step through all 128 experts (moe.py:99-105 loop)"
+    if config == 4:
+        K, N = 8192, 28672 // 8
+        wq, ws = qw(N, K)
+        xs = [torch.randn(M, K, generator=g).half() for M in (16, 512, 4096)]
+
+        def step():
+            for x in xs:
+                O.linear_w8a8(x, wq, ws, exact=False)
+
+        return step, sum(2 * x.shape[0] * N * K for x in xs), 1e12, "one 1/8 column shard (N=3584) at M=16/512/4096"
+    raise ValueError(config)
+
+
+def reference_arm(args, world, rank):
+    """The reference's CPU int8 path on the host cores (oracle port), same config/metric."""
+    if rank != 0:
+        return None
+    torch.set_num_threads(os.cpu_count() or 1)
+    step, work, scale, sample = cpu_workload(args.config)
+    for _ in range(max(1, min(args.warmup, 2))):
         step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step()
     dt = (time.perf_counter() - t0) / args.steps
     v = work / dt / scale
-    return {"metric": metric, "value": round(v, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
+    metric, unit = METRICS[args.config]
+    return {"metric": metric, "value": round(v, 4), "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
             "config": {"workload": f"BASELINE config {args.config}", "parallelism": "host cores"},
-            "cpu_baseline": {"value": round(v, 3), "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": f"{args.steps} full steps of config {args.config} on the host "
-                                       "(torch._int_mm int8->int32 + fp32 dequant, oracle/w8a8_oracle.py)"},
-            "e2e": {"value": round(v, 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "cpu_baseline": {"value": round(v, 4), "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(v, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def cpu_baseline_sample(config, seconds=10.0):
     """Bounded CPU sample of the same workload for the cpu_baseline key of our line."""
-    from oracle import w8a8_oracle as O
-
     torch.set_num_threads(os.cpu_count() or 1)
-    g = torch.Generator().manual_seed(0)
-    if config == 1:
-        items = []
-        for M in DECODE_M:
-            for name, K, N in QWEN3_8B:
-                q, s = O.quantize_weight_rowwise(0.02 * torch.randn(N, K, generator=g))
-                items.append((M, K, N, q, s, torch.randn(M, K, generator=g).half()))
-        nbytes = sum(decode_bytes(M, K, N) for M, K, N, *_ in items)
-        n, t0 = 0, time.perf_counter()
-        while True:
-            for M, K, N, q, s, x in items:
-                O.linear_w8a8(x, q, s, exact=False)
-            n += 1
-            if time.perf_counter() - t0 > seconds:
-                break
-        dt = (time.perf_counter() - t0) / n
-        return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(),
-                "kind": "port", "sample": f"{n} full config-1 steps (20 linears) on the host, "
-                                          "torch._int_mm + fp32 dequant (oracle/w8a8_oracle.py)"}
-    if config == 2:
-        M = 512  # 1/16 of the M=8192 prefill, same K/N
-        x = torch.randn(M, 4096, generator=g).half()
-        ws = [(O.quantize_weight_rowwise(0.02 * torch.randn(N, K, generator=g)), K, N) for _, K, N in QWEN3_8B]
-        ops = sum(2 * M * K * N for _, K, N in QWEN3_8B)
-        n, t0 = 0, time.perf_counter()
-        while True:
-            q, s = O.quantize_rows(O.rmsnorm(x, torch.ones(4096, dtype=torch.float16), 1e-6))
-            for (wq, wsc), K, N in ws:
-                a = q if K == 4096 else torch.randint(-127, 128, (M, K), dtype=torch.int8)
-                O.dequant(O.int_mm_fast(a, wq), s, wsc)
-            n += 1
-            if time.perf_counter() - t0 > seconds:
-                break
-        dt = (time.perf_counter() - t0) / n
-        return {"value": round(ops / dt / 1e12, 4), "unit": "TOP/s", "cores": torch.get_num_threads(),
-                "kind": "port", "sample": f"{n} steps of the config-2 chain at M=512 (1/16 of M=8192)"}
-    return None
+    step, work, scale, sample = cpu_workload(config)
+    step()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = (time.perf_counter() - t0) / n
+    return {"value": round(work / dt / scale, 4), "unit": METRICS[config][1], "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{n} steps of {sample}"}
 
 
 def main():
@@ -490,7 +727,7 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     init_dist(world, local)
-    runners = {1: run_config1, 2: run_config2}
+    runners = {0: run_config0, 1: run_config1, 2: run_config2, 3: run_config3, 4: run_config4}
     if args.config not in runners:
         raise SystemExit(f"config {args.config}: not wired into bench.py yet")
     line, _ = runners[args.config](args, world, rank, dev)

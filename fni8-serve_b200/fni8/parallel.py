@@ -71,16 +71,31 @@ def segments_from_counts(recv_counts: torch.Tensor):
     return exp, off, cnt
 
 
-class ExpertParallelMoE:
-    """Routed-expert block with experts sharded over the ranks of `group`."""
+class KernelOps:
+    """The device kernels one expert-parallel layer uses (the C ABI through fni8)."""
 
-    def __init__(self, local: ExpertStack, num_experts: int, group=None, act: str = "silu"):
+    quantize_rows = staticmethod(quantize_rows)
+    plan = staticmethod(plan)
+    gather_rows = staticmethod(gather_rows)
+    grouped_gemm = staticmethod(grouped_gemm)
+    act_and_mul_quant = staticmethod(act_and_mul_quant)
+    combine = staticmethod(combine)
+
+
+class ExpertParallelMoE:
+    """Routed-expert block with experts sharded over the ranks of `group`.
+
+    `ops` supplies the compute steps (default: the sm_100a kernels); the exchange logic
+    around them is what this class owns."""
+
+    def __init__(self, local: ExpertStack, num_experts: int, group=None, act: str = "silu", ops=KernelOps):
         self.local = local
         self.E = num_experts
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.act = act
+        self.ops = ops
         lo, hi = expert_shard(num_experts, self.world, self.rank)
         if local.num_experts != hi - lo:
             raise ValueError("local expert stack does not match this rank's shard")
@@ -88,23 +103,24 @@ class ExpertParallelMoE:
     def __call__(self, x: torch.Tensor, topi: torch.Tensor, topw: torch.Tensor) -> torch.Tensor:
         T, H = x.shape
         k = topi.shape[1]
-        xq, xs = quantize_rows(x)
-        counts, offsets, ros, sor = plan(topi, self.E)
+        ops = self.ops
+        xq, xs = ops.quantize_rows(x)
+        counts, offsets, ros, sor = ops.plan(topi, self.E)
         recv_counts, send_splits, recv_splits = exchange_plan(counts, self.world, self.group)
         n_send, n_recv = sum(send_splits), sum(recv_splits)
-        aq, as_ = gather_rows(xq, xs, sor, n_send, k)
+        aq, as_ = ops.gather_rows(xq, xs, sor, n_send, k)
         rq = torch.empty((n_recv, H), dtype=torch.int8, device=x.device)
         rs = torch.empty((n_recv,), dtype=torch.float32, device=x.device)
         dist.all_to_all_single(rq, aq, recv_splits, send_splits, group=self.group)
         dist.all_to_all_single(rs, as_, recv_splits, send_splits, group=self.group)
         exp, off, cnt = segments_from_counts(recv_counts)
         L = self.local
-        h = grouped_gemm(rq, rs, L.w_gu, L.s_gu, exp, off, cnt, out_dtype=x.dtype)
-        hq, hs = act_and_mul_quant(h, self.act)
-        y = grouped_gemm(hq, hs, L.w_dn, L.s_dn, exp, off, cnt, out_dtype=x.dtype)
+        h = ops.grouped_gemm(rq, rs, L.w_gu, L.s_gu, exp, off, cnt, out_dtype=x.dtype)
+        hq, hs = ops.act_and_mul_quant(h, self.act)
+        y = ops.grouped_gemm(hq, hs, L.w_dn, L.s_dn, exp, off, cnt, out_dtype=x.dtype)
         back = torch.empty((n_send, H), dtype=x.dtype, device=x.device)
         dist.all_to_all_single(back, y, send_splits, recv_splits, group=self.group)
-        return combine(back, ros, topw)
+        return ops.combine(back, ros, topw)
 
 
 def shard_rows(qt: QTensor, world: int, rank: int) -> QTensor:
@@ -119,19 +135,20 @@ def shard_rows(qt: QTensor, world: int, rank: int) -> QTensor:
 class ColumnParallelLinearW8A8:
     """y = x W^T with W's output channels sharded over the ranks of `group`."""
 
-    def __init__(self, shard: QTensor, group=None):
+    def __init__(self, shard: QTensor, group=None, matmul=linear):
         self.shard = shard
         self.group = group
         self.world = dist.get_world_size(group)
+        self.matmul = matmul  # fni8.linear (the sm_100a kernels) unless a test swaps it
 
     def __call__(self, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
         K = x.shape[-1]
         x2 = x.reshape(-1, K)
         M = x2.shape[0]
         n = self.shard.data.shape[0]
-        y = linear(x2, self.shard, bias)
+        y = self.matmul(x2, self.shard, bias)
         if self.world == 1:
             return y.reshape(*x.shape[:-1], n)
-        parts = torch.empty((self.world, M, n), dtype=y.dtype, device=y.device)
-        dist.all_gather_into_tensor(parts, y, group=self.group)
-        return parts.permute(1, 0, 2).reshape(*x.shape[:-1], self.world * n)
+        parts = torch.empty((self.world * M, n), dtype=y.dtype, device=y.device)
+        dist.all_gather_into_tensor(parts, y.contiguous(), group=self.group)
+        return parts.view(self.world, M, n).permute(1, 0, 2).reshape(*x.shape[:-1], self.world * n)

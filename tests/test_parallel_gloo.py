@@ -1,0 +1,163 @@
+"""Multi-process logic of the multi-GPU forms, on CPU gloo ranks (world_size 2).
+
+The expert-parallel layer (fni8/parallel.py) owns the exchange: per-expert counts,
+split sizes, int8 row dispatch, (source rank, local expert) segments and the combine
+return trip. Here its compute steps are the CPU oracle's, so two gloo ranks must
+reproduce the single-process oracle MoE bit for bit; the column-parallel linear must
+reassemble the unsharded output exactly. No GPU is involved.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+class OracleOps:
+    """The compute steps of ExpertParallelMoE, restated on CPU with the oracle."""
+
+    @staticmethod
+    def quantize_rows(x):
+        from oracle import w8a8_oracle as O
+
+        return O.quantize_rows(x)
+
+    @staticmethod
+    def plan(topi, E):
+        from oracle import w8a8_oracle as O
+
+        c, o, r, s = O.moe_plan(topi, E)
+        return c.int(), o.int(), r.int(), s.int()
+
+    @staticmethod
+    def gather_rows(q, s, slot_of_row, rows, k):
+        t = slot_of_row[:rows].long() // k
+        return q[t], s[t]
+
+    @staticmethod
+    def grouped_gemm(a, a_scale, w, w_scale, exp, off, cnt, out_dtype=torch.float16):
+        from oracle import w8a8_oracle as O
+
+        out = torch.zeros((a.shape[0], w.shape[1]), dtype=out_dtype)
+        for e, o, c in zip(exp.tolist(), off.tolist(), cnt.tolist()):
+            if c:
+                out[o:o + c] = O.dequant(O.int_mm_fast(a[o:o + c], w[e]), a_scale[o:o + c], w_scale[e],
+                                         out_dtype=out_dtype)
+        return out
+
+    @staticmethod
+    def act_and_mul_quant(h, act):
+        from oracle import w8a8_oracle as O
+
+        return O.quantize_rows(O.act_and_mul(h, act))
+
+    @staticmethod
+    def combine(y, row_of_slot, topw):
+        T, k = topw.shape
+        acc = torch.zeros((T, y.shape[1]), dtype=torch.float32)
+        for j in range(k):
+            r = row_of_slot.view(T, k)[:, j].long()
+            acc = acc + topw[:, j:j + 1].float() * y[r].float()
+        return acc.to(y.dtype)
+
+
+def _weights(E, H, I):
+    from oracle import w8a8_oracle as O
+
+    g = torch.Generator().manual_seed(5)
+    gu = [O.quantize_weight_rowwise(0.05 * torch.randn(2 * I, H, generator=g)) for _ in range(E)]
+    dn = [O.quantize_weight_rowwise(0.05 * torch.randn(H, I, generator=g)) for _ in range(E)]
+    return (torch.stack([q for q, _ in gu]), torch.stack([s for _, s in gu]),
+            torch.stack([q for q, _ in dn]), torch.stack([s for _, s in dn]))
+
+
+def _ep_worker(rank, world, port, errq):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from fni8.moe import ExpertStack
+        from fni8.parallel import ExpertParallelMoE, expert_shard
+        from oracle import w8a8_oracle as O
+
+        E, k, H, I, T = 8, 2, 64, 32, 24 + 8 * rank  # ragged: ranks hold different token counts
+        w_gu, s_gu, w_dn, s_dn = _weights(E, H, I)
+        lo, hi = expert_shard(E, world, rank)
+        ep = ExpertParallelMoE(ExpertStack(w_gu[lo:hi], s_gu[lo:hi], w_dn[lo:hi], s_dn[lo:hi]), E, ops=OracleOps)
+        g = torch.Generator().manual_seed(100 + rank)
+        x = torch.randn(T, H, generator=g).half()
+        bias = torch.zeros(E)
+        bias[0] = 3.0  # skew: expert 0 (rank 0) is popular
+        topi, topw = O.moe_route(torch.randn(T, E, generator=g) + bias, k)
+        got = ep(x, topi.int(), topw.float())
+        ref = O.moe_experts_w8a8(x, topi, topw.float(), w_gu, s_gu, w_dn, s_dn, exact=False)
+        assert torch.equal(got, ref), (got.float() - ref.float()).abs().max()
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report to the parent, which fails the test
+        errq.put(f"rank {rank}: {e!r}")
+        raise
+
+
+def _cp_worker(rank, world, port, errq):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from fni8 import QTensor
+        from fni8.parallel import ColumnParallelLinearW8A8, shard_rows
+        from oracle import w8a8_oracle as O
+
+        M, K, N = 7, 64, 96
+        g = torch.Generator().manual_seed(3)
+        wq, ws = O.quantize_weight_rowwise(0.02 * torch.randn(N, K, generator=g))
+        x = torch.randn(M, K, generator=g).half()
+        full = QTensor(wq, ws)
+
+        def mm(x2, qt, bias):
+            return O.linear_w8a8(x2, qt.data, qt.scale, bias=bias, exact=False)
+
+        cp = ColumnParallelLinearW8A8(shard_rows(full, world, rank), matmul=mm)
+        got = cp(x)
+        assert torch.equal(got, O.linear_w8a8(x, wq, ws, exact=False))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        errq.put(f"rank {rank}: {e!r}")
+        raise
+
+
+@pytest.mark.parametrize("worker", [_ep_worker, _cp_worker], ids=["expert_parallel", "column_parallel"])
+def test_two_gloo_ranks(worker):
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=worker, args=(r, 2, port, errq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            errs.append("rank timed out")
+    assert not errs and all(p.exitcode == 0 for p in procs), errs
+
+
+def test_exchange_helpers_single_rank():
+    from fni8.parallel import expert_shard, segments_from_counts
+
+    assert expert_shard(128, 8, 3) == (48, 64)
+    with pytest.raises(ValueError):
+        expert_shard(10, 4, 0)
+    exp, off, cnt = segments_from_counts(torch.tensor([[2, 0, 5], [1, 3, 0]]))
+    assert exp.tolist() == [0, 1, 2, 0, 1, 2] and off.tolist() == [0, 2, 2, 7, 8, 11] and cnt.tolist() == [2, 0, 5, 1, 3, 0]

@@ -66,7 +66,11 @@ struct Cfg {
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SEG_BYTES = (kMaxSeg + 1 + 3 * kMaxSeg) * 4;
-  static constexpr int SMEM = 1024 + STAGES * STAGE + BAR_BYTES + SEG_BYTES;
+  // per epilogue warp, two 32 x 32 16-bit output staging buffers for the TMA store
+  static constexpr int STG_BUF = 32 * 32 * 2;
+  static constexpr int STG_BYTES = 4 * 2 * STG_BUF;
+  static constexpr int STG_OFF = (STAGES * STAGE + BAR_BYTES + SEG_BYTES + 1023) / 1024 * 1024;  // swizzle-aligned
+  static constexpr int SMEM = 1024 + STG_OFF + STG_BYTES + 2 * BN * 4;  // + per-tile column scales, bias
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
   static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
 };
@@ -111,33 +115,23 @@ __device__ __forceinline__ TileCoord decode_tile(int t, int M, int m_tiles, int 
   return tc;
 }
 
+// Per-thread stores of one 32-column chunk of one output row (the path for residual adds,
+// rows cut by a segment end and unaligned outputs). ws/bs: the chunk's column scales and
+// bias (fp32, from shared memory).
 template <typename T>
 __device__ __forceinline__ void store_chunk(const Epi& epi, const uint32_t (&r)[32], int64_t row, int n0, int N,
-                                            float a_s, const float* wsc, bool vec_ok) {
+                                            float a_s, const float* ws, const float* bs, bool vec_ok) {
   T* out = static_cast<T*>(epi.out) + row * static_cast<int64_t>(N);
-  const T* bias = static_cast<const T*>(epi.bias);
   const T* res = epi.residual ? static_cast<const T*>(epi.residual) + row * static_cast<int64_t>(N) : nullptr;
+  const bool has_bias = epi.bias != nullptr;
   if (vec_ok && n0 + 32 <= N) {
-    float ws[32];
-#pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      const float4 f = __ldg(reinterpret_cast<const float4*>(wsc + n0 + j));
-      ws[j] = f.x;
-      ws[j + 1] = f.y;
-      ws[j + 2] = f.z;
-      ws[j + 3] = f.w;
-    }
 #pragma unroll
     for (int j8 = 0; j8 < 32; j8 += 8) {
       float v[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < 8; ++j) {
         v[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j8 + j])), a_s), ws[j8 + j]);
-      if (bias != nullptr) {
-        const uint4 b = __ldg(reinterpret_cast<const uint4*>(bias + n0 + j8));
-        const T* bb = reinterpret_cast<const T*>(&b);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], to_f32<T>(bb[j]));
+        if (has_bias) v[j] = __fadd_rn(v[j], bs[j8 + j]);
       }
       if (res != nullptr) {
         const uint4 b = __ldg(reinterpret_cast<const uint4*>(res + n0 + j8));
@@ -156,8 +150,8 @@ __device__ __forceinline__ void store_chunk(const Epi& epi, const uint32_t (&r)[
     for (int j = 0; j < 32; ++j) {
       const int n = n0 + j;
       if (n < N) {
-        float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), a_s), __ldg(wsc + n));
-        if (bias != nullptr) v = __fadd_rn(v, to_f32<T>(bias[n]));
+        float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), a_s), ws[j]);
+        if (has_bias) v = __fadd_rn(v, bs[j]);
         if (res != nullptr) v = __fadd_rn(v, to_f32<T>(res[n]));
         out[n] = from_f32<T>(v);
       }
@@ -181,8 +175,9 @@ __device__ __forceinline__ void store_chunk_i32(const Epi& epi, const uint32_t (
 
 template <int BN, bool GROUPED>
 __global__ void __launch_bounds__(kThreads, 1)
-    w8a8_tile_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Epi epi,
-                     Groups grp, int M, int N, int K, int vec_ok) {
+    w8a8_tile_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmOut, Epi epi, Groups grp, int M, int N, int K, int vec_ok,
+                     int tma_store) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -197,6 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   int32_t* soff = prefix + kMaxSeg + 1;
   int32_t* scnt = soff + kMaxSeg;
   int32_t* sexp = scnt + kMaxSeg;
+  uint8_t* stg = smem + C::STG_OFF;  // 1024-aligned: the 64B-swizzle pattern follows address bits
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -378,32 +374,101 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lanes [32q, 32q+32) are reachable from this warp
+    // 4 warps; warp q reads TMEM lanes [32q, 32q+32) = rows of the tile, one per thread.
+    // Per tile the column scales (and bias) are staged in shared memory; their loads are
+    // issued before the accumulator wait so they overlap the MMA. 16-bit outputs leave
+    // through 64B-swizzled 32 x 32 staging buffers and TMA stores.
+    const int q = warp & 3;
     const int row_local = q * 32 + lane;
+    const int et = threadIdx.x - 64;  // 0..127 across the epilogue warps
+    float* s_ws = reinterpret_cast<float*>(stg + C::STG_BYTES);
+    float* s_bias = s_ws + BN;
     int acc = 0;
     uint32_t aph = 0;
+    int sb = 0;  // staging buffer of this warp used next
+    if (tma_store && lane == 0) tma_prefetch_desc(&tmOut);
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const TileCoord tc = decode_tile<GROUPED>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
+      const bool valid = row_local < tc.rows_valid;
+      const int64_t row = static_cast<int64_t>(tc.row0) + row_local;
+      const int nb0 = tc.n_blk * BN;
+      const float* wsc = epi.w_scale + static_cast<int64_t>(tc.expert) * N;
+      float wreg[BN / 128], breg[BN / 128];
+      float a_s = 0.0f;
+      if (epi.mode != kOutI32) {
+#pragma unroll
+        for (int i = 0; i < BN / 128; ++i) {
+          const int col = nb0 + et + i * 128;
+          wreg[i] = col < N ? __ldg(wsc + col) : 0.0f;
+          breg[i] = 0.0f;
+          if (epi.bias != nullptr && col < N)
+            breg[i] = epi.mode == kOutF16 ? __half2float(static_cast<const __half*>(epi.bias)[col])
+                                          : __bfloat162float(static_cast<const __nv_bfloat16*>(epi.bias)[col]);
+        }
+        if (valid) a_s = __ldg(epi.a_scale + row);
+      }
       int ok = 0;
       if (lane == 0) ok = mbar_wait(&tfull[acc], aph, &g_status, kCodeEpilogue) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
+      if (!named_bar_and(2, 128, ok)) break;  // also: every reader of the previous tile's scales is done
       tc_fence_after();
-      const bool valid = row_local < tc.rows_valid;
-      const int64_t row = static_cast<int64_t>(tc.row0) + row_local;
-      const float a_s = (valid && epi.mode != kOutI32) ? __ldg(epi.a_scale + row) : 0.0f;
-      const float* wsc = epi.w_scale + static_cast<int64_t>(tc.expert) * N;
+      if (epi.mode != kOutI32) {
+#pragma unroll
+        for (int i = 0; i < BN / 128; ++i) {
+          s_ws[et + i * 128] = wreg[i];
+          s_bias[et + i * 128] = breg[i];
+        }
+        named_bar_sync(2, 128);
+      }
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      // TMA store of whole 32-row slabs; a slab cut by a segment end (grouped) or any
+      // residual add takes the per-thread path
+      const bool slab_tma = tma_store && epi.residual == nullptr &&
+                            (!GROUPED || tc.rows_valid - q * 32 >= 32) && q * 32 < tc.rows_valid;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
         tmem_ld32(tbase + static_cast<uint32_t>(c), r);
         tmem_ld_wait();
-        const int n0 = tc.n_blk * BN + c;
-        if (valid && n0 < N) {
-          if (epi.mode == kOutF16) store_chunk<__half>(epi, r, row, n0, N, a_s, wsc, vec_ok != 0);
-          else if (epi.mode == kOutBF16) store_chunk<__nv_bfloat16>(epi, r, row, n0, N, a_s, wsc, vec_ok != 0);
-          else store_chunk_i32(epi, r, row, n0, N, vec_ok != 0);
+        const int n0 = nb0 + c;
+        if (n0 >= N) continue;
+        if (slab_tma) {
+          uint8_t* buf = stg + (q * 2 + sb) * C::STG_BUF;
+          if (lane == 0) bulk_wait_group_read<1>();  // the store issued from this buffer 2 chunks ago
+          __syncwarp();
+#pragma unroll
+          for (int j8 = 0; j8 < 4; ++j8) {  // 8 outputs = one 16-byte chunk of this row
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int col = c + j8 * 8 + j;
+              v[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j8 * 8 + j])), a_s), s_ws[col]);
+              if (epi.bias != nullptr) v[j] = __fadd_rn(v[j], s_bias[col]);
+            }
+            uint4 o;
+            if (epi.mode == kOutF16) {
+              __half* oo = reinterpret_cast<__half*>(&o);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) oo[j] = __float2half_rn(v[j]);
+            } else {
+              __nv_bfloat16* oo = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) oo[j] = __float2bfloat16_rn(v[j]);
+            }
+            // 64-byte swizzle of the store map: 16-byte chunk index ^= (row >> 1) & 3
+            *reinterpret_cast<uint4*>(buf + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = o;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmOut, buf, n0, tc.row0 + q * 32);
+            bulk_commit_group();
+          }
+          sb ^= 1;
+        } else if (valid) {
+          if (epi.mode == kOutI32) store_chunk_i32(epi, r, row, n0, N, vec_ok != 0);
+          else if (epi.mode == kOutF16) store_chunk<__half>(epi, r, row, n0, N, a_s, s_ws + c, s_bias + c, vec_ok != 0);
+          else store_chunk<__nv_bfloat16>(epi, r, row, n0, N, a_s, s_ws + c, s_bias + c, vec_ok != 0);
         }
       }
       tc_fence_before();
@@ -412,6 +477,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc ^= 1;
       if (acc == 0) aph ^= 1u;
     }
+    if (tma_store && lane == 0) bulk_wait_group<0>();  // stores complete before the CTA exits
+    __syncwarp();
   }
 
   __syncthreads();
@@ -422,8 +489,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int BN, bool GROUPED>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Epi& epi, const Groups& grp, int M, int N, int K,
-           int grid, bool vec_ok, cudaStream_t st) {
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, bool tma_store, const Epi& epi,
+           const Groups& grp, int M, int N, int K, int grid, bool vec_ok, cudaStream_t st) {
   using C = Cfg<BN>;
   auto kern = w8a8_tile_kernel<BN, GROUPED>;
   static bool configured[fni8h::kMaxDevices] = {};  // the attribute is set per device
@@ -448,7 +515,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const Epi& epi, const G
   attr[0].val.programmaticStreamSerializationAllowed = fni8h::pdl_enabled();
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, epi, grp, M, N, K, vec_ok ? 1 : 0);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, to, epi, grp, M, N, K, vec_ok ? 1 : 0, tma_store ? 1 : 0);
   if (e != cudaSuccess) return fni8h::cuda_status(e, "launch tile gemm");
   return FNI8_OK;
 }
@@ -474,6 +541,16 @@ int tile_status_read_and_clear(int* code) {
   return FNI8_OK;
 }
 
+// Tensor map for the TMA-store epilogue: 16-bit outputs whose rows are 16-byte aligned.
+// Returns false (per-thread stores) otherwise; no error is raised for that.
+static bool out_tma_map(CUtensorMap* map, void* out, int out_mode, int64_t rows, int64_t N) {
+  if (out_mode == tile::kOutI32 || (N * 2) % 16 != 0 || (reinterpret_cast<uintptr_t>(out) & 15u) != 0) return false;
+  if (encode_tmap_2d_16_sw(map, out, out_mode == tile::kOutBF16, (uint64_t)N, (uint64_t)rows, (uint64_t)N * 2, 32, 32,
+                           true) != FNI8_OK)
+    return false;
+  return true;
+}
+
 int tile_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
               const void* residual, void* out, int out_mode, int64_t M, int64_t N, int64_t K, int bn,
               cudaStream_t st) {
@@ -493,9 +570,11 @@ int tile_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const floa
   const bool vec_ok = ((N * (int64_t)esz) % 16 == 0) && (((uintptr_t)out & 15u) == 0) &&
                       (((uintptr_t)w_scale & 15u) == 0) && (bias == nullptr || ((uintptr_t)bias & 15u) == 0) &&
                       (residual == nullptr || ((uintptr_t)residual & 15u) == 0);
+  CUtensorMap to;
+  const bool tma_store = out_tma_map(&to, out, out_mode, M, N);
   if (bn == 256)
-    return tile::launch<256, false>(ta, tb, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
-  return tile::launch<128, false>(ta, tb, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
+    return tile::launch<256, false>(ta, tb, to, tma_store, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
+  return tile::launch<128, false>(ta, tb, to, tma_store, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
 }
 
 int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w, const float* w_scale,
@@ -514,9 +593,11 @@ int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const in
   const size_t esz = out_mode == tile::kOutI32 ? 4 : 2;
   const bool vec_ok = ((N * (int64_t)esz) % 16 == 0) && (((uintptr_t)out & 15u) == 0) &&
                       (((uintptr_t)w_scale & 15u) == 0) && ((N % 4) == 0);
+  CUtensorMap to;
+  const bool tma_store = out_tma_map(&to, out, out_mode, R, N);
   if (bn == 256)
-    return tile::launch<256, true>(ta, tb, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
-  return tile::launch<128, true>(ta, tb, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
+    return tile::launch<256, true>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
+  return tile::launch<128, true>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
 }
 
 }  // namespace fni8h

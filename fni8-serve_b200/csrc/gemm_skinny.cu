@@ -1,7 +1,7 @@
 // Fused decode linear: fni8.linear(x, qt) for M <= 32 tokens in ONE launch.
 //
 //   out[m, n] = dtype((float(sum_k q[m,k] * w[n,k]) * s[m]) * w_scale[n] (+ bias[n]))
-//   s[m] = absmax(x[m, :]) / 127,  q = round_half_even(x / s[m])       (per-token int8)
+//   s[m] = absmax(x[m, :]) / 127,  q = round_half_even(x * (127 / absmax))   (per-token int8)
 //
 // At decode sizes a linear is a chain of short latencies (launch, first HBM round trip,
 // cross-CTA reduction), so the activation quantisation and the split-K reduction live in
@@ -86,9 +86,8 @@ __device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   for (int i = 0; i < 8; ++i) f[i] = to_f32<T>(h[i]);
 }
 
-__device__ __forceinline__ int8_t q8(float v, float s) {
-  if (!(s > 0.0f)) return 0;
-  float q = rintf(__fdiv_rn(v, s));
+__device__ __forceinline__ int8_t q8(float v, float inv) {  // inv = 127 / absmax (0 for a zero row)
+  float q = rintf(__fmul_rn(v, inv));
   q = fminf(fmaxf(q, -127.0f), 127.0f);
   return static_cast<int8_t>(static_cast<int>(q));
 }
@@ -113,6 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   int* s_pmax = reinterpret_cast<int*>(tmem_slot + 4);  // [32] absmax bits of this CTA's K slice
   float* s_scale = reinterpret_cast<float*>(s_pmax + 32);
+  float* s_inv = s_scale + 32;
   int32_t* part = reinterpret_cast<int32_t*>(smem);  // [128][PART_LD] partial sums, after the mainloop
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -257,7 +257,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (2) publish the slice maxima to every CTA of the cluster, then combine all slices
     bool ok = true;
     if (full_row) {
-      if (ct < NT) s_scale[ct] = __fdiv_rn(__int_as_float(s_pmax[ct]), 127.0f);
+      if (ct < NT) {
+        const float mx = __int_as_float(s_pmax[ct]);
+        s_scale[ct] = __fdiv_rn(mx, 127.0f);
+        s_inv[ct] = mx > 0.0f ? __fdiv_rn(127.0f, mx) : 0.0f;
+      }
     } else {
       if (ct == 0)
         for (uint32_t p = 0; p < S; ++p) mbar_arrive_cluster(mapa_shared(smem_u32(pmax_bar), p));
@@ -267,6 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (uint32_t p = 0; p < S; ++p)
           mx = max(mx, static_cast<int>(ld_dsmem_u32(mapa_shared(smem_u32(&s_pmax[ct]), p))));
         s_scale[ct] = __fdiv_rn(__int_as_float(mx), 127.0f);
+        s_inv[ct] = __int_as_float(mx) > 0.0f ? __fdiv_rn(127.0f, __int_as_float(mx)) : 0.0f;
       }
     }
     named_bar_sync(1, 128);
@@ -304,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float f[16];
           unpack8<T>(raw[u][0], f);
           unpack8<T>(raw[u][1], f + 8);
-          const float s = s_scale[r];
+          const float s = s_inv[r];
           uint32_t w4[4];
 #pragma unroll
           for (int q = 0; q < 4; ++q)

@@ -94,19 +94,22 @@ __device__ __forceinline__ float block_reduce_sum(float v, float* red) {
   return r;
 }
 
+// scale = absmax / 127 is what the GEMM epilogue multiplies with; the codes are
+// round_half_even(x * (127 / absmax)) — one reciprocal per row instead of a division per
+// element (measured: the per-element IEEE division halved the quantiser's throughput).
 __device__ __forceinline__ float quant_scale(float amax) { return __fdiv_rn(amax, 127.0f); }
-__device__ __forceinline__ int8_t quant_one(float v, float s) {
-  if (!(s > 0.0f)) return 0;
-  float q = rintf(__fdiv_rn(v, s));
+__device__ __forceinline__ float quant_inv(float amax) { return amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f; }
+__device__ __forceinline__ int8_t quant_one(float v, float inv) {
+  float q = rintf(__fmul_rn(v, inv));
   q = fminf(fmaxf(q, -127.0f), 127.0f);
   return static_cast<int8_t>(static_cast<int>(q));
 }
-__device__ __forceinline__ uint2 quant8(const float (&f)[8], float s) {
+__device__ __forceinline__ uint2 quant8(const float (&f)[8], float inv) {
   uint32_t lo = 0, hi = 0;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) lo |= (static_cast<uint32_t>(static_cast<uint8_t>(quant_one(f[i], s)))) << (8 * i);
+  for (int i = 0; i < 4; ++i) lo |= (static_cast<uint32_t>(static_cast<uint8_t>(quant_one(f[i], inv)))) << (8 * i);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) hi |= (static_cast<uint32_t>(static_cast<uint8_t>(quant_one(f[4 + i], s)))) << (8 * i);
+  for (int i = 0; i < 4; ++i) hi |= (static_cast<uint32_t>(static_cast<uint8_t>(quant_one(f[4 + i], inv)))) << (8 * i);
   return make_uint2(lo, hi);
 }
 
@@ -147,7 +150,7 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_vec(const T* __restric
       }
     }
     amax = block_reduce_max(amax, red);
-    const float s = quant_scale(amax);
+    const float s = quant_scale(amax), inv = quant_inv(amax);
     uint2* qr = reinterpret_cast<uint2*>(q + row * K);
 #pragma unroll
     for (int i = 0; i < MAXC; ++i) {
@@ -155,7 +158,7 @@ __global__ void __launch_bounds__(kRowThreads) quant_rows_vec(const T* __restric
       if (c < nch) {
         float f[8];
         Vec8<T>::unpack(raw[i], f);
-        qr[c] = quant8(f, s);
+        qr[c] = quant8(f, inv);
       }
     }
     if (threadIdx.x == 0) scale[row] = s;
@@ -223,7 +226,7 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_vec(const T* __restrict__
     }
     if constexpr (QUANT) {
       amax = block_reduce_max(amax, red);
-      const float s = quant_scale(amax);
+      const float s = quant_scale(amax), inv = quant_inv(amax);
       uint2* qr = reinterpret_cast<uint2*>(q + row * K);
 #pragma unroll
       for (int i = 0; i < MAXC; ++i) {
@@ -231,7 +234,7 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_vec(const T* __restrict__
         if (c < nch) {
           float f[8];
           Vec8<T>::unpack(raw[i], f);
-          qr[c] = quant8(f, s);
+          qr[c] = quant8(f, inv);
         }
       }
       if (threadIdx.x == 0) scale[row] = s;
@@ -271,7 +274,7 @@ __global__ void __launch_bounds__(kRowThreads) act_mul_vec(const T* __restrict__
     }
     if constexpr (QUANT) {
       amax = block_reduce_max(amax, red);
-      const float s = quant_scale(amax);
+      const float s = quant_scale(amax), inv = quant_inv(amax);
       uint2* qr = reinterpret_cast<uint2*>(q + row * I);
 #pragma unroll
       for (int i = 0; i < MAXC; ++i) {
@@ -279,7 +282,7 @@ __global__ void __launch_bounds__(kRowThreads) act_mul_vec(const T* __restrict__
         if (c < nch) {
           float f[8];
           Vec8<T>::unpack(raw[i], f);
-          qr[c] = quant8(f, s);
+          qr[c] = quant8(f, inv);
         }
       }
       if (threadIdx.x == 0) scale[row] = s;
@@ -340,17 +343,154 @@ __global__ void __launch_bounds__(kRowThreads) row_scalar(const T* __restrict__ 
     }
     if constexpr (QUANT) {
       amax = block_reduce_max(amax, red);
-      const float s = quant_scale(amax);
-      for (int k = threadIdx.x; k < K; k += kRowThreads) q[row * K + k] = quant_one(value(k, rinv), s);
+      const float s = quant_scale(amax), inv = quant_inv(amax);
+      for (int k = threadIdx.x; k < K; k += kRowThreads) q[row * K + k] = quant_one(value(k, rinv), inv);
       if (threadIdx.x == 0) scale[row] = s;
     }
   }
 }
 
+// ---------------------------------------------------------------- warp-per-row kernels
+// Rows of up to 32 * 8 * MW (<= 1024) elements: one warp per row, 8 rows per CTA, shuffle-only
+// reductions (no block barriers), so many rows are in flight per SM. Same arithmetic as
+// the CTA-per-row kernels above. OP: 0 quant, 1 rmsnorm, 2 rmsnorm+quant, 3 act_mul,
+// 4 act_mul+quant.
+constexpr int kWarpRows = 8;
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <typename T, int OP, int ACT, int MW>
+__global__ void __launch_bounds__(32 * kWarpRows) row_warp(const T* __restrict__ x, const T* __restrict__ res,
+                                                            const T* __restrict__ w, int64_t M, int K, float eps,
+                                                            int unit_offset, T* __restrict__ out,
+                                                            T* __restrict__ res_out, int8_t* __restrict__ q,
+                                                            float* __restrict__ scale) {
+  constexpr bool NORM = (OP == 1 || OP == 2);
+  constexpr bool ACTM = (OP == 3 || OP == 4);
+  constexpr bool QUANT = (OP == 0 || OP == 2 || OP == 4);
+  pdl_launch_dependents();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int nch = K >> 3;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarpRows;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpRows + (threadIdx.x >> 5); row < M; row += stride) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * (ACTM ? 2 * static_cast<int64_t>(K) : K));
+    uint4 raw[MW];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MW; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nch) {
+        if constexpr (ACTM) {
+          float g[8], u[8];
+          Vec8<T>::unpack(__ldg(xr + c), g);
+          Vec8<T>::unpack(__ldg(xr + nch + c), u);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) g[j] = round_trip<T>(__fmul_rn(round_trip<T>(act_fn<ACT>(g[j])), u[j]));
+          raw[i] = Vec8<T>::pack(g);
+        } else if constexpr (NORM) {
+          raw[i] = __ldg(xr + c);
+          if (res != nullptr) {
+            float a[8], b[8];
+            Vec8<T>::unpack(raw[i], a);
+            Vec8<T>::unpack(__ldg(reinterpret_cast<const uint4*>(res + row * K) + c), b);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) a[j] = __fadd_rn(a[j], b[j]);
+            raw[i] = Vec8<T>::pack(a);
+            reinterpret_cast<uint4*>(res_out + row * K)[c] = raw[i];
+          }
+          float f[8];
+          Vec8<T>::unpack(raw[i], f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss = __fadd_rn(ss, __fmul_rn(f[j], f[j]));
+        } else {
+          raw[i] = __ldg(xr + c);
+        }
+      }
+    }
+    if constexpr (NORM) {
+      ss = warp_sum_f(ss);
+      const float rinv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps)));
+#pragma unroll
+      for (int i = 0; i < MW; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nch) {
+          float f[8], g[8];
+          Vec8<T>::unpack(raw[i], f);
+          Vec8<T>::unpack(__ldg(reinterpret_cast<const uint4*>(w) + c), g);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float gj = unit_offset ? __fadd_rn(1.0f, g[j]) : g[j];
+            f[j] = round_trip<T>(__fmul_rn(__fmul_rn(f[j], rinv), gj));
+          }
+          raw[i] = Vec8<T>::pack(f);
+          if (out != nullptr) reinterpret_cast<uint4*>(out + row * K)[c] = raw[i];
+        }
+      }
+    }
+    if constexpr (ACTM && !QUANT) {
+#pragma unroll
+      for (int i = 0; i < MW; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nch) reinterpret_cast<uint4*>(out + row * K)[c] = raw[i];
+      }
+    }
+    if constexpr (QUANT) {
+      float amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < MW; ++i) {
+        if (lane + 32 * i < nch) {
+          float f[8];
+          Vec8<T>::unpack(raw[i], f);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+        }
+      }
+      const float amax_w = warp_max_f(amax);
+      const float s = quant_scale(amax_w), inv = quant_inv(amax_w);
+      uint2* qr = reinterpret_cast<uint2*>(q + row * K);
+#pragma unroll
+      for (int i = 0; i < MW; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nch) {
+          float f[8];
+          Vec8<T>::unpack(raw[i], f);
+          qr[c] = quant8(f, inv);
+        }
+      }
+      if (lane == 0) scale[row] = s;
+    }
+  }
+}
+
+// Launch the warp-per-row kernel for short rows (K <= 1024); returns false otherwise.
+template <typename T, int OP, int ACT>
+bool launch_row_warp(const T* x, const T* res, const T* w, int64_t M, int K, float eps, int uo, T* out, T* res_out,
+                     int8_t* q, float* s, cudaStream_t st) {
+  const int nch = K / 8;
+  const int64_t ctas_needed = (M + kWarpRows - 1) / kWarpRows;
+  const int grid = static_cast<int>(ctas_needed < 148LL * 8 ? ctas_needed : 148LL * 8);
+  const dim3 blk(32 * kWarpRows);
+  if (nch <= 32) fni8h::launch_pdl(row_warp<T, OP, ACT, 1>, dim3(grid), blk, 0, st, x, res, w, M, K, eps, uo, out, res_out, q, s);
+  else if (nch <= 64) fni8h::launch_pdl(row_warp<T, OP, ACT, 2>, dim3(grid), blk, 0, st, x, res, w, M, K, eps, uo, out, res_out, q, s);
+  else if (nch <= 128) fni8h::launch_pdl(row_warp<T, OP, ACT, 4>, dim3(grid), blk, 0, st, x, res, w, M, K, eps, uo, out, res_out, q, s);
+  else return false;  // longer rows: the CTA-per-row kernels spread a row over 4 warps (measured faster)
+  return true;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int row_grid(int64_t M) {
-  const int64_t cap = 148LL * 16LL;
+int row_grid(int64_t M) {  // one row per CTA up to ~64 CTAs per SM (measured best)
+  const int64_t cap = 148LL * 64LL;
   return static_cast<int>(M < cap ? M : cap);
 }
 
@@ -364,6 +504,11 @@ template <typename T>
 int quant_dispatch(const void* x, int64_t M, int64_t K, int8_t* q, float* s, cudaStream_t st) {
   const int64_t nch = K / 8;
   const bool vec = (K % 8 == 0) && aligned16(x) && aligned16(q) && nch <= 16 * kRowThreads;
+  if (vec && launch_row_warp<T, 0, 0>(static_cast<const T*>(x), nullptr, nullptr, M, (int)K, 0.f, 0, nullptr, nullptr, q,
+                                      s, st)) {
+    FNI8_CHECK_LAUNCH("quantize_rows_i8");
+    return FNI8_OK;
+  }
   if (vec) {
     if (nch <= 2 * kRowThreads) launch_quant_vec<T, 2>(x, M, (int)K, q, s, st);
     else if (nch <= 4 * kRowThreads) launch_quant_vec<T, 4>(x, M, (int)K, q, s, st);
@@ -391,6 +536,10 @@ int norm_dispatch(const void* x, const void* res, const void* w, int64_t M, int6
   T* oo = static_cast<T*>(out);
   T* ro = static_cast<T*>(res_out);
   const int g = row_grid(M);
+  if (vec && launch_row_warp<T, QUANT ? 2 : 1, 0>(xx, rr, ww, M, (int)K, eps, uo, oo, ro, q, s, st)) {
+    FNI8_CHECK_LAUNCH(QUANT ? "rmsnorm_quant_i8" : "rmsnorm");
+    return FNI8_OK;
+  }
   if (vec) {
     if (nch <= 2 * kRowThreads)
       fni8h::launch_pdl(rmsnorm_vec<T, 2, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, rr, ww, M, (int)K, eps, uo, oo, ro, q, s);
@@ -416,6 +565,11 @@ int act_dispatch(const void* x, int64_t M, int64_t I, void* out, int8_t* q, floa
   const T* xx = static_cast<const T*>(x);
   T* oo = static_cast<T*>(out);
   const int g = row_grid(M);
+  if (vec && launch_row_warp<T, QUANT ? 4 : 3, ACT>(xx, nullptr, nullptr, M, (int)I, 0.f, 0, QUANT ? nullptr : oo,
+                                                    nullptr, q, s, st)) {
+    FNI8_CHECK_LAUNCH(QUANT ? "act_and_mul_quant_i8" : "act_and_mul");
+    return FNI8_OK;
+  }
   if (vec) {
     if (nch <= 2 * kRowThreads) fni8h::launch_pdl(act_mul_vec<T, 2, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s);
     else if (nch <= 4 * kRowThreads)

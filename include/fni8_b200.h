@@ -17,8 +17,8 @@
  *  - Activations: dtype FNI8_F16 or FNI8_BF16. Weights: int8 [N, K] (out_features x
  *    in_features, K contiguous) with one fp32 scale per output row (`per_row_i8`).
  *  - Per-token activation quantisation: scale[m] = absmax(x[m, :]) / 127 (fp32),
- *    q = round_half_even(x / scale) clamped to [-127, 127]; an all-zero row gets
- *    scale 0 and q = 0.
+ *    q = round_half_even(x * (127 / absmax)) clamped to [-127, 127] (one reciprocal
+ *    per row, fp32); an all-zero row gets scale 0 and q = 0.
  *  - Dequant epilogue (fp32, evaluated left to right, no fused multiply-add):
  *    y = (float(acc) * a_scale[m]) * w_scale[n] (+ bias[n]) (+ residual[m, n]),
  *    rounded once to the output dtype.

@@ -706,6 +706,16 @@ def cpu_baseline_sample(config, seconds=10.0):
             "kind": "port", "sample": f"{n} steps of {sample}"}
 
 
+def json_channel():
+    """The JSON line goes to the original stdout; everything else written to fd 1 for the
+    rest of the run (NCCL's version banner, library notices) is sent to stderr, so rank 0's
+    stdout carries exactly one line."""
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    return os.fdopen(saved, "w")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -717,11 +727,12 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()
+    out = json_channel()
 
     if args.impl == "reference":
         line = reference_arm(args, world, rank)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            print(json.dumps(line), file=out, flush=True)
         return 0
 
     torch.cuda.set_device(local)
@@ -734,7 +745,7 @@ def main():
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample(args.config)
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=out, flush=True)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

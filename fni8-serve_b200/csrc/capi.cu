@@ -125,21 +125,45 @@ static int check_gemm(const int8_t* a, const int8_t* w, const void* out, int64_t
   return FNI8_OK;
 }
 
-// Largest M the AUTO choice sends to the stream-K kernel (tuning knob for measurements).
+// Largest M the AUTO choice sends to the stream-K kernel: none by default, the split-K
+// kernel measured faster at every decode size on B200 (FNI8_STREAM_AUTO_MAX_M overrides).
 static int64_t stream_auto_max_m() {
   static int64_t m = [] {
     const char* e = getenv("FNI8_STREAM_AUTO_MAX_M");
-    const long v = e ? atol(e) : 16;
+    const long v = e ? atol(e) : 0;
     return (int64_t)(v < 0 ? 0 : (v > kStreamMaxM ? kStreamMaxM : v));
   }();
   return m;
 }
 
+// Largest M the AUTO choice sends to the split-K kernel: measured on B200, it beats the
+// tile kernel up to 128 tokens (FNI8_SPLITK_AUTO_MAX_M overrides it for measurements).
+static int64_t splitk_auto_max_m() {
+  static int64_t m = [] {
+    const char* e = getenv("FNI8_SPLITK_AUTO_MAX_M");
+    const long v = e ? atol(e) : 128;
+    return (int64_t)(v < 0 ? 0 : (v > kSplitkMaxM ? kSplitkMaxM : v));
+  }();
+  return m;
+}
+
 static int pick_path(int path, int64_t M, size_t ws_bytes, int64_t N, int64_t K) {
-  if (path == FNI8_PATH_TILE || path == FNI8_PATH_STREAM) return path;
+  if (path == FNI8_PATH_TILE || path == FNI8_PATH_STREAM || path == FNI8_PATH_SPLITK) return path;
   if (M <= stream_auto_max_m() && ws_bytes >= stream_workspace_bytes(M, N, K)) return FNI8_PATH_STREAM;
-  if (path == FNI8_PATH_FUSED) return FNI8_PATH_TILE;
+  if (M <= splitk_auto_max_m() && splitk_supported(M, N, K) && ws_bytes >= splitk_workspace_bytes(M, N, K))
+    return FNI8_PATH_SPLITK;
   return FNI8_PATH_TILE;
+}
+
+// Explicit GEMM kernel choices of the int8-activation entry points.
+static int check_path(int path, int64_t M) {
+  if (path != FNI8_PATH_AUTO && path != FNI8_PATH_TILE && path != FNI8_PATH_STREAM && path != FNI8_PATH_SPLITK)
+    return fail(FNI8_ERR_INVALID, "unknown path %d", path);
+  if (path == FNI8_PATH_STREAM && M > kStreamMaxM)
+    return fail(FNI8_ERR_UNSUPPORTED, "stream path takes M <= %lld", (long long)kStreamMaxM);
+  if (path == FNI8_PATH_SPLITK && M > kSplitkMaxM)
+    return fail(FNI8_ERR_UNSUPPORTED, "split-K path takes M <= %lld", (long long)kSplitkMaxM);
+  return FNI8_OK;
 }
 
 static int pick_bn(int64_t M, int64_t N) {
@@ -153,6 +177,8 @@ static int gemm_any(const int8_t* a, const float* a_scale, const int8_t* w, cons
   const int p = pick_path(path, M, ws_bytes, N, K);
   if (p == FNI8_PATH_STREAM)
     return stream_gemm(a, a_scale, w, w_scale, bias, residual, out, mode, M, N, K, ws, ws_bytes, st);
+  if (p == FNI8_PATH_SPLITK)
+    return splitk_gemm(a, a_scale, w, w_scale, bias, residual, out, mode, M, N, K, ws, ws_bytes, st);
   return tile_gemm(a, a_scale, w, w_scale, bias, residual, out, mode, M, N, K, pick_bn(M, N), st);
 }
 
@@ -181,16 +207,18 @@ extern "C" int fni8_device_status(int* code_out) {
   if (code_out == nullptr) return fail(FNI8_ERR_INVALID, "null code_out");
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_status(e, "cudaDeviceSynchronize");
-  int a = 0, b = 0, c = 0;
+  int a = 0, b = 0, c = 0, d = 0;
   if (int s = tile_status_read_and_clear(&a)) return s;
   if (int s = stream_status_read_and_clear(&b)) return s;
   if (int s = skinny_status_read_and_clear(&c)) return s;
-  *code_out = a != 0 ? a : (b != 0 ? b : c);
+  if (int s = splitk_status_read_and_clear(&d)) return s;
+  *code_out = a != 0 ? a : (b != 0 ? b : (c != 0 ? c : d));
   return *code_out == 0 ? FNI8_OK : fail(FNI8_ERR_DEVICE_TIMEOUT, "device watchdog code 0x%x", *code_out);
 }
 
 extern "C" size_t fni8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  return stream_workspace_bytes(M, N, K);
+  const size_t a = stream_workspace_bytes(M, N, K), b = splitk_workspace_bytes(M, N, K);
+  return a > b ? a : b;
 }
 
 extern "C" int fni8_workspace_init(void* workspace, size_t bytes, void* stream) {
@@ -208,10 +236,8 @@ extern "C" int fni8_gemm_w8a8_ex(const int8_t* a, const float* a_scale, const in
   if (int s = check_gemm(a, w, out, M, N, K)) return s;
   if (out_dtype != FNI8_F16 && out_dtype != FNI8_BF16)
     return fail(FNI8_ERR_INVALID, "out_dtype %d: expected F16 or BF16", out_dtype);
-  if (path < FNI8_PATH_AUTO || path > FNI8_PATH_STREAM) return fail(FNI8_ERR_INVALID, "unknown path %d", path);
+  if (int s = check_path(path, M)) return s;
   if (M > 0 && (a_scale == nullptr || w_scale == nullptr)) return fail(FNI8_ERR_INVALID, "null scale");
-  if (path == FNI8_PATH_STREAM && M > kStreamMaxM)
-    return fail(FNI8_ERR_UNSUPPORTED, "stream path takes M <= %lld", (long long)kStreamMaxM);
   if (M == 0) return FNI8_OK;
   return gemm_any(a, a_scale, w, w_scale, bias, residual, out, out_dtype == FNI8_F16 ? 0 : 1, M, N, K, path,
                   workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
@@ -227,9 +253,7 @@ extern "C" int fni8_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_
 extern "C" int fni8_gemm_w8a8_i32(const int8_t* a, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
                                   int path, void* workspace, size_t workspace_bytes, void* stream) {
   if (int s = check_gemm(a, w, acc, M, N, K)) return s;
-  if (path < FNI8_PATH_AUTO || path > FNI8_PATH_STREAM) return fail(FNI8_ERR_INVALID, "unknown path %d", path);
-  if (path == FNI8_PATH_STREAM && M > kStreamMaxM)
-    return fail(FNI8_ERR_UNSUPPORTED, "stream path takes M <= %lld", (long long)kStreamMaxM);
+  if (int s = check_path(path, M)) return s;
   if (M == 0) return FNI8_OK;
   return gemm_any(a, nullptr, w, nullptr, nullptr, nullptr, acc, 2, M, N, K, path, workspace, workspace_bytes,
                   static_cast<cudaStream_t>(stream));
@@ -239,7 +263,11 @@ extern "C" int fni8_linear_w8a8_ex(const void* x, int dtype, const int8_t* w, co
                                    void* out, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
                                    int path, void* workspace, size_t workspace_bytes, void* stream) {
   if (dtype != FNI8_F16 && dtype != FNI8_BF16) return fail(FNI8_ERR_INVALID, "dtype %d: expected F16 or BF16", dtype);
-  if (path < FNI8_PATH_AUTO || path > FNI8_PATH_FUSED) return fail(FNI8_ERR_INVALID, "unknown path %d", path);
+  if (path < FNI8_PATH_AUTO || path > FNI8_PATH_SPLITK) return fail(FNI8_ERR_INVALID, "unknown path %d", path);
+  if (path == FNI8_PATH_STREAM && M > kStreamMaxM)
+    return fail(FNI8_ERR_UNSUPPORTED, "stream path takes M <= %lld", (long long)kStreamMaxM);
+  if (path == FNI8_PATH_SPLITK && M > kSplitkMaxM)
+    return fail(FNI8_ERR_UNSUPPORTED, "split-K path takes M <= %lld", (long long)kSplitkMaxM);
   if (M < 0 || N <= 0 || K <= 0) return fail(FNI8_ERR_INVALID, "bad linear shape M=%lld N=%lld K=%lld", (long long)M,
                                               (long long)N, (long long)K);
   if (K % 16 != 0) return fail(FNI8_ERR_UNSUPPORTED, "K=%lld must be a multiple of 16", (long long)K);

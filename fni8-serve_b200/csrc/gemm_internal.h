@@ -34,4 +34,14 @@ int skinny_linear(const void* x, bool bf16, const int8_t* w, const float* w_scal
                   int64_t M, int64_t N, int64_t K, cudaStream_t st);
 int skinny_status_read_and_clear(int* code);
 
+// Cluster split-K swap-AB GEMM for decode (gemm_splitk.cu): int8 activations; partial sums
+// of a split K range cross the zero-maintained GEMM workspace and are zeroed again.
+constexpr int64_t kSplitkMaxM = 256;
+bool splitk_supported(int64_t M, int64_t N, int64_t K);
+size_t splitk_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int splitk_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
+                const void* residual, void* out, int out_mode, int64_t M, int64_t N, int64_t K, void* ws,
+                size_t ws_bytes, cudaStream_t st);
+int splitk_status_read_and_clear(int* code);
+
 }  // namespace fni8h

@@ -515,13 +515,14 @@ bool skinny_supported(const void* x, int64_t M, int64_t N, int64_t K) {
          (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && plan_skinny(M, N, K, &p);
 }
 
-// Largest M the AUTO choice of fni8_linear_w8a8 sends to the fused kernel: measured on
-// B200, the fused kernel wins at 1-2 tokens, the quantiser + stream-K GEMM above that
-// (FNI8_SKINNY_AUTO_MAX_M overrides it; 0 disables the fused kernel in AUTO).
+// Largest M the AUTO choice of fni8_linear_w8a8 sends to the fused kernel: none by
+// default — measured on B200, the quantiser + split-K GEMM pair is faster at every decode
+// size, the fused kernel stays available as FNI8_PATH_FUSED (FNI8_SKINNY_AUTO_MAX_M
+// overrides the AUTO choice for measurements).
 int64_t skinny_auto_max_m() {
   static const int64_t m = [] {
     const char* e = getenv("FNI8_SKINNY_AUTO_MAX_M");
-    const long v = e ? atol(e) : 2;
+    const long v = e ? atol(e) : 0;
     return (int64_t)(v < 0 ? 0 : (v > kSkinnyMaxM ? kSkinnyMaxM : v));
   }();
   return m;

@@ -1,0 +1,566 @@
+// Decode W8A8 GEMM for 1..256 tokens: every SM streams weights, partial sums stay on chip.
+//
+//   acc^T[n, m] = sum_k W[n, k] * q[m, k]     (tcgen05.mma kind::i8, M=128 weight rows, N=NT tokens)
+//   out[m, n]   = dtype((float(acc) * a_scale[m]) * w_scale[n] (+ bias[n]) (+ residual[m, n]))
+//
+// At decode sizes the GEMM reads W[N, K] once and is bound by how many SMs keep weight
+// loads in flight, not by the tensor cores. The tile kernel gives one CTA per 128x128
+// output tile (32-48 CTAs for a Qwen3-8B projection), the stream-K kernel reduces its
+// partial tiles with global atomics whose count grows with the token count. Here:
+//
+//  * grid = n_tiles x S CTAs, clustered S (<= 8) at a time. A cluster owns 128 weight
+//    rows; CTA rank r of the cluster the r-th slice of the K range, so n_tiles x S ~ the
+//    SM count for any N and K.
+//  * warp 0 streams (weight, activation) k-blocks of its slice through a TMA ring. Weights
+//    never depend on the previous kernel: the first ring of weight tiles is issued and the
+//    following tiles are pulled into L2 before the grid-dependency wait; the int8
+//    activations (written by the quantiser just before) are loaded after it.
+//  * warp 1 issues the MMAs into one TMEM accumulator of NT columns.
+//  * the S partial accumulators meet in shared memory: per pass of up to 64 token columns
+//    every CTA stages its columns, the cluster synchronises, and CTA r sums the r-th
+//    share of the columns over all S CTAs (ld.shared::cluster) and stores those outputs.
+//    Integer sums are associative, so the result is bit-exact for every split.
+// No workspace and no global atomics. Shared memory stays under half an SM at NT <= 128,
+// so the next kernel's CTAs (PDL) become resident beside this one and start streaming.
+// Every mbarrier wait is bounded (fni8_common.cuh).
+#include "fni8_common.cuh"
+#include "gemm_internal.h"
+
+#include <stdlib.h>
+
+namespace fni8b {
+namespace splitk {
+
+constexpr int kThreads = 192;
+constexpr int BNW = 128;  // weight rows per tile (MMA M)
+constexpr int BK = 128;   // K elements per stage
+constexpr int kMaxStages = 8;
+constexpr int kL2Ahead = 16;  // weight k-blocks per CTA pulled into L2 before the dependency wait
+constexpr int kBarBytes = 256;
+constexpr int kAsBytes = 1024;  // per-token activation scales of up to 256 tokens
+
+static __device__ int g_status;
+
+// Timeline tracing for measurement builds only (-DFNI8_TRACE): per CTA, the globaltimer
+// of the kernel's phases, in launch order.
+#ifdef FNI8_TRACE
+static __device__ unsigned long long g_trace[65536 * 8];
+static __device__ unsigned int g_trace_seq;
+#define FNI8_TRACE_SLOT                                                  \
+  __shared__ unsigned int s_trace_slot;                                  \
+  if (threadIdx.x == 0) s_trace_slot = atomicAdd(&g_trace_seq, 1u) % 65536u;
+#define FNI8_TRACE_AT(i) (g_trace[s_trace_slot * 8u + (i)] = globaltimer_ns())
+#define FNI8_TRACE_VAL(i, v) (g_trace[s_trace_slot * 8u + (i)] = (v))
+#else
+#define FNI8_TRACE_SLOT
+#define FNI8_TRACE_AT(i) ((void)0)
+#define FNI8_TRACE_VAL(i, v) ((void)0)
+#endif
+
+enum : int { kCodeProducer = 0x501, kCodeMma = 0x502, kCodeEpilogue = 0x503, kCodeDrain = 0x504 };
+enum : int { kOutF16 = 0, kOutBF16 = 1, kOutI32 = 2 };
+
+struct Epi {
+  const float* a_scale;  // [M]
+  const float* w_scale;  // [N]
+  const void* bias;      // [N] or null
+  const void* residual;  // [M, N] or null
+  void* out;             // [M, N]
+  int mode;
+  int vec;  // fp16/bf16 out, no residual, rows 16-byte aligned: stage the tile, store 16 B per thread
+};
+
+template <int NT>
+struct Cfg {
+  static constexpr int W_BYTES = BNW * BK;
+  static constexpr int X_BYTES = NT * BK;
+  static constexpr int STAGE = W_BYTES + X_BYTES;
+  static constexpr int TMEM_COLS = NT < 32 ? 32 : NT;
+  static_assert(STAGE % 1024 == 0, "stages keep the 1024-byte alignment of the 128B swizzle");
+};
+
+// out[m0 + j, n] for the CNT accumulator values of weight row n, tokens m0 + j < mlim,
+// straight to global memory (int32 output, residual add, or unaligned rows). s_as holds
+// the per-token scales in shared memory; residual values are all loaded before the first
+// store (a load issued after a store it might alias would wait for that store).
+template <typename T, int CNT>
+__device__ __forceinline__ void emit_batch(const Epi& epi, const uint32_t (&acc)[CNT], int m0, int mlim, int n, int N,
+                                           float wsn, float bn, const float* s_as) {
+  if (epi.mode == kOutI32) {
+    int32_t* o = static_cast<int32_t*>(epi.out);
+#pragma unroll
+    for (int j = 0; j < CNT; ++j)
+      if (m0 + j < mlim) o[static_cast<int64_t>(m0 + j) * N + n] = static_cast<int32_t>(acc[j]);
+    return;
+  }
+  float rs[CNT];
+  if (epi.residual != nullptr) {
+    const T* r = static_cast<const T*>(epi.residual);
+#pragma unroll
+    for (int j = 0; j < CNT; ++j) rs[j] = m0 + j < mlim ? to_f32<T>(r[static_cast<int64_t>(m0 + j) * N + n]) : 0.0f;
+  }
+  T* o = static_cast<T*>(epi.out);
+#pragma unroll
+  for (int j = 0; j < CNT; ++j) {
+    if (m0 + j < mlim) {
+      float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(acc[j])), s_as[m0 + j]), wsn);
+      if (epi.bias != nullptr) v = __fadd_rn(v, bn);
+      if (epi.residual != nullptr) v = __fadd_rn(v, rs[j]);
+      o[static_cast<int64_t>(m0 + j) * N + n] = from_f32<T>(v);
+    }
+  }
+}
+
+// Same values into the shared-memory output tile stage[m - m_base][128] (row n of the
+// weight tile is column trow), for the coalesced copy-out.
+template <typename T, int CNT>
+__device__ __forceinline__ void stage_batch(const Epi& epi, const uint32_t (&acc)[CNT], int m0, int mlim, int m_base,
+                                            T* stage, int trow, float wsn, float bn, const float* s_as) {
+#pragma unroll
+  for (int j = 0; j < CNT; ++j) {
+    if (m0 + j < mlim) {
+      float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(acc[j])), s_as[m0 + j]), wsn);
+      if (epi.bias != nullptr) v = __fadd_rn(v, bn);
+      stage[(m0 + j - m_base) * BNW + trow] = from_f32<T>(v);
+    }
+  }
+}
+
+// Split-K ownership. The token columns that carry real tokens (the first mcols, M rounded
+// up to 4) are dealt out in shares of `share` columns (a multiple of 4) to the S CTAs of
+// the cluster: CTA o sums and stores columns [o*share, (o+1)*share). The other CTAs'
+// partial sums of those columns reach it through their workspace slabs: CTA b writes
+// [NT/4 column groups][128 rows] of 16-byte granules at ws + b * (NT/4) * 128, the weight
+// row innermost, so a warp's 32 stores or loads cover 512 contiguous bytes.
+__host__ __device__ __forceinline__ int split_share(int mcols, int S) { return ((mcols + S - 1) / S + 3) & ~3; }
+
+// Owned columns [own0, own0 + len) of row trow: this CTA's accumulator (TMEM) plus the
+// peers' slab granules, all copied into `land` ([S-1][len/4][128] granules) by one batch
+// of asynchronous copies and zeroed in the workspace again (it stays zero between calls);
+// then staged for the copy-out or stored. 16 columns per batch.
+template <typename T>
+__device__ __forceinline__ void finish_owned(const Epi& epi, uint32_t taddr, uint4* ws, int nt4, int block0,
+                                             uint32_t rank, uint32_t S, int own0, int len, int M, int N, int n,
+                                             int trow, float wsn, float bn, const float* s_as, T* stage, uint4* land) {
+  const int g_own = len >> 2;
+  if (S > 1) {
+    int pi = 0;
+    for (uint32_t p = 0; p < S; ++p) {
+      if (p == rank) continue;
+      uint4* slab = ws + static_cast<int64_t>(block0 + static_cast<int>(p)) * nt4 * BNW + (own0 >> 2) * BNW + trow;
+      for (int g = 0; g < g_own; ++g) cp_async_16(land + (pi * g_own + g) * BNW + trow, slab + g * BNW);
+      ++pi;
+    }
+    cp_async_commit();
+    cp_async_wait_group<0>();
+    for (uint32_t p = 0; p < S; ++p) {
+      if (p == rank) continue;
+      uint4* slab = ws + static_cast<int64_t>(block0 + static_cast<int>(p)) * nt4 * BNW + (own0 >> 2) * BNW + trow;
+      for (int g = 0; g < g_own; ++g) __stcg(slab + g * BNW, make_uint4(0, 0, 0, 0));
+    }
+  }
+  // every lane of the warp runs the tcgen05.ld below (.sync.aligned): rows past N only
+  // skip their stores
+  const bool nvalid = n < N;
+  const int mlim = (own0 + len) < M ? own0 + len : M;
+#pragma unroll 1
+  for (int c0 = 0; c0 < len; c0 += 16) {
+    uint32_t acc[16];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      uint32_t r[4] = {0u, 0u, 0u, 0u};
+      if (c0 + 4 * g < len) tmem_ld4(taddr + static_cast<uint32_t>(own0 + c0 + 4 * g), r);
+      acc[4 * g] = r[0];
+      acc[4 * g + 1] = r[1];
+      acc[4 * g + 2] = r[2];
+      acc[4 * g + 3] = r[3];
+    }
+    tmem_ld_wait();
+    for (int pi = 0; pi + 1 < static_cast<int>(S); ++pi) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        if (c0 + 4 * g < len) {
+          const uint4 v = land[(pi * g_own + (c0 >> 2) + g) * BNW + trow];
+          acc[4 * g] += v.x;
+          acc[4 * g + 1] += v.y;
+          acc[4 * g + 2] += v.z;
+          acc[4 * g + 3] += v.w;
+        }
+      }
+    }
+    if (!nvalid || own0 + c0 >= M) continue;
+    if (stage != nullptr) stage_batch<T, 16>(epi, acc, own0 + c0, mlim, own0, stage, trow, wsn, bn, s_as);
+    else emit_batch<T, 16>(epi, acc, own0 + c0, mlim, n, N, wsn, bn, s_as);
+  }
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 2)
+    w8a8_splitk_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, Epi epi,
+                       int M, int N, int K, int STG, uint4* ws) {
+  using C = Cfg<NT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STG * C::STAGE);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* tfull = empty + kMaxStages;
+  uint64_t* drain = tfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  float* s_as = reinterpret_cast<float*>(smem + STG * C::STAGE + kBarBytes);  // [NT] activation scales
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t S = cluster_nctarank();
+  const int tile = static_cast<int>(blockIdx.x / S);
+  const int kb = (K + BK - 1) / BK;
+  const int kbeg = static_cast<int>(static_cast<int64_t>(rank) * kb / S);
+  const int nk = static_cast<int>(static_cast<int64_t>(rank + 1) * kb / S) - kbeg;
+
+  FNI8_TRACE_SLOT
+  if (threadIdx.x == 0) {
+    FNI8_TRACE_AT(0);
+    FNI8_TRACE_VAL(7, (static_cast<unsigned long long>(N) << 40) | (static_cast<unsigned long long>(K) << 16) |
+                          blockIdx.x);
+    for (int s = 0; s < STG; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(tfull, 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();  // the next kernel may start its prologue; it waits for our completion
+
+  auto stage_at = [&](int s) { return smem + s * C::STAGE; };
+  int okt = 0;  // epilogue warps: the accumulator is complete
+  const int n_row = tile * BNW + (warp & 3) * 32 + lane;  // epilogue warps: weight row of this thread
+  float wsn = 0.0f, bn = 0.0f;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmW);
+      tma_prefetch_desc(&tmX);
+      const int pre = nk < STG ? nk : STG;
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], C::STAGE);
+        tma_load_2d(&tmW, &full[i], stage_at(i), (kbeg + i) * BK, tile * BNW);
+      }
+      const int l2_end = (nk - pre) < kL2Ahead ? nk : pre + kL2Ahead;
+      for (int i = pre; i < l2_end; ++i) tma_prefetch_l2_2d(&tmW, (kbeg + i) * BK, tile * BNW);
+      pdl_wait();  // the activations come from the previous kernel
+      FNI8_TRACE_AT(1);
+      for (int i = 0; i < pre; ++i) tma_load_2d(&tmX, &full[i], stage_at(i) + C::W_BYTES, (kbeg + i) * BK, 0);
+      int stage = pre % STG;
+      uint32_t ph = (pre == STG) ? 1u : 0u;
+      uint32_t armed = 0;
+      int issued = pre;
+      for (int i = pre; i < nk; ++i) {
+        if (!mbar_wait(&empty[stage], ph ^ 1u, &g_status, kCodeProducer)) break;
+        mbar_arrive_expect_tx(&full[stage], C::STAGE);
+        tma_load_2d(&tmW, &full[stage], stage_at(stage), (kbeg + i) * BK, tile * BNW);
+        tma_load_2d(&tmX, &full[stage], stage_at(stage) + C::W_BYTES, (kbeg + i) * BK, 0);
+        armed = (armed & ~(1u << stage)) | (ph << stage);
+        ++issued;
+        if (++stage == STG) {
+          stage = 0;
+          ph ^= 1u;
+        }
+      }
+      // every load still in flight lands before the ring is reused for the partial sums
+      const int pending = issued < STG ? issued : STG;
+      for (int i = 0; i < pending; ++i) {
+        const int s = (stage - 1 - i + 2 * STG) % STG;
+        mbar_wait(&full[s], (armed >> s) & 1u, &g_status, kCodeDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = idesc_i8(BNW, NT);
+      int stage = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int i = 0; i < nk; ++i) {
+        if (!mbar_wait(&full[stage], ph, &g_status, kCodeMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (i == 0) FNI8_TRACE_AT(2);
+        const uint64_t adesc = sw128_kmajor_desc(smem_u32(stage_at(stage)));
+        const uint64_t bdesc = sw128_kmajor_desc(smem_u32(stage_at(stage) + C::W_BYTES));
+#pragma unroll
+        for (int kk = 0; kk < BK / 32; ++kk)
+          umma_i8(tmem_base, adesc + static_cast<uint64_t>(kk * 2), bdesc + static_cast<uint64_t>(kk * 2), kIdesc,
+                  (i | kk) != 0 ? 1u : 0u);
+        umma_commit(&empty[stage]);
+        if (++stage == STG) {
+          stage = 0;
+          ph ^= 1u;
+        }
+      }
+      if (ok) umma_commit(tfull);
+      FNI8_TRACE_AT(3);
+      umma_commit(drain);
+      mbar_wait(drain, 0, &g_status, kCodeDrain);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue warps
+    // While the mainloop runs: the per-token scales into shared memory, this thread's
+    // weight-row scale and bias into registers (they may come from the previous kernel).
+    pdl_wait();
+    if (epi.mode != kOutI32) {
+      for (int m = threadIdx.x - 64; m < M; m += 128) s_as[m] = __ldg(epi.a_scale + m);
+      if (n_row < N) {
+        wsn = __ldg(epi.w_scale + n_row);
+        if (epi.bias != nullptr)
+          bn = epi.mode == kOutBF16 ? to_f32<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(epi.bias)[n_row])
+                                    : to_f32<__half>(static_cast<const __half*>(epi.bias)[n_row]);
+      }
+    }
+    named_bar_sync(1, 128);
+    if (lane == 0) okt = mbar_wait(tfull, 0, &g_status, kCodeEpilogue) ? 1 : 0;
+    okt = __shfl_sync(0xffffffffu, okt, 0);
+    tc_fence_after();
+    if (threadIdx.x == 64) FNI8_TRACE_AT(4);
+  }
+  __syncwarp();
+
+  const int q = warp & 3;  // TMEM lane quarter this warp may read (warps 2-5 -> 2,3,0,1)
+  const int trow = q * 32 + lane;
+  const int n = n_row;
+  const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+  const int mcols = (M + 3) & ~3;
+  const int share = S > 1 ? split_share(mcols, static_cast<int>(S)) : mcols;
+  const int own0 = static_cast<int>(rank) * share;
+  const int len = own0 < mcols ? (mcols - own0 < share ? mcols - own0 : share) : 0;
+  // the producer drained the ring (every load landed) and the MMAs are complete: the ring
+  // is free for the output tile
+  __syncthreads();
+  if (S > 1) {
+    // publish the partial sums of the columns other CTAs own
+    if (warp >= 2 && okt) {
+      uint4* slab = ws + static_cast<int64_t>(blockIdx.x) * (NT / 4) * BNW;
+      constexpr int CH = NT < 32 ? NT : 32;
+#pragma unroll 1
+      for (int c0 = 0; c0 < mcols; c0 += CH) {
+        uint32_t r[CH];
+        if constexpr (CH == 16) tmem_ld16(taddr + c0, reinterpret_cast<uint32_t(&)[16]>(r));
+        else tmem_ld32(taddr + c0, reinterpret_cast<uint32_t(&)[32]>(r));
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < CH; j += 4) {
+          const int col = c0 + j;
+          if (col < mcols && col / share != static_cast<int>(rank))
+            __stcg(slab + (col >> 2) * BNW + trow, make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
+        }
+      }
+    }
+    cluster_sync_all();  // release/acquire at cluster scope: the slabs are visible to the owners
+    if (threadIdx.x == 64) FNI8_TRACE_AT(5);
+  }
+  if (warp >= 2 && okt && len > 0) {
+    const int block0 = static_cast<int>(blockIdx.x) - static_cast<int>(rank);
+    // drained ring: [output tile share x 128 x 2 B][landing area for the peers' granules]
+    uint4* land = reinterpret_cast<uint4*>(smem + ((share * BNW * 2 + 15) & ~15));
+    if (epi.mode == kOutBF16)
+      finish_owned<__nv_bfloat16>(epi, taddr, ws, NT / 4, block0, rank, S, own0, len, M, N, n, trow, wsn, bn, s_as,
+                                  epi.vec ? reinterpret_cast<__nv_bfloat16*>(smem) : nullptr, land);
+    else
+      finish_owned<__half>(epi, taddr, ws, NT / 4, block0, rank, S, own0, len, M, N, n, trow, wsn, bn, s_as,
+                           epi.vec ? reinterpret_cast<__half*>(smem) : nullptr, land);
+  }
+  if (warp >= 2 && epi.vec) {
+    // coalesced copy-out of the staged rows: 16 bytes per thread, 512 bytes per warp
+    named_bar_sync(1, 128);
+    const int rows = (okt && own0 < M) ? ((own0 + len < M ? own0 + len : M) - own0) : 0;
+    const int n0 = tile * BNW;
+    const int chunks_per_row = (N - n0) >= BNW ? BNW / 8 : (N - n0) / 8;
+    const int ct = threadIdx.x - 64;
+    const uint4* src = reinterpret_cast<const uint4*>(smem);
+    uint16_t* dst = static_cast<uint16_t*>(epi.out);
+    for (int i = ct; i < rows * (BNW / 8); i += 128) {
+      const int r = i >> 4, ch = i & 15;
+      if (ch < chunks_per_row)
+        *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(own0 + r) * N + n0 + ch * 8) = src[i];
+    }
+  }
+
+  if (threadIdx.x == 64) FNI8_TRACE_AT(6);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace splitk
+}  // namespace fni8b
+
+namespace fni8h {
+
+using namespace fni8b;
+
+#ifdef FNI8_TRACE
+extern "C" __attribute__((visibility("default"))) int fni8_trace_read_splitk(unsigned long long* dst, int n_records) {
+  const size_t bytes = static_cast<size_t>(n_records) * 8 * sizeof(unsigned long long);
+  if (cudaMemcpyFromSymbol(dst, splitk::g_trace, bytes) != cudaSuccess) return FNI8_ERR_CUDA;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, splitk::g_trace) != cudaSuccess) return FNI8_ERR_CUDA;
+  if (cudaMemset(p, 0, sizeof(splitk::g_trace)) != cudaSuccess) return FNI8_ERR_CUDA;
+  unsigned int z = 0;
+  if (cudaMemcpyToSymbol(splitk::g_trace_seq, &z, sizeof(z)) != cudaSuccess) return FNI8_ERR_CUDA;
+  return FNI8_OK;
+}
+#endif
+
+int splitk_status_read_and_clear(int* code) {
+  int v = 0, z = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, splitk::g_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "read split-K watchdog");
+  e = cudaMemcpyToSymbol(splitk::g_status, &z, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "clear split-K watchdog");
+  *code = v;
+  return FNI8_OK;
+}
+
+static int env_int(const char* name, int dflt) {
+  const char* e = getenv(name);
+  return e ? atoi(e) : dflt;
+}
+
+struct SplitPlan {
+  int nt, S, grid, stages, smem;
+  size_t ws_bytes;  // partial-sum slabs of the K split (zero-maintained GEMM workspace)
+};
+
+// NT: tokens rounded up to a power of two >= 16. S: the cluster size that brings the grid
+// (n_tiles x S) closest to the SM count without exceeding it (at least 1, at most 8 and
+// the number of K blocks). Ring: as many stages as fit in ~half an SM's shared memory
+// (two CTAs per SM, so the next kernel can become resident), at least 3 when the K range
+// is split (2 otherwise), else the whole SM; the drained ring must also hold the staged
+// output tile of the CTA's columns. FNI8_SPLITK_S, FNI8_SPLITK_TARGET_PCT and
+// FNI8_SPLITK_SMEM_KB override (measurement knobs).
+static bool plan_splitk(int64_t M, int64_t N, int64_t K, SplitPlan* p) {
+  if (M < 1 || M > kSplitkMaxM) return false;
+  int nt = 16;
+  while (nt < M) nt <<= 1;
+  p->nt = nt;
+  const int stage = splitk::BNW * splitk::BK + nt * splitk::BK;
+  const int n_tiles = (int)((N + splitk::BNW - 1) / splitk::BNW);
+  const int kb = (int)((K + splitk::BK - 1) / splitk::BK);
+  const int sms = num_sms(current_device());
+  static const int forced_s = env_int("FNI8_SPLITK_S", 0);
+  static const int target_pct = env_int("FNI8_SPLITK_TARGET_PCT", 100);
+  static const int forced_kb = env_int("FNI8_SPLITK_SMEM_KB", 0);
+  int S = forced_s;
+  if (S < 1 || S > 8) {
+    const int target = sms * target_pct / 100;
+    S = n_tiles >= target ? 1 : target / n_tiles;
+    if (S < 1) S = 1;
+    if (S > 8) S = 8;
+  }
+  if (S > kb) S = kb;
+  p->S = S;
+  p->grid = n_tiles * S;
+  const int sh = S > 1 ? splitk::split_share(nt, S) : nt;
+  const int out_tile = ((sh * splitk::BNW * 2 + 15) & ~15) + (S - 1) * sh * splitk::BNW * 4;
+  const int fixed = 1024 + splitk::kBarBytes + splitk::kAsBytes;
+  int stages = 0;
+  if (forced_kb > 0) {
+    stages = (forced_kb * 1024 - fixed) / stage;
+  } else {
+    stages = (113 * 1024 - fixed) / stage;
+    if (stages > splitk::kMaxStages) stages = splitk::kMaxStages;
+    if (stages < (S > 1 ? 3 : 2) || stages * stage < out_tile) stages = (225 * 1024 - fixed) / stage;
+  }
+  if (stages > splitk::kMaxStages) stages = splitk::kMaxStages;
+  if (stages < 2 || stages * stage < out_tile || fixed + stages * stage > 227 * 1024) return false;
+  p->stages = stages;
+  p->smem = fixed + stages * stage;
+  p->ws_bytes = S > 1 ? static_cast<size_t>(p->grid) * nt * splitk::BNW * 4 : 0;
+  return true;
+}
+
+template <int NT>
+static int launch_splitk(const CUtensorMap& tw, const CUtensorMap& tx, const splitk::Epi& epi, int M, int N, int K,
+                         const SplitPlan& p, uint4* ws, cudaStream_t st) {
+  auto kern = splitk::w8a8_splitk_kernel<NT>;
+  static bool configured[kMaxDevices] = {};
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return fail(FNI8_ERR_CUDA, "no current CUDA device");
+  if (!configured[dev]) {
+    // plans stay within 225 KB; the margin leaves room for static shared memory
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024);
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(split-K gemm)");
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return cuda_status(e, "carveout(split-K gemm)");
+    configured[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(splitk::kThreads);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled();
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, epi, M, N, K, p.stages, ws);
+  if (e != cudaSuccess) return cuda_status(e, "launch split-K gemm");
+  return FNI8_OK;
+}
+
+bool splitk_supported(int64_t M, int64_t N, int64_t K) {
+  SplitPlan p;
+  return N < (1LL << 31) && K < (1LL << 31) && plan_splitk(M, N, K, &p);
+}
+
+size_t splitk_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  SplitPlan p;
+  return plan_splitk(M, N, K, &p) ? p.ws_bytes : 0;
+}
+
+int splitk_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
+                const void* residual, void* out, int out_mode, int64_t M, int64_t N, int64_t K, void* ws,
+                size_t ws_bytes, cudaStream_t st) {
+  if (M <= 0 || N <= 0) return FNI8_OK;
+  SplitPlan p;
+  if (!plan_splitk(M, N, K, &p))
+    return fail(FNI8_ERR_UNSUPPORTED, "split-K decode GEMM takes 1 <= M <= %lld (got %lld)", (long long)kSplitkMaxM,
+                (long long)M);
+  if (p.ws_bytes > 0 && (ws == nullptr || ws_bytes < p.ws_bytes))
+    return fail(FNI8_ERR_WORKSPACE, "split-K GEMM needs %zu workspace bytes (got %zu)", p.ws_bytes, ws_bytes);
+  if ((reinterpret_cast<uintptr_t>(ws) & 15u) != 0) return fail(FNI8_ERR_ALIGN, "workspace must be 16-byte aligned");
+  CUtensorMap tw, tx;
+  if (int s = encode_tmap_2d_i8(&tw, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, 128, 128)) return s;
+  if (int s = encode_tmap_2d_i8(&tx, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, 128, (uint32_t)p.nt)) return s;
+  const int vec = out_mode != splitk::kOutI32 && residual == nullptr && N % 8 == 0 &&
+                  (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+  splitk::Epi epi{a_scale, w_scale, bias, residual, out, out_mode, vec};
+  uint4* w4 = static_cast<uint4*>(ws);
+  switch (p.nt) {
+    case 16: return launch_splitk<16>(tw, tx, epi, (int)M, (int)N, (int)K, p, w4, st);
+    case 32: return launch_splitk<32>(tw, tx, epi, (int)M, (int)N, (int)K, p, w4, st);
+    case 64: return launch_splitk<64>(tw, tx, epi, (int)M, (int)N, (int)K, p, w4, st);
+    case 128: return launch_splitk<128>(tw, tx, epi, (int)M, (int)N, (int)K, p, w4, st);
+    default: return launch_splitk<256>(tw, tx, epi, (int)M, (int)N, (int)K, p, w4, st);
+  }
+}
+
+}  // namespace fni8h

@@ -17,7 +17,7 @@ OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_ALIGN, ERR_CUDA, ERR_WORKSPACE, ERR_DEVICE
 F16, BF16, F32, I32, I8 = range(5)
 ACT_SILU, ACT_GELU_TANH = 0, 1
 SCORE_SOFTMAX, SCORE_SIGMOID = 0, 1
-PATH_AUTO, PATH_TILE, PATH_STREAM, PATH_FUSED = 0, 1, 2, 3
+PATH_AUTO, PATH_TILE, PATH_STREAM, PATH_FUSED, PATH_SPLITK = 0, 1, 2, 3, 4
 
 _p = ctypes.c_void_p
 _i = ctypes.c_int

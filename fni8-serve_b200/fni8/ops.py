@@ -60,9 +60,10 @@ def _act_dtype(x: torch.Tensor, what: str) -> int:
 class _Workspace:
     """Per-device GEMM workspace: zeroed once, kept zero by the kernels, never freed.
 
-    Sized for the largest skinny-M problem the stream-K kernel takes (M <= 256), so it
-    is allocated once, before any CUDA-graph capture, and reused by every call. Calls on
-    different streams of one device must not overlap while they share it.
+    Sized for the largest decode problem (M <= 256) of the stream-K kernel and of the
+    split-K kernel, so it is allocated once, before any CUDA-graph capture, and reused by
+    every call. Calls on different streams of one device must not overlap while they
+    share it.
     """
 
     def __init__(self):
@@ -76,9 +77,10 @@ class _Workspace:
             with self._lock:
                 buf = self._bufs.get(idx)
                 if buf is None:
-                    # G slots of 128 x 256 int32 + G counters for G <= SM count
+                    # stream-K: G slots of 128 x 256 int32 + G counters, G <= SM count;
+                    # split-K: one 128 x 256 int32 slab per CTA, up to 2 CTAs per SM
                     sms = torch.cuda.get_device_properties(idx).multi_processor_count
-                    nbytes = sms * (128 * 256 + 1) * 4
+                    nbytes = 2 * sms * (128 * 256 + 1) * 4
                     buf = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
                     self._bufs[idx] = buf
         return buf

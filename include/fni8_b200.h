@@ -64,7 +64,8 @@ enum fni8_gemm_path {
   FNI8_PATH_AUTO = 0,   /* by shape, from B200 measurements */
   FNI8_PATH_TILE = 1,   /* tcgen05 tile kernel, 128-row activation tiles */
   FNI8_PATH_STREAM = 2, /* swap-AB stream-K kernel for M <= 256 (uses the workspace) */
-  FNI8_PATH_FUSED = 3   /* linear only: quantisation fused into a cluster split-K kernel, M <= 32 */
+  FNI8_PATH_FUSED = 3,  /* linear only: quantisation fused into a cluster split-K kernel, M <= 32 */
+  FNI8_PATH_SPLITK = 4  /* swap-AB cluster split-K kernel for M <= 256 (uses the workspace) */
 };
 
 /* ------------------------------------------------------------------ library */

@@ -5,6 +5,8 @@ given identical inputs, MoE grouping) must be bit-exact. Floating-point producer
 whose reduction order differs from torch's CPU order (RMSNorm's sum of squares) or
 whose transcendental differs from torch's (expf in SiLU/GELU) are held to one fp16 ulp.
 """
+import os
+
 import pytest
 import torch
 
@@ -14,6 +16,7 @@ pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a B200")]
 
 DEV = "cuda"
+PKG = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "fni8-serve_b200")
 
 
 def gen(seed):
@@ -145,25 +148,27 @@ def test_gemm_int32_bit_exact(M, N, K):
 
     a, w = _int8((M, K), M + 1), _int8((N, K), N + 2)
     ref = O.int_mm_fast(a, w)
-    paths = [nat.PATH_TILE, nat.PATH_AUTO] + ([nat.PATH_STREAM] if M <= 256 else [])
+    paths = [nat.PATH_TILE, nat.PATH_AUTO] + ([nat.PATH_STREAM, nat.PATH_SPLITK] if M <= 256 else [])
     for p in paths:
         got = fni8.gemm_i32(a.to(DEV), w.to(DEV), path=p).cpu()
         assert torch.equal(got, ref), (p, (got - ref).abs().max())
 
 
+@pytest.mark.parametrize("path", ["stream", "splitk"])
 @pytest.mark.parametrize("M,N,K", [(1, 6144, 4096), (32, 4096, 4096), (7, 24576, 4096), (256, 4096, 12288),
                                    (96, 1000, 2048)])
-def test_stream_gemm_repeat_and_workspace_clean(M, N, K):
-    """Stream-K partial tiles go through the shared workspace: results stay exact across
-    calls of different shapes, and the workspace is zero again after each call."""
+def test_decode_gemm_repeat_and_workspace_clean(M, N, K, path):
+    """Stream-K and split-K partial sums go through the shared workspace: results stay
+    exact across calls of different shapes, and the workspace is zero again after each call."""
     import fni8
     from fni8 import _native as nat
     from fni8.ops import WORKSPACE
 
+    p = nat.PATH_STREAM if path == "stream" else nat.PATH_SPLITK
     a, w = _int8((M, K), 5 * M), _int8((N, K), 7)
     ref = O.int_mm_fast(a, w)
     for _ in range(3):
-        got = fni8.gemm_i32(a.to(DEV), w.to(DEV), path=nat.PATH_STREAM).cpu()
+        got = fni8.gemm_i32(a.to(DEV), w.to(DEV), path=p).cpu()
         assert torch.equal(got, ref)
     torch.cuda.synchronize()
     assert int(WORKSPACE.get(torch.device(DEV)).count_nonzero()) == 0
@@ -171,7 +176,7 @@ def test_stream_gemm_repeat_and_workspace_clean(M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(16, 256, 512), (256, 6144, 1024), (77, 4104, 1024), (1024, 2048, 2048),
-                                   (4, 100, 64)])
+                                   (4, 100, 64), (40, 4096, 12288), (130, 520, 4096)])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("extras", ["none", "bias", "bias+residual"])
 def test_dequant_epilogue_bit_exact(M, N, K, dtype, extras):
@@ -186,11 +191,38 @@ def test_dequant_epilogue_bit_exact(M, N, K, dtype, extras):
     res = torch.randn(M, N, generator=g).to(dtype) if extras == "bias+residual" else None
     ref = O.dequant(O.int_mm_fast(q, wq), s, ws, bias=bias, residual=res, out_dtype=dtype)
     qt = fni8.QTensor(wq.to(DEV), ws.to(DEV), scheme="per_row_i8")
-    paths = [nat.PATH_TILE] + ([nat.PATH_STREAM] if M <= 256 else [])
+    paths = [nat.PATH_TILE] + ([nat.PATH_STREAM, nat.PATH_SPLITK] if M <= 256 else [])
     for p in paths:
         got = fni8.linear_q(q.to(DEV), s.to(DEV), qt, bias=None if bias is None else bias.to(DEV),
                             residual=None if res is None else res.to(DEV), out_dtype=dtype, path=p).cpu()
         assert torch.equal(got, ref), (p, (got.float() - ref.float()).abs().max())
+
+
+@pytest.mark.parametrize("S", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("M,N,K", [(1, 640, 2048), (17, 1000, 4096), (64, 384, 1152), (200, 4104, 8192)])
+def test_splitk_every_cluster_size(M, N, K, S):
+    """The split-K kernel under each cluster size (forced through FNI8_SPLITK_S in a child
+    process, since the plan reads it once): int32 sums exact for every K split."""
+    import subprocess
+    import sys
+
+    code = f"""
+import sys, torch
+sys.path.insert(0, {PKG!r})
+import fni8
+from fni8 import _native as nat
+g = torch.Generator().manual_seed({M + N + S})
+a = torch.randint(-127, 128, ({M}, {K}), generator=g, dtype=torch.int8)
+w = torch.randint(-127, 128, ({N}, {K}), generator=g, dtype=torch.int8)
+ref = (a.long() @ w.long().T).int()
+got = fni8.gemm_i32(a.cuda(), w.cuda(), path=nat.PATH_SPLITK).cpu()
+assert torch.equal(got, ref), (got - ref).abs().max()
+assert fni8.device_status() == 0
+print("ok")
+"""
+    env = dict(os.environ, FNI8_SPLITK_S=str(S))
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
 
 
 @pytest.mark.parametrize("M,K,N", [(256, 1024, 6144), (1, 4096, 6144), (8, 4096, 4096), (32, 4096, 24576),

@@ -1,0 +1,119 @@
+"""The multi-GPU forms on 2 GPUs over NCCL (skipped with fewer than 2 GPUs).
+
+The expert-parallel MoE layer and the column-parallel linear run the sm_100a kernels
+on each rank and exchange over NCCL; each rank checks its result against the
+single-GPU kernels on the unsharded weights, bit for bit (every row's int32 sums and
+its dequant epilogue do not depend on how the rows or columns were grouped).
+"""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+
+
+def _ep_worker(rank, world, port, errq):
+    try:
+        _init(rank, world, port)
+        import fni8.moe as moe
+        from fni8 import QTensor
+        from fni8.moe import ExpertStack
+        from fni8.parallel import ExpertParallelMoE, expert_shard
+        from fni8.quant.core import quantize_int8_rowwise
+
+        dev = torch.device("cuda", rank)
+        E, k, H, I = 16, 4, 512, 256
+        T = 300 + 77 * rank  # ragged: the ranks hold different token counts
+        g = torch.Generator(device=dev).manual_seed(5)
+        gu = [quantize_int8_rowwise(0.05 * torch.randn(2 * I, H, generator=g, device=dev)) for _ in range(E)]
+        dn = [quantize_int8_rowwise(0.05 * torch.randn(H, I, generator=g, device=dev)) for _ in range(E)]
+        w_gu = torch.stack([q for q, _ in gu])
+        s_gu = torch.stack([s.view(-1) for _, s in gu])
+        w_dn = torch.stack([q for q, _ in dn])
+        s_dn = torch.stack([s.view(-1) for _, s in dn])
+        lo, hi = expert_shard(E, world, rank)
+        ep = ExpertParallelMoE(ExpertStack(w_gu[lo:hi].contiguous(), s_gu[lo:hi].contiguous(),
+                                           w_dn[lo:hi].contiguous(), s_dn[lo:hi].contiguous()), E)
+        full = ExpertStack(w_gu, s_gu, w_dn, s_dn)
+        gx = torch.Generator(device=dev).manual_seed(100 + rank)
+        x = torch.randn(T, H, generator=gx, device=dev).half()
+        bias = torch.zeros(E, device=dev)
+        bias[0] = 3.0  # skew: expert 0 (rank 0) is popular
+        topi, topw = moe.route(torch.randn(T, E, generator=gx, device=dev) + bias, k)
+        got = ep(x, topi, topw)
+        ref = moe.experts(x, topi, topw, full)
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref), (got.float() - ref.float()).abs().max().item()
+        # a rank with no tokens still takes every collective step
+        got0 = ep(x[:0], topi[:0], topw[:0]) if rank == 1 else ep(x, topi, topw)
+        assert got0.shape[0] == (0 if rank == 1 else T)
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report to the parent, which fails the test
+        errq.put(f"rank {rank}: {e!r}")
+        raise
+
+
+def _cp_worker(rank, world, port, errq):
+    try:
+        _init(rank, world, port)
+        import fni8
+        from fni8 import QTensor
+        from fni8.parallel import ColumnParallelLinearW8A8, shard_rows
+        from fni8.quant.core import quantize_int8_rowwise
+
+        dev = torch.device("cuda", rank)
+        K, N = 1024, 2048
+        g = torch.Generator(device=dev).manual_seed(3)
+        q, s = quantize_int8_rowwise(0.02 * torch.randn(N, K, generator=g, device=dev))
+        full = QTensor(q, s.view(-1))
+        cp = ColumnParallelLinearW8A8(shard_rows(full, world, rank))
+        for M in (1, 16, 300):
+            x = torch.randn(M, K, generator=g, device=dev).half()
+            got = cp(x)
+            ref = fni8.linear(x, full)
+            assert torch.equal(got, ref), (M, (got.float() - ref.float()).abs().max().item())
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        errq.put(f"rank {rank}: {e!r}")
+        raise
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("worker", [_ep_worker, _cp_worker], ids=["expert_parallel", "column_parallel"])
+def test_two_nccl_ranks(worker):
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=worker, args=(r, 2, port, errq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            errs.append("rank timed out")
+    assert not errs and all(p.exitcode == 0 for p in procs), errs

@@ -179,7 +179,9 @@ static int gemm_any(const int8_t* a, const float* a_scale, const int8_t* w, cons
     return stream_gemm(a, a_scale, w, w_scale, bias, residual, out, mode, M, N, K, ws, ws_bytes, st);
   if (p == FNI8_PATH_SPLITK)
     return splitk_gemm(a, a_scale, w, w_scale, bias, residual, out, mode, M, N, K, ws, ws_bytes, st);
-  return tile_gemm(a, a_scale, w, w_scale, bias, residual, out, mode, M, N, K, pick_bn(M, N), st);
+  // prefill sizes: 256-row tiles on CTA pairs, each SM holding half of a weight tile
+  const bool pair = tile_pair_enabled() && M >= 256;
+  return tile_gemm(a, a_scale, w, w_scale, bias, residual, out, mode, M, N, K, pair ? 256 : pick_bn(M, N), pair, st);
 }
 
 }  // namespace fni8h

@@ -10,12 +10,17 @@ constexpr int kMaxDevices = 64;
 constexpr int kTileMaxSeg = 512;  // segments of one grouped launch
 
 // tcgen05 tile GEMM (gemm_tile.cu). out_mode: 0 fp16, 1 bf16, 2 int32 accumulators.
+// pair: 256-row tiles on CTA pairs (tcgen05.mma.cta_group::2).
 int tile_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
-              const void* residual, void* out, int out_mode, int64_t M, int64_t N, int64_t K, int bn,
+              const void* residual, void* out, int out_mode, int64_t M, int64_t N, int64_t K, int bn, bool pair,
               cudaStream_t st);
 int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w, const float* w_scale,
                       int64_t E, int64_t N, int64_t K, const int32_t* seg_expert, const int32_t* seg_off,
-                      const int32_t* seg_cnt, int64_t S, void* out, int out_mode, int bn, cudaStream_t st);
+                      const int32_t* seg_cnt, int64_t S, void* out, int out_mode, int bn, bool pair,
+                      cudaStream_t st);
+// Whether dense (prefill-size) and grouped tile GEMMs run on CTA pairs.
+bool tile_pair_enabled();
+bool grouped_pair_enabled();
 int tile_status_read_and_clear(int* code);
 
 // Swap-AB stream-K GEMM for skinny M (gemm_stream.cu).

@@ -15,6 +15,12 @@
 // Tiles are visited in bands of kGroupM m-tiles so a wave of 148 CTAs reuses the same
 // A rows and W columns out of the 126 MB L2.
 //
+// PAIR: two CTAs of a cluster run each tile of 256 rows as one tcgen05.mma.cta_group::2
+// (M=256): each loads its 128 A rows and half of the BN weight rows, so a weight tile is
+// read once per 256 rows and each SM's shared memory holds and feeds half of it. The even
+// CTA of the pair arms the stage barriers (the odd CTA's loads complete on them) and
+// issues the MMAs; the commits reach both CTAs' barriers; each CTA stores its own rows.
+//
 // GROUPED: the A rows are split into segments (one per expert, or per (source rank,
 // expert) pair under expert parallelism); segment s multiplies rows
 // [off[s], off[s]+cnt[s]) by expert exp[s] of a [E, N, K] weight stack (3-D TMA map).
@@ -26,6 +32,8 @@
 // sees FNI8_ERR_DEVICE_TIMEOUT from fni8_device_status().
 #include "fni8_common.cuh"
 #include "gemm_internal.h"
+
+#include <stdlib.h>
 
 namespace fni8b {
 namespace tile {
@@ -57,12 +65,14 @@ struct Groups {
   int S;
 };
 
-template <int BN>
+template <int BN, bool PAIR>
 struct Cfg {
+  static constexpr int BMT = PAIR ? 2 * BM : BM;  // rows of a tile
+  static constexpr int BNL = PAIR ? BN / 2 : BN;  // weight rows this CTA loads per stage
   static constexpr int A_BYTES = BM * BK;
-  static constexpr int B_BYTES = BN * BK;
+  static constexpr int B_BYTES = BNL * BK;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int STAGES = PAIR ? (BN == 256 ? 6 : 8) : ((BN == 256) ? 4 : 6);
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SEG_BYTES = (kMaxSeg + 1 + 3 * kMaxSeg) * 4;
@@ -82,7 +92,8 @@ struct TileCoord {
   int expert;
 };
 
-template <bool GROUPED>
+// Tile t -> rows [row0, row0 + rows_valid) (rows_valid <= BMT) and weight block n_blk.
+template <bool GROUPED, int BMT>
 __device__ __forceinline__ TileCoord decode_tile(int t, int M, int m_tiles, int n_tiles, const int32_t* prefix,
                                                  const int32_t* soff, const int32_t* scnt, const int32_t* sexp,
                                                  int S) {
@@ -97,8 +108,8 @@ __device__ __forceinline__ TileCoord decode_tile(int t, int M, int m_tiles, int 
       else hi = mid - 1;
     }
     const int ml = mt - prefix[lo];
-    tc.row0 = soff[lo] + ml * BM;
-    tc.rows_valid = min(BM, scnt[lo] - ml * BM);
+    tc.row0 = soff[lo] + ml * BMT;
+    tc.rows_valid = min(BMT, scnt[lo] - ml * BMT);
     tc.expert = sexp[lo];
   } else {
     const int band_tiles = kGroupM * n_tiles;
@@ -108,8 +119,8 @@ __device__ __forceinline__ TileCoord decode_tile(int t, int M, int m_tiles, int 
     const int local = t - band * band_tiles;
     const int m_blk = first_m + local % gm;
     tc.n_blk = local / gm;
-    tc.row0 = m_blk * BM;
-    tc.rows_valid = min(BM, M - tc.row0);
+    tc.row0 = m_blk * BMT;
+    tc.rows_valid = min(BMT, M - tc.row0);
     tc.expert = 0;
   }
   return tc;
@@ -173,12 +184,12 @@ __device__ __forceinline__ void store_chunk_i32(const Epi& epi, const uint32_t (
   }
 }
 
-template <int BN, bool GROUPED>
+template <int BN, bool GROUPED, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a8_tile_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmOut, Epi epi, Groups grp, int M, int N, int K, int vec_ok,
                      int tma_store) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE);
@@ -195,6 +206,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* stg = smem + C::STG_OFF;  // 1024-aligned: the 64B-swizzle pattern follows address bits
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // pair role: half = 0 for the even CTA (arms the stage barriers, issues the MMAs)
+  const uint32_t half = PAIR ? (cluster_ctarank() & 1u) : 0u;
+  const uint32_t lead = PAIR ? (cluster_ctarank() & ~1u) : 0u;  // cluster rank of the even CTA
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << lead);
+  const int t0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int tstep = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -203,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);  // one arrive per epilogue warp
+      mbar_init(&tempty[b], PAIR ? 8 : 4);  // one arrive per epilogue warp (of both CTAs)
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -213,8 +230,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, C::TMEM_COLS);  // both CTAs, same warp, same address
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    }
     tc_fence_before();
   }
 
@@ -225,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (GROUPED || !(warp == 0 && lane == 0)) pdl_wait();
 
   const int n_tiles = (N + BN - 1) / BN;
-  const int m_tiles = (M + BM - 1) / BM;
+  const int m_tiles = (M + C::BMT - 1) / C::BMT;
   const int kb = (K + BK - 1) / BK;
   int S = 0;
   if constexpr (GROUPED) {
@@ -241,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) prefix[0] = 0;
       for (int base = 0; base < S; base += 32) {
         const int i = base + lane;
-        int v = (i < S) ? (scnt[i] + BM - 1) / BM : 0;
+        int v = (i < S) ? (scnt[i] + C::BMT - 1) / C::BMT : 0;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const int u = __shfl_up_sync(0xffffffffu, v, o);
@@ -252,7 +274,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
-  __syncthreads();
+  // a pair's CTAs signal each other's barriers from here on: both are initialised first
+  if constexpr (PAIR) cluster_sync_all();
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total = GROUPED ? prefix[S] * n_tiles : m_tiles * n_tiles;
@@ -265,39 +289,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t armed = 0;  // parity each stage was last armed with (bit per stage)
       int issued = 0;
       bool ok = true;
-      int t = blockIdx.x, k = 0;
+      int t = t0, k = 0;
       TileCoord tc{};
-      if (t < total) tc = decode_tile<GROUPED>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
+      if (t < total) tc = decode_tile<GROUPED, C::BMT>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
+      // this CTA's A rows and weight rows of a tile; stage loads complete on the even CTA's
+      // barrier under PAIR, which is armed with the bytes of both CTAs
+      const int a_off = static_cast<int>(half) * BM;
+      const int b_off = static_cast<int>(half) * C::BNL;
+      constexpr uint32_t kStageTx = PAIR ? 2 * C::STAGE : C::STAGE;
+      auto load_a = [&](int s, int kx, int row) {
+        if constexpr (PAIR) tma_load_2d_pair(&tmA, mapa_shared(smem_u32(&full[s]), lead), smem + s * C::STAGE, kx, row + a_off);
+        else tma_load_2d(&tmA, &full[s], smem + s * C::STAGE, kx, row);
+      };
+      auto load_b = [&](int s, int kx, int nb, int ex) {
+        uint8_t* dst = smem + s * C::STAGE + C::A_BYTES;
+        if constexpr (PAIR) {
+          const uint32_t bar = mapa_shared(smem_u32(&full[s]), lead);
+          if constexpr (GROUPED) tma_load_3d_pair(&tmB, bar, dst, kx, nb * BN + b_off, ex);
+          else tma_load_2d_pair(&tmB, bar, dst, kx, nb * BN + b_off);
+        } else {
+          if constexpr (GROUPED) tma_load_3d(&tmB, &full[s], dst, kx, nb * BN, ex);
+          else tma_load_2d(&tmB, &full[s], dst, kx, nb * BN);
+        }
+      };
       auto advance = [&]() {
         if (++k == kb) {
           k = 0;
-          t += gridDim.x;
-          if (t < total) tc = decode_tile<GROUPED>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
+          t += tstep;
+          if (t < total) tc = decode_tile<GROUPED, C::BMT>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
         }
       };
       if constexpr (!GROUPED) {
         int pre_row[C::STAGES], pre_k[C::STAGES];
         int pre = 0;
         for (; pre < C::STAGES && t < total; ++pre, advance()) {  // first use of each stage
-          uint8_t* sa = smem + pre * C::STAGE;
-          mbar_arrive_expect_tx(&full[pre], C::STAGE);
-          tma_load_2d(&tmB, &full[pre], sa + C::A_BYTES, k * BK, tc.n_blk * BN);
+          if (half == 0) mbar_arrive_expect_tx(&full[pre], kStageTx);
+          load_b(pre, k * BK, tc.n_blk, 0);
           pre_row[pre] = tc.row0;
           pre_k[pre] = k;
         }
         {  // weight tiles of the next units into L2 while the upstream kernel drains
           int tt = t, kk = k, nb = tc.n_blk;
           for (int i = 0; i < kL2AheadUnits && tt < total; ++i) {
-            tma_prefetch_l2_2d(&tmB, kk * BK, nb * BN);
+            tma_prefetch_l2_2d(&tmB, kk * BK, nb * BN + b_off);
             if (++kk == kb) {
               kk = 0;
-              tt += gridDim.x;
-              if (tt < total) nb = decode_tile<GROUPED>(tt, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S).n_blk;
+              tt += tstep;
+              if (tt < total) nb = decode_tile<GROUPED, C::BMT>(tt, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S).n_blk;
             }
           }
         }
         pdl_wait();
-        for (int i = 0; i < pre; ++i) tma_load_2d(&tmA, &full[i], smem + i * C::STAGE, pre_k[i] * BK, pre_row[i]);
+        for (int i = 0; i < pre; ++i) load_a(i, pre_k[i] * BK, pre_row[i]);
         issued = pre;
         stage = pre % C::STAGES;
         ph = (pre == C::STAGES) ? 1u : 0u;
@@ -307,12 +350,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        uint8_t* sa = smem + stage * C::STAGE;
-        uint8_t* sb = sa + C::A_BYTES;
-        mbar_arrive_expect_tx(&full[stage], C::STAGE);
-        tma_load_2d(&tmA, &full[stage], sa, k * BK, tc.row0);
-        if constexpr (GROUPED) tma_load_3d(&tmB, &full[stage], sb, k * BK, tc.n_blk * BN, tc.expert);
-        else tma_load_2d(&tmB, &full[stage], sb, k * BK, tc.n_blk * BN);
+        if (half == 0) mbar_arrive_expect_tx(&full[stage], kStageTx);
+        load_a(stage, k * BK, tc.row0);
+        load_b(stage, k * BK, tc.n_blk, tc.expert);
         armed = (armed & ~(1u << stage)) | (ph << stage);
         ++issued;
         if (++stage == C::STAGES) {
@@ -321,23 +361,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Drain: the loads of the last min(issued, STAGES) stages must have landed before
-      // the CTA may exit (normally they have: the MMA consumed them).
+      // the CTA may exit (normally they have: the MMA consumed them). The odd CTA of a pair
+      // sees its loads land through the release of the stage (the MMA consumed them).
+      uint64_t* done = half == 0 ? full : empty;
       const int pending = issued < C::STAGES ? issued : C::STAGES;
       for (int i = 0; i < pending; ++i) {
         const int s = (stage - 1 - i + 2 * C::STAGES) % C::STAGES;
-        mbar_wait(&full[s], (armed >> s) & 1u, &g_status, kCodeDrain);
+        mbar_wait(&done[s], (armed >> s) & 1u, &g_status, kCodeDrain);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t kIdesc = idesc_i8(BM, BN);
+    if (lane == 0 && half == 0) {
+      constexpr uint32_t kIdesc = idesc_i8(C::BMT, BN);
       int stage = 0;
       uint32_t ph = 0;
       int acc = 0;
       uint32_t aph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      for (int t = t0; t < total && ok; t += tstep) {
         if (!mbar_wait(&tempty[acc], aph ^ 1u, &g_status, kCodeMma)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -353,22 +395,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk) {
             // advance the start address by kk * 32 bytes inside the 128-byte swizzle atom
-            umma_i8(d, adesc + static_cast<uint64_t>(kk * 2), bdesc + static_cast<uint64_t>(kk * 2), kIdesc,
-                    (k | kk) != 0 ? 1u : 0u);
+            if constexpr (PAIR)
+              umma_i8_pair(d, adesc + static_cast<uint64_t>(kk * 2), bdesc + static_cast<uint64_t>(kk * 2), kIdesc,
+                           (k | kk) != 0 ? 1u : 0u);
+            else
+              umma_i8(d, adesc + static_cast<uint64_t>(kk * 2), bdesc + static_cast<uint64_t>(kk * 2), kIdesc,
+                      (k | kk) != 0 ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          if constexpr (PAIR) umma_commit_pair_to(&empty[stage], pair_mask);
+          else umma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
             ph ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        if constexpr (PAIR) umma_commit_pair_to(&tfull[acc], pair_mask);
+        else umma_commit(&tfull[acc]);
         acc ^= 1;
         if (acc == 0) aph ^= 1u;
       }
       // All MMAs issued by this thread must retire before TMEM is freed.
-      umma_commit(drain);
+      if constexpr (PAIR) umma_commit_pair(drain);
+      else umma_commit(drain);
       mbar_wait(drain, 0, &g_status, kCodeDrain);
     }
     __syncwarp();
@@ -387,10 +436,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t aph = 0;
     int sb = 0;  // staging buffer of this warp used next
     if (tma_store && lane == 0) tma_prefetch_desc(&tmOut);
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      const TileCoord tc = decode_tile<GROUPED>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
-      const bool valid = row_local < tc.rows_valid;
-      const int64_t row = static_cast<int64_t>(tc.row0) + row_local;
+    for (int t = t0; t < total; t += tstep) {
+      const TileCoord tc = decode_tile<GROUPED, C::BMT>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
+      // this CTA's rows of the tile
+      const int row0 = tc.row0 + static_cast<int>(half) * BM;
+      const int rows_here = tc.rows_valid - static_cast<int>(half) * BM;
+      const bool valid = row_local < rows_here;
+      const int64_t row = static_cast<int64_t>(row0) + row_local;
       const int nb0 = tc.n_blk * BN;
       const float* wsc = epi.w_scale + static_cast<int64_t>(tc.expert) * N;
       float wreg[BN / 128], breg[BN / 128];
@@ -424,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // TMA store of whole 32-row slabs; a slab cut by a segment end (grouped) or any
       // residual add takes the per-thread path
       const bool slab_tma = tma_store && epi.residual == nullptr &&
-                            (!GROUPED || tc.rows_valid - q * 32 >= 32) && q * 32 < tc.rows_valid;
+                            (!GROUPED || rows_here - q * 32 >= 32) && q * 32 < rows_here;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
@@ -461,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmOut, buf, n0, tc.row0 + q * 32);
+            tma_store_2d(&tmOut, buf, n0, row0 + q * 32);
             bulk_commit_group();
           }
           sb ^= 1;
@@ -473,7 +525,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if (half == 0) mbar_arrive(&tempty[acc]);
+        else mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), lead));  // the even CTA's MMA waits on it
+      }
       acc ^= 1;
       if (acc == 0) aph ^= 1u;
     }
@@ -481,18 +536,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   }
 
-  __syncthreads();
+  // under PAIR also: neither CTA exits while the other may still signal its barriers
+  if constexpr (PAIR) cluster_sync_all();
+  else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
-template <int BN, bool GROUPED>
+template <int BN, bool GROUPED, bool PAIR>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, bool tma_store, const Epi& epi,
            const Groups& grp, int M, int N, int K, int grid, bool vec_ok, cudaStream_t st) {
-  using C = Cfg<BN>;
-  auto kern = w8a8_tile_kernel<BN, GROUPED>;
+  using C = Cfg<BN, PAIR>;
+  auto kern = w8a8_tile_kernel<BN, GROUPED, PAIR>;
   static bool configured[fni8h::kMaxDevices] = {};  // the attribute is set per device
   const int dev = fni8h::current_device();
   if (dev < 0 || dev >= fni8h::kMaxDevices) return fni8h::fail(FNI8_ERR_CUDA, "no current CUDA device");
@@ -510,11 +568,15 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, 
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = fni8h::pdl_enabled();
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = PAIR ? 2 : 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = PAIR ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, to, epi, grp, M, N, K, vec_ok ? 1 : 0, tma_store ? 1 : 0);
   if (e != cudaSuccess) return fni8h::cuda_status(e, "launch tile gemm");
   return FNI8_OK;
@@ -541,6 +603,25 @@ int tile_status_read_and_clear(int* code) {
   return FNI8_OK;
 }
 
+// Measured on B200: CTA pairs raise the dense prefill GEMMs by 4-10 %, while the grouped
+// expert GEMM, whose experts mostly hold fewer than 256 rows, loses ~10 % (a pair spends
+// two SMs on a short segment). FNI8_TILE_PAIR / FNI8_GROUPED_PAIR override for measurements.
+bool tile_pair_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("FNI8_TILE_PAIR");
+    return e == nullptr || atoi(e) != 0;
+  }();
+  return on;
+}
+
+bool grouped_pair_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("FNI8_GROUPED_PAIR");
+    return e != nullptr && atoi(e) != 0;
+  }();
+  return on;
+}
+
 // Tensor map for the TMA-store epilogue: 16-bit outputs whose rows are 16-byte aligned.
 // Returns false (per-thread stores) otherwise; no error is raised for that.
 static bool out_tma_map(CUtensorMap* map, void* out, int out_mode, int64_t rows, int64_t N) {
@@ -552,52 +633,69 @@ static bool out_tma_map(CUtensorMap* map, void* out, int out_mode, int64_t rows,
 }
 
 int tile_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
-              const void* residual, void* out, int out_mode, int64_t M, int64_t N, int64_t K, int bn,
+              const void* residual, void* out, int out_mode, int64_t M, int64_t N, int64_t K, int bn, bool pair,
               cudaStream_t st) {
   if (M <= 0 || N <= 0) return FNI8_OK;
   if (bn != 128 && bn != 256) return fail(FNI8_ERR_INVALID, "tile BN must be 128 or 256");
   CUtensorMap ta, tb;
   if (int s = encode_tmap_2d_i8(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, 128, 128)) return s;
-  if (int s = encode_tmap_2d_i8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, 128, (uint32_t)bn)) return s;
+  if (int s = encode_tmap_2d_i8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, 128, (uint32_t)(pair ? bn / 2 : bn)))
+    return s;
   tile::Epi epi{a_scale, w_scale, bias, residual, out, out_mode};
   tile::Groups grp{nullptr, nullptr, nullptr, 0};
-  const int m_tiles = (int)((M + 127) / 128);
+  const int bmt = pair ? 256 : 128;
+  const int m_tiles = (int)((M + bmt - 1) / bmt);
   const int n_tiles = (int)((N + bn - 1) / bn);
   const int64_t tiles = (int64_t)m_tiles * n_tiles;
   const int sms = num_sms(current_device());
-  const int grid = (int)(tiles < sms ? tiles : sms);
+  // one CTA per tile (two per tile under PAIR), at most one per SM
+  const int64_t ctas = pair ? 2 * tiles : tiles;
+  const int cap = pair ? (sms & ~1) : sms;
+  const int grid = (int)(ctas < cap ? ctas : cap);
   const size_t esz = out_mode == tile::kOutI32 ? 4 : 2;
   const bool vec_ok = ((N * (int64_t)esz) % 16 == 0) && (((uintptr_t)out & 15u) == 0) &&
                       (((uintptr_t)w_scale & 15u) == 0) && (bias == nullptr || ((uintptr_t)bias & 15u) == 0) &&
                       (residual == nullptr || ((uintptr_t)residual & 15u) == 0);
   CUtensorMap to;
   const bool tma_store = out_tma_map(&to, out, out_mode, M, N);
+  if (pair) {
+    if (bn == 256)
+      return tile::launch<256, false, true>(ta, tb, to, tma_store, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
+    return tile::launch<128, false, true>(ta, tb, to, tma_store, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
+  }
   if (bn == 256)
-    return tile::launch<256, false>(ta, tb, to, tma_store, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
-  return tile::launch<128, false>(ta, tb, to, tma_store, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
+    return tile::launch<256, false, false>(ta, tb, to, tma_store, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
+  return tile::launch<128, false, false>(ta, tb, to, tma_store, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
 }
 
 int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w, const float* w_scale,
                       int64_t E, int64_t N, int64_t K, const int32_t* seg_expert, const int32_t* seg_off,
-                      const int32_t* seg_cnt, int64_t S, void* out, int out_mode, int bn, cudaStream_t st) {
+                      const int32_t* seg_cnt, int64_t S, void* out, int out_mode, int bn, bool pair,
+                      cudaStream_t st) {
   if (R <= 0 || N <= 0 || S <= 0) return FNI8_OK;
   if (S > tile::kMaxSeg) return fail(FNI8_ERR_UNSUPPORTED, "at most %d segments (got %lld)", tile::kMaxSeg, (long long)S);
   CUtensorMap ta, tb;
   if (int s = encode_tmap_2d_i8(&ta, a, (uint64_t)K, (uint64_t)R, (uint64_t)K, 128, 128)) return s;
   if (int s = encode_tmap_3d_i8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)E, (uint64_t)K, (uint64_t)(N * K), 128,
-                                (uint32_t)bn))
+                                (uint32_t)(pair ? bn / 2 : bn)))
     return s;
   tile::Epi epi{a_scale, w_scale, nullptr, nullptr, out, out_mode};
   tile::Groups grp{seg_expert, seg_off, seg_cnt, (int)S};
-  const int grid = num_sms(current_device());
+  const int sms = num_sms(current_device());
+  const int grid = pair ? (sms & ~1) : sms;
   const size_t esz = out_mode == tile::kOutI32 ? 4 : 2;
   const bool vec_ok = ((N * (int64_t)esz) % 16 == 0) && (((uintptr_t)out & 15u) == 0) &&
                       (((uintptr_t)w_scale & 15u) == 0) && ((N % 4) == 0);
   CUtensorMap to;
   const bool tma_store = out_tma_map(&to, out, out_mode, R, N);
+  if (pair) {
+    if (bn == 256)
+      return tile::launch<256, true, true>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
+    return tile::launch<128, true, true>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
+  }
   if (bn == 256)
-    return tile::launch<256, true>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
-  return tile::launch<128, true>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
+    return tile::launch<256, true, false>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
+  return tile::launch<128, true, false>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
 }
 
 }  // namespace fni8h

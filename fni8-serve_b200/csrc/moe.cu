@@ -382,6 +382,7 @@ extern "C" int fni8_grouped_gemm_w8a8(const int8_t* a, const float* a_scale, int
   const int mode = out_dtype == FNI8_F16 ? 0 : (out_dtype == FNI8_BF16 ? 1 : 2);
   const int bn = (N % 256 == 0 || N > 1024) ? 256 : 128;
   return tile_gemm_grouped(a, a_scale, R, w, w_scale, E, N, K, seg_expert, seg_off, seg_cnt, S, out, mode, bn,
+                           grouped_pair_enabled(),
                            static_cast<cudaStream_t>(stream));
 }
 

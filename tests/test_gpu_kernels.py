@@ -225,6 +225,50 @@ print("ok")
     assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
 
 
+@pytest.mark.parametrize("pair", ["0", "1"])
+def test_tile_gemm_with_and_without_cta_pairs(pair):
+    """The tile kernel with 256-row tiles on CTA pairs (tcgen05.mma.cta_group::2) and with
+    128-row tiles on single CTAs gives the same exact int32 sums, dense and grouped, for
+    shapes with ragged M, N and K (both settings forced through the environment in a
+    child process, since the library reads them once)."""
+    import subprocess
+    import sys
+
+    code = f"""
+import sys, torch
+sys.path.insert(0, {PKG!r})
+import fni8
+from fni8 import _native as nat
+from fni8.moe import grouped_gemm
+g = torch.Generator().manual_seed(11)
+for M, N, K in [(256, 256, 128), (300, 512, 1024), (1024, 2048, 2048), (777, 1000, 272), (4096, 768, 4096)]:
+    a = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+    w = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
+    ref = (a.long() @ w.long().T).int()
+    got = fni8.gemm_i32(a.cuda(), w.cuda(), path=nat.PATH_TILE).cpu()
+    assert torch.equal(got, ref), ("dense", M, N, K)
+E, N, K = 6, 512, 256
+cnt = torch.tensor([0, 300, 17, 256, 129, 40], dtype=torch.int32)
+off = torch.zeros(E, dtype=torch.int32)
+off[1:] = torch.cumsum(cnt, 0)[:-1]
+R = int(cnt.sum())
+a = torch.randint(-127, 128, (R, K), generator=g, dtype=torch.int8)
+w = torch.randint(-127, 128, (E, N, K), generator=g, dtype=torch.int8)
+exp = torch.tensor([5, 0, 2, 1, 4, 3], dtype=torch.int32)
+got = grouped_gemm(a.cuda(), torch.ones(R).cuda(), w.cuda(), torch.ones(E, N).cuda(), exp.cuda(), off.cuda(),
+                   cnt.cuda(), out_dtype=torch.int32).cpu()
+for s in range(E):
+    o, c = int(off[s]), int(cnt[s])
+    if c:
+        assert torch.equal(got[o:o + c], (a[o:o + c].long() @ w[int(exp[s])].long().T).int()), ("grouped", s)
+assert fni8.device_status() == 0
+print("ok")
+"""
+    env = dict(os.environ, FNI8_TILE_PAIR=pair, FNI8_GROUPED_PAIR=pair)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+
+
 @pytest.mark.parametrize("M,K,N", [(256, 1024, 6144), (1, 4096, 6144), (8, 4096, 4096), (32, 4096, 24576),
                                    (128, 12288, 4096), (512, 4096, 6144)])
 def test_linear_bit_exact_vs_oracle(M, K, N):

@@ -26,6 +26,7 @@ import os
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 
 import torch
@@ -59,18 +60,52 @@ def committed_traffic(key):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and clock-event (throttle) reasons of this GPU, sampled every 2 ms through
+    NVML while the timed region runs (read-only queries; falls back to `nvidia-smi -lms 200`
+    when NVML is unavailable)."""
 
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
     Q = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device):
         self.uuid = str(torch.cuda.get_device_properties(device).uuid)
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        self.p = None
+        self.samples, self.max_mhz, self.stop = [], None, threading.Event()
+        self.thread = self.p = self.f = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            u = self.uuid if self.uuid.startswith("GPU-") else "GPU-" + self.uuid
+            try:
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(u)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(u.encode())
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self.nv = None
+
+    def _poll(self):
+        nv = self.nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop.is_set():
+            try:
+                self.samples.append((float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)),
+                                     int(get_reasons(self.h))))
+            except Exception:
+                pass
+            self.stop.wait(0.002)
 
     def __enter__(self):
+        if self.nv is not None:
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                        "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
@@ -79,6 +114,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.p is not None:
             self.p.terminate()
             try:
@@ -87,24 +125,32 @@ class ClockSampler:
                 self.p.kill()
 
     def summary(self):
-        self.f.flush()
+        if self.nv is not None:
+            if not self.samples:
+                return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+            sm = sorted(s for s, _ in self.samples)
+            reasons = sorted({name for _, r in self.samples for bit, name in self.REASONS.items() if r & bit})
+            return {"sm_mhz": sm[len(sm) // 2], "sm_min_mhz": sm[0], "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                    "samples": len(self.samples), "source": "nvml, 2 ms"}
         rows = []
-        for ln in open(self.f.name):
-            c = [x.strip() for x in ln.split(",")]
-            if len(c) < 10:
-                continue
-            u = c[1][4:] if c[1].startswith("GPU-") else c[1]
-            if self.uuid.replace("GPU-", "") not in u and u not in self.uuid:
-                continue
-            rows.append(c)
-        os.unlink(self.f.name)
+        if self.f is not None:
+            self.f.flush()
+            for ln in open(self.f.name):
+                c = [x.strip() for x in ln.split(",")]
+                if len(c) < 10:
+                    continue
+                u = c[1][4:] if c[1].startswith("GPU-") else c[1]
+                if self.uuid.replace("GPU-", "") not in u and u not in self.uuid:
+                    continue
+                rows.append(c)
+            os.unlink(self.f.name)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = sorted(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower().startswith("active")})
         return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": float(rows[0][3]), "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "source": "nvidia-smi, 200 ms"}
 
 
 def dist_env():
@@ -321,7 +367,7 @@ def run_config1(args, world, rank, dev):
         "frac_of_hbm": round(value / world / pk["hbm_gbs"], 3),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 3), "traffic": committed_traffic("decode_gemm"),
-                     "kernel": "w8a8_stream_kernel (the 20 decode GEMMs, graph-replayed, per-M graphs)",
+                     "kernel": "w8a8_splitk_kernel (M<=128) / CTA-pair w8a8_tile_kernel (M=256): the 20 decode GEMMs, graph-replayed, per-M graphs",
                      "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs)",
                      "gemm_gbs_per_M": per, "gemm_us_per_step": round(gemm_ms * 1e3, 2)},
         "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -392,7 +438,7 @@ def run_config2(args, world, rank, dev):
         "frac_of_int8_nominal": round(value / world / INT8_DENSE_NOMINAL_TOPS, 3),
         "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": INT8_DENSE_NOMINAL_TOPS,
                      "unit": "TOP/s", "frac": round(ach / INT8_DENSE_NOMINAL_TOPS, 3),
-                     "traffic": committed_traffic("prefill_gate_up"), "kernel": "w8a8_tile_kernel (gate_up)",
+                     "traffic": committed_traffic("prefill_gate_up"), "kernel": "w8a8_tile_kernel, CTA pairs (gate_up)",
                      "peak_source": "nominal dense int8 (no measured int8 peak); 2x measured bf16 = "
                                     f"{2 * pk['bf16_tflops']:.0f}"},
         "e2e": {"value": round(world * ops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TOP/s",
@@ -573,7 +619,7 @@ def run_config4(args, world, rank, dev):
     line["shard_kernels"] = per
     line["roofline"] = {"bound": "tensor", "achieved": per["M4096_shard"]["TOP/s"], "peak": INT8_DENSE_NOMINAL_TOPS,
                         "unit": "TOP/s", "frac": round(per["M4096_shard"]["TOP/s"] / INT8_DENSE_NOMINAL_TOPS, 3),
-                        "traffic": committed_traffic("sweep_m4096"), "kernel": "w8a8_tile_kernel (M=4096 shard)"}
+                        "traffic": committed_traffic("sweep_m4096"), "kernel": "w8a8_tile_kernel, CTA pairs (M=4096 shard)"}
     line["e2e"] = None
     line["gpu_launches"] = 6 * args.steps
     line["clocks"] = clk.summary()

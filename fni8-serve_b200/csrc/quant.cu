@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(kRowThreads) act_mul_vec(const T* __restrict__
           amax = fmaxf(amax, fabsf(g[j]));
         }
         raw[i] = Vec8<T>::pack(g);
-        if constexpr (!QUANT) reinterpret_cast<uint4*>(out + row * I)[c] = raw[i];
+        if (!QUANT || out != nullptr) reinterpret_cast<uint4*>(out + row * I)[c] = raw[i];
       }
     }
     if constexpr (QUANT) {
@@ -437,11 +437,13 @@ __global__ void __launch_bounds__(32 * kWarpRows) row_warp(const T* __restrict__
         }
       }
     }
-    if constexpr (ACTM && !QUANT) {
+    if constexpr (ACTM) {  // the product itself (always without quantisation, optional with it)
+      if (!QUANT || out != nullptr) {
 #pragma unroll
-      for (int i = 0; i < MW; ++i) {
-        const int c = lane + 32 * i;
-        if (c < nch) reinterpret_cast<uint4*>(out + row * K)[c] = raw[i];
+        for (int i = 0; i < MW; ++i) {
+          const int c = lane + 32 * i;
+          if (c < nch) reinterpret_cast<uint4*>(out + row * K)[c] = raw[i];
+        }
       }
     }
     if constexpr (QUANT) {
@@ -560,13 +562,13 @@ int norm_dispatch(const void* x, const void* res, const void* w, int64_t M, int6
 template <typename T, int ACT, bool QUANT>
 int act_dispatch(const void* x, int64_t M, int64_t I, void* out, int8_t* q, float* s, cudaStream_t st) {
   const int64_t nch = I / 8;
-  const bool vec = (I % 8 == 0) && aligned16(x) && (QUANT ? aligned16(q) : aligned16(out)) &&
+  // QUANT with `out`: both the product and its int8 rows are written
+  const bool vec = (I % 8 == 0) && aligned16(x) && (!QUANT || aligned16(q)) && (out == nullptr || aligned16(out)) &&
                    nch <= 16 * kRowThreads;
   const T* xx = static_cast<const T*>(x);
   T* oo = static_cast<T*>(out);
   const int g = row_grid(M);
-  if (vec && launch_row_warp<T, QUANT ? 4 : 3, ACT>(xx, nullptr, nullptr, M, (int)I, 0.f, 0, QUANT ? nullptr : oo,
-                                                    nullptr, q, s, st)) {
+  if (vec && launch_row_warp<T, QUANT ? 4 : 3, ACT>(xx, nullptr, nullptr, M, (int)I, 0.f, 0, oo, nullptr, q, s, st)) {
     FNI8_CHECK_LAUNCH(QUANT ? "act_and_mul_quant_i8" : "act_and_mul");
     return FNI8_OK;
   }
@@ -580,8 +582,8 @@ int act_dispatch(const void* x, int64_t M, int64_t I, void* out, int8_t* q, floa
       fni8h::launch_pdl(act_mul_vec<T, 16, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s);
   } else {
     fni8h::launch_pdl(row_scalar<T, QUANT ? 4 : 3, ACT>, dim3(g), dim3(kRowThreads), 0, st, xx,
-                      static_cast<const T*>(nullptr), static_cast<const T*>(nullptr), M, (int)I, 0.f, 0,
-                      QUANT ? static_cast<T*>(nullptr) : oo, static_cast<T*>(nullptr), q, s);
+                      static_cast<const T*>(nullptr), static_cast<const T*>(nullptr), M, (int)I, 0.f, 0, oo,
+                      static_cast<T*>(nullptr), q, s);
   }
   FNI8_CHECK_LAUNCH(QUANT ? "act_and_mul_quant_i8" : "act_and_mul");
   return FNI8_OK;
@@ -656,15 +658,15 @@ static int act_common(const void* x, int dtype, int act, int64_t M, int64_t I, v
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == FNI8_F16) {
     if (act == FNI8_ACT_SILU)
-      return quant ? act_dispatch<__half, FNI8_ACT_SILU, true>(x, M, I, nullptr, q, scale, s)
+      return quant ? act_dispatch<__half, FNI8_ACT_SILU, true>(x, M, I, out, q, scale, s)
                    : act_dispatch<__half, FNI8_ACT_SILU, false>(x, M, I, out, nullptr, nullptr, s);
-    return quant ? act_dispatch<__half, FNI8_ACT_GELU_TANH, true>(x, M, I, nullptr, q, scale, s)
+    return quant ? act_dispatch<__half, FNI8_ACT_GELU_TANH, true>(x, M, I, out, q, scale, s)
                  : act_dispatch<__half, FNI8_ACT_GELU_TANH, false>(x, M, I, out, nullptr, nullptr, s);
   }
   if (act == FNI8_ACT_SILU)
-    return quant ? act_dispatch<__nv_bfloat16, FNI8_ACT_SILU, true>(x, M, I, nullptr, q, scale, s)
+    return quant ? act_dispatch<__nv_bfloat16, FNI8_ACT_SILU, true>(x, M, I, out, q, scale, s)
                  : act_dispatch<__nv_bfloat16, FNI8_ACT_SILU, false>(x, M, I, out, nullptr, nullptr, s);
-  return quant ? act_dispatch<__nv_bfloat16, FNI8_ACT_GELU_TANH, true>(x, M, I, nullptr, q, scale, s)
+  return quant ? act_dispatch<__nv_bfloat16, FNI8_ACT_GELU_TANH, true>(x, M, I, out, q, scale, s)
                : act_dispatch<__nv_bfloat16, FNI8_ACT_GELU_TANH, false>(x, M, I, out, nullptr, nullptr, s);
 }
 
@@ -675,4 +677,10 @@ extern "C" int fni8_act_and_mul(const void* x, int dtype, int act, int64_t M, in
 extern "C" int fni8_act_and_mul_quant_i8(const void* x, int dtype, int act, int64_t M, int64_t I, int8_t* q,
                                          float* scale, void* stream) {
   return act_common(x, dtype, act, M, I, nullptr, q, scale, stream, true);
+}
+
+extern "C" int fni8_act_and_mul_dual(const void* x, int dtype, int act, int64_t M, int64_t I, void* out, int8_t* q,
+                                     float* scale, void* stream) {
+  if (M > 0 && out == nullptr) return fni8h::fail(FNI8_ERR_INVALID, "null output");
+  return act_common(x, dtype, act, M, I, out, q, scale, stream, true);
 }

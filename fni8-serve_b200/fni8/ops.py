@@ -28,11 +28,12 @@ from .qtensor import QTensor
 _DT = {torch.float16: nat.F16, torch.bfloat16: nat.BF16}
 _ACT = {"silu": nat.ACT_SILU, "gelu_tanh": nat.ACT_GELU_TANH, "gelu_pytorch_tanh": nat.ACT_GELU_TANH}
 
-# Fused RMSNorm -> int8 hand-off: fni8.rmsnorm can leave the int8 rows and scales of its
-# output on the tensor, so the fni8.linear that consumes it skips its own quantisation
-# pass. The side-car is only trusted while the tensor is unmodified (same storage, shape
-# and version counter).
+# Fused int8 hand-off: fni8.rmsnorm and fni8.act_and_mul can leave the int8 rows and
+# scales of their output on the tensor, so the fni8.linear that consumes it (QKV / gate_up
+# after the norm, down after the activation) skips its own quantisation pass. The side-car
+# is only trusted while the tensor is unmodified (same storage, shape and version counter).
 FUSE_NORM_QUANT = True
+FUSE_ACT_QUANT = True
 _SIDECAR_MIN_K = 512
 
 
@@ -197,8 +198,18 @@ def act_and_mul(x: torch.Tensor, act: str = "silu") -> torch.Tensor:
     x2 = x.reshape(-1, two_i).contiguous()
     M = x2.shape[0]
     out = torch.empty((M, I), dtype=x.dtype, device=x.device)
-    nat.call("fni8_act_and_mul", _vp(x2), dt, _ACT[act], M, I, _vp(out), _stream(x.device))
-    return out.reshape(*x.shape[:-1], I)
+    use_q = FUSE_ACT_QUANT and I >= _SIDECAR_MIN_K and I % 16 == 0
+    if use_q:
+        # the down projection that consumes the product finds its int8 rows ready
+        q = torch.empty((M, I), dtype=torch.int8, device=x.device)
+        s = torch.empty((M,), dtype=torch.float32, device=x.device)
+        nat.call("fni8_act_and_mul_dual", _vp(x2), dt, _ACT[act], M, I, _vp(out), _vp(q), _vp(s), _stream(x.device))
+    else:
+        nat.call("fni8_act_and_mul", _vp(x2), dt, _ACT[act], M, I, _vp(out), _stream(x.device))
+    y = out.reshape(*x.shape[:-1], I)
+    if use_q:
+        _attach_sidecar(y, q.reshape(*x.shape[:-1], I), s.reshape(x.shape[:-1]))
+    return y
 
 
 def act_and_mul_quant(x: torch.Tensor, act: str = "silu") -> tuple[torch.Tensor, torch.Tensor]:
@@ -262,7 +273,7 @@ def linear(x: torch.Tensor, qt: QTensor, bias: torch.Tensor | None = None, path:
     N = qt.data.shape[0]
     sc = _sidecar(x) if path == nat.PATH_AUTO else None
     if sc is not None:
-        return linear_q(sc[0], sc[1], qt, bias=bias, out_dtype=x.dtype)
+        return linear_q(sc[0], sc[1], qt, bias=bias, out_dtype=x.dtype).reshape(*x.shape[:-1], N)
     x2 = x.reshape(-1, K).contiguous()
     M = x2.shape[0]
     out = torch.empty((M, N), dtype=x.dtype, device=x.device)

@@ -105,6 +105,12 @@ FNI8_API int fni8_act_and_mul(const void* x, int dtype, int act, int64_t M, int6
  * down_proj in GatedMLP.forward, fni8serve/layers/mlp.py:39-40). */
 FNI8_API int fni8_act_and_mul_quant_i8(const void* x, int dtype, int act, int64_t M, int64_t I, int8_t* q, float* scale,
                               void* stream);
+/* Both at once: out[M, I] = act_and_mul(x) and its per-token int8 rows q[M, I] / scale[M]
+ * (the q of fni8_act_and_mul_quant_i8), in one pass over x. fni8.act_and_mul uses it to hand
+ * the int8 rows to the down projection that consumes `out` (GatedMLP.forward,
+ * fni8serve/layers/mlp.py:39-40). */
+FNI8_API int fni8_act_and_mul_dual(const void* x, int dtype, int act, int64_t M, int64_t I, void* out, int8_t* q,
+                                   float* scale, void* stream);
 
 /* ------------------------------------------------------------------ dense GEMM */
 /* Bytes of workspace fni8_gemm_w8a8* may use for an M x N x K problem (0 when none). */

@@ -43,6 +43,50 @@ def test_norm_to_linear_sidecar_is_invisible():
     assert torch.equal(fni8.linear(h, qt), fni8.linear(h.clone(), qt))
 
 
+@pytest.mark.parametrize("shape", [(2, 33, 4096), (48, 4096)])
+@pytest.mark.parametrize("act", ["silu", "gelu_tanh"])
+def test_act_to_down_sidecar_is_invisible(shape, act):
+    """fni8.act_and_mul writes the product and its int8 rows in one pass; the down
+    projection consumes the rows. The product equals the unfused kernel's, the down
+    output equals the unfused chain's exactly (3-D inputs keep their leading dims), and a
+    modified product is re-quantised."""
+    import fni8
+    from fni8 import ops
+
+    *lead, two_i = shape
+    I, N = two_i // 2, 640
+    x = torch.randn(*lead, two_i, generator=gen(3)).half().to(DEV)
+    wq, ws = qweight(N, I, 4)
+    qt = fni8.QTensor(wq.to(DEV), ws.to(DEV))
+    h = fni8.act_and_mul(x, act)
+    assert getattr(h, "_fni8_q", None) is not None
+    ops.FUSE_ACT_QUANT = False
+    try:
+        h_plain = fni8.act_and_mul(x, act)
+    finally:
+        ops.FUSE_ACT_QUANT = True
+    assert getattr(h_plain, "_fni8_q", None) is None
+    assert torch.equal(h, h_plain)
+    fused = fni8.linear(h, qt)
+    assert fused.shape == (*lead, N)
+    assert torch.equal(fused, fni8.linear(h_plain, qt))
+    h.add_(1)
+    assert torch.equal(fni8.linear(h, qt), fni8.linear(h.clone(), qt))
+
+
+def test_norm_to_linear_sidecar_keeps_leading_dims():
+    import fni8
+
+    B, S, K, N = 2, 17, 1024, 384
+    x = torch.randn(B, S, K, generator=gen(5)).half().to(DEV)
+    w = torch.ones(K, dtype=torch.float16, device=DEV)
+    wq, ws = qweight(N, K, 6)
+    qt = fni8.QTensor(wq.to(DEV), ws.to(DEV))
+    h = fni8.rmsnorm(x, w, 1e-6)
+    y = fni8.linear(h, qt)
+    assert y.shape == (B, S, N) and torch.equal(y, fni8.linear(h.clone(), qt))
+
+
 def test_decode_ops_capture_in_cuda_graph():
     """The reference engine captures decode in a CUDA graph (engine/cuda_graph.py); the
     ops must be capturable (no host sync, no allocation outside the caching allocator)."""

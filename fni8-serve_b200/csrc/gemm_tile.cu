@@ -9,9 +9,11 @@
 //               and, from one thread, issues tcgen05.mma.kind::i8 (M=128, N=BN, K=32;
 //               4 per 128-byte stage); tcgen05.commit frees smem stages and publishes
 //               finished accumulators.
-//   warps 2-5   epilogue: tcgen05.ld of one accumulator row per thread, fp32 dequant
-//               (+bias, +residual), rounding to fp16/bf16 (or raw int32), global stores.
-//               The other accumulator buffer is being filled meanwhile.
+//   warps 2-9   epilogue: tcgen05.ld of one accumulator row per thread, fp32 dequant
+//               (+bias, +residual), rounding to fp16/bf16 (or raw int32), global stores;
+//               two warps per TMEM lane quarter, each taking half of the BN columns, so
+//               the epilogue keeps up with short K loops (e.g. the MoE down projection,
+//               K=768). The other accumulator buffer is being filled meanwhile.
 // Tiles are visited in bands of kGroupM m-tiles so a wave of 148 CTAs reuses the same
 // A rows and W columns out of the 126 MB L2.
 //
@@ -40,7 +42,9 @@ namespace tile {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes == int8 elements per stage along K
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // two per TMEM lane quarter
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kMaxSeg = fni8h::kTileMaxSeg;
 constexpr int kGroupM = 16;
 constexpr int kL2AheadUnits = 16;  // weight k-blocks per CTA prefetched into L2 before the PDL wait
@@ -76,9 +80,9 @@ struct Cfg {
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 512;
   static constexpr int SEG_BYTES = (kMaxSeg + 1 + 3 * kMaxSeg) * 4;
-  // per epilogue warp, two 32 x 32 16-bit output staging buffers for the TMA store
+  // per epilogue warp, one 32 x 32 16-bit output staging buffer for the TMA store
   static constexpr int STG_BUF = 32 * 32 * 2;
-  static constexpr int STG_BYTES = 4 * 2 * STG_BUF;
+  static constexpr int STG_BYTES = kEpiWarps * STG_BUF;
   static constexpr int STG_OFF = (STAGES * STAGE + BAR_BYTES + SEG_BYTES + 1023) / 1024 * 1024;  // swizzle-aligned
   static constexpr int SMEM = 1024 + STG_OFF + STG_BYTES + 2 * BN * 4;  // + per-tile column scales, bias
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
@@ -220,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], PAIR ? 8 : 4);  // one arrive per epilogue warp (of both CTAs)
+      mbar_init(&tempty[b], PAIR ? 2 * kEpiWarps : kEpiWarps);  // one arrive per epilogue warp (of both CTAs)
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -423,18 +427,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    // 4 warps; warp q reads TMEM lanes [32q, 32q+32) = rows of the tile, one per thread.
+    // 8 warps; warp w reads TMEM lanes [32q, 32q+32), q = w % 4 (rows of the tile, one
+    // per thread), and the columns [h*BN/2, (h+1)*BN/2) of its half h = (w - 2) / 4.
     // Per tile the column scales (and bias) are staged in shared memory; their loads are
     // issued before the accumulator wait so they overlap the MMA. 16-bit outputs leave
-    // through 64B-swizzled 32 x 32 staging buffers and TMA stores.
+    // through a 64B-swizzled 32 x 32 staging buffer per warp and TMA stores.
     const int q = warp & 3;
+    const int ew = warp - 2;                     // 0..7
+    const int c_beg = (ew >> 2) * (BN / 2);      // this warp's columns of the tile
     const int row_local = q * 32 + lane;
-    const int et = threadIdx.x - 64;  // 0..127 across the epilogue warps
+    const int et = threadIdx.x - 64;  // 0..255 across the epilogue warps
     float* s_ws = reinterpret_cast<float*>(stg + C::STG_BYTES);
     float* s_bias = s_ws + BN;
     int acc = 0;
     uint32_t aph = 0;
-    int sb = 0;  // staging buffer of this warp used next
     if (tma_store && lane == 0) tma_prefetch_desc(&tmOut);
     for (int t = t0; t < total; t += tstep) {
       const TileCoord tc = decode_tile<GROUPED, C::BMT>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
@@ -445,32 +451,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row = static_cast<int64_t>(row0) + row_local;
       const int nb0 = tc.n_blk * BN;
       const float* wsc = epi.w_scale + static_cast<int64_t>(tc.expert) * N;
-      float wreg[BN / 128], breg[BN / 128];
+      static_assert(BN <= kEpiThreads, "one column scale per epilogue thread");
+      float wreg = 0.0f, breg = 0.0f;
       float a_s = 0.0f;
       if (epi.mode != kOutI32) {
-#pragma unroll
-        for (int i = 0; i < BN / 128; ++i) {
-          const int col = nb0 + et + i * 128;
-          wreg[i] = col < N ? __ldg(wsc + col) : 0.0f;
-          breg[i] = 0.0f;
-          if (epi.bias != nullptr && col < N)
-            breg[i] = epi.mode == kOutF16 ? __half2float(static_cast<const __half*>(epi.bias)[col])
-                                          : __bfloat162float(static_cast<const __nv_bfloat16*>(epi.bias)[col]);
+        const int col = nb0 + et;
+        if (et < BN && col < N) {
+          wreg = __ldg(wsc + col);
+          if (epi.bias != nullptr)
+            breg = epi.mode == kOutF16 ? __half2float(static_cast<const __half*>(epi.bias)[col])
+                                       : __bfloat162float(static_cast<const __nv_bfloat16*>(epi.bias)[col]);
         }
         if (valid) a_s = __ldg(epi.a_scale + row);
       }
       int ok = 0;
       if (lane == 0) ok = mbar_wait(&tfull[acc], aph, &g_status, kCodeEpilogue) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!named_bar_and(2, 128, ok)) break;  // also: every reader of the previous tile's scales is done
+      // also: every reader of the previous tile's scales is done
+      if (!named_bar_and(2, kEpiThreads, ok)) break;
       tc_fence_after();
       if (epi.mode != kOutI32) {
-#pragma unroll
-        for (int i = 0; i < BN / 128; ++i) {
-          s_ws[et + i * 128] = wreg[i];
-          s_bias[et + i * 128] = breg[i];
+        if (et < BN) {
+          s_ws[et] = wreg;
+          s_bias[et] = breg;
         }
-        named_bar_sync(2, 128);
+        named_bar_sync(2, kEpiThreads);
       }
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       // TMA store of whole 32-row slabs; a slab cut by a segment end (grouped) or any
@@ -478,15 +483,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool slab_tma = tma_store && epi.residual == nullptr &&
                             (!GROUPED || rows_here - q * 32 >= 32) && q * 32 < rows_here;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = c_beg; c < c_beg + BN / 2; c += 32) {
         uint32_t r[32];
         tmem_ld32(tbase + static_cast<uint32_t>(c), r);
         tmem_ld_wait();
         const int n0 = nb0 + c;
         if (n0 >= N) continue;
         if (slab_tma) {
-          uint8_t* buf = stg + (q * 2 + sb) * C::STG_BUF;
-          if (lane == 0) bulk_wait_group_read<1>();  // the store issued from this buffer 2 chunks ago
+          uint8_t* buf = stg + ew * C::STG_BUF;
+          if (lane == 0) bulk_wait_group_read<0>();  // the previous store from this buffer has read it
           __syncwarp();
 #pragma unroll
           for (int j8 = 0; j8 < 4; ++j8) {  // 8 outputs = one 16-byte chunk of this row
@@ -516,7 +521,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_store_2d(&tmOut, buf, n0, row0 + q * 32);
             bulk_commit_group();
           }
-          sb ^= 1;
         } else if (valid) {
           if (epi.mode == kOutI32) store_chunk_i32(epi, r, row, n0, N, vec_ok != 0);
           else if (epi.mode == kOutF16) store_chunk<__half>(epi, r, row, n0, N, a_s, s_ws + c, s_bias + c, vec_ok != 0);

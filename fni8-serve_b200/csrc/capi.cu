@@ -150,7 +150,12 @@ static int64_t splitk_auto_max_m() {
 static int pick_path(int path, int64_t M, size_t ws_bytes, int64_t N, int64_t K) {
   if (path == FNI8_PATH_TILE || path == FNI8_PATH_STREAM || path == FNI8_PATH_SPLITK) return path;
   if (M <= stream_auto_max_m() && ws_bytes >= stream_workspace_bytes(M, N, K)) return FNI8_PATH_STREAM;
-  if (M <= splitk_auto_max_m() && splitk_supported(M, N, K) && ws_bytes >= splitk_workspace_bytes(M, N, K))
+  // Above 64 tokens a weight matrix with at least one 256-row tile per SM (an LM head:
+  // N = 151936) streams faster through the tile kernel, whose MMAs consume twice the
+  // weight bytes per instruction (measured on B200).
+  const bool wide = M > 64 && (N + 255) / 256 >= num_sms(current_device());
+  if (M <= splitk_auto_max_m() && !wide && splitk_supported(M, N, K) &&
+      ws_bytes >= splitk_workspace_bytes(M, N, K))
     return FNI8_PATH_SPLITK;
   return FNI8_PATH_TILE;
 }

@@ -87,6 +87,14 @@ int encode_tmap_2d_i8(CUtensorMap* map, const void* base, uint64_t inner, uint64
   return encode(map, base, 2, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+int encode_tmap_2d_u8_sw64(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                           uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  return encode(map, base, 2, dims, strides, box, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 int encode_tmap_3d_i8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
                       uint64_t stride2, uint32_t box0, uint32_t box1) {
   const cuuint64_t dims[3] = {d0, d1, d2};
@@ -214,18 +222,22 @@ extern "C" int fni8_device_status(int* code_out) {
   if (code_out == nullptr) return fail(FNI8_ERR_INVALID, "null code_out");
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_status(e, "cudaDeviceSynchronize");
-  int a = 0, b = 0, c = 0, d = 0;
-  if (int s = tile_status_read_and_clear(&a)) return s;
-  if (int s = stream_status_read_and_clear(&b)) return s;
-  if (int s = skinny_status_read_and_clear(&c)) return s;
-  if (int s = splitk_status_read_and_clear(&d)) return s;
-  *code_out = a != 0 ? a : (b != 0 ? b : (c != 0 ? c : d));
+  int codes[5] = {0, 0, 0, 0, 0};
+  if (int s = tile_status_read_and_clear(&codes[0])) return s;
+  if (int s = stream_status_read_and_clear(&codes[1])) return s;
+  if (int s = skinny_status_read_and_clear(&codes[2])) return s;
+  if (int s = splitk_status_read_and_clear(&codes[3])) return s;
+  if (int s = w4a8_status_read_and_clear(&codes[4])) return s;
+  *code_out = 0;
+  for (int v : codes)
+    if (*code_out == 0) *code_out = v;
   return *code_out == 0 ? FNI8_OK : fail(FNI8_ERR_DEVICE_TIMEOUT, "device watchdog code 0x%x", *code_out);
 }
 
 extern "C" size_t fni8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   const size_t a = stream_workspace_bytes(M, N, K), b = splitk_workspace_bytes(M, N, K);
-  return a > b ? a : b;
+  const size_t ab = a > b ? a : b, c = w4a8_workspace_bytes(M, N, K);
+  return ab > c ? ab : c;
 }
 
 extern "C" int fni8_workspace_init(void* workspace, size_t bytes, void* stream) {
@@ -304,4 +316,41 @@ extern "C" int fni8_linear_w8a8(const void* x, int dtype, const int8_t* w, const
                                 void* workspace, size_t workspace_bytes, void* stream) {
   return fni8_linear_w8a8_ex(x, dtype, w, w_scale, bias, out, M, N, K, q_scratch, s_scratch, FNI8_PATH_AUTO,
                              workspace, workspace_bytes, stream);
+}
+
+// ------------------------------------------------------------------ W4A8 (per_group_i4, int4)
+static int check_w4(const int8_t* a, const float* a_scale, const uint8_t* w4, const float* w_scale, const void* out,
+                    int out_dtype, int64_t M, int64_t N, int64_t K, int64_t group_size) {
+  if (M < 0 || N <= 0 || K <= 0) return fail(FNI8_ERR_INVALID, "bad W4A8 shape M=%lld N=%lld K=%lld", (long long)M,
+                                              (long long)N, (long long)K);
+  if (group_size != 128) return fail(FNI8_ERR_UNSUPPORTED, "W4A8 takes group_size 128 (got %lld)", (long long)group_size);
+  if (K % 128 != 0) return fail(FNI8_ERR_UNSUPPORTED, "W4A8 takes K a multiple of 128 (got %lld)", (long long)K);
+  if (M >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31))
+    return fail(FNI8_ERR_UNSUPPORTED, "GEMM dimensions must be < 2^31");
+  if (out_dtype != FNI8_F16 && out_dtype != FNI8_BF16) return fail(FNI8_ERR_INVALID, "out_dtype %d", out_dtype);
+  if (M > 0 && (a == nullptr || a_scale == nullptr || w4 == nullptr || w_scale == nullptr || out == nullptr))
+    return fail(FNI8_ERR_INVALID, "null W4A8 operand");
+  return FNI8_OK;
+}
+
+extern "C" int fni8_gemm_w4a8(const int8_t* a, const float* a_scale, const uint8_t* w4, const float* w_scale,
+                              int64_t group_size, const void* bias, void* out, int out_dtype, int64_t M, int64_t N,
+                              int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int s = check_w4(a, a_scale, w4, w_scale, out, out_dtype, M, N, K, group_size)) return s;
+  if (M == 0) return FNI8_OK;
+  return w4a8_gemm(a, a_scale, w4, w_scale, bias, out, out_dtype == FNI8_F16 ? 0 : 1, M, N, K, workspace,
+                   workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fni8_linear_w4a8(const void* x, int dtype, const uint8_t* w4, const float* w_scale, int64_t group_size,
+                                const void* bias, void* out, int64_t M, int64_t N, int64_t K, int8_t* q_scratch,
+                                float* s_scratch, void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != FNI8_F16 && dtype != FNI8_BF16) return fail(FNI8_ERR_INVALID, "dtype %d: expected F16 or BF16", dtype);
+  if (M > 0 && (x == nullptr || q_scratch == nullptr || s_scratch == nullptr))
+    return fail(FNI8_ERR_INVALID, "null linear input or scratch");
+  if (int s = check_w4(M > 0 ? q_scratch : nullptr, s_scratch, w4, w_scale, out, dtype, M, N, K, group_size)) return s;
+  if (M == 0) return FNI8_OK;
+  if (int s = fni8_quantize_rows_i8(x, dtype, M, K, q_scratch, s_scratch, stream)) return s;
+  return w4a8_gemm(q_scratch, s_scratch, w4, w_scale, bias, out, dtype == FNI8_F16 ? 0 : 1, M, N, K, workspace,
+                   workspace_bytes, static_cast<cudaStream_t>(stream));
 }

@@ -421,6 +421,9 @@ int encode_tmap_2d_16_sw(CUtensorMap* map, const void* base, bool bf16, uint64_t
 // 16-bit elements (fp16 / bf16), no swizzle: rows of box_inner elements land contiguously.
 int encode_tmap_2d_16(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64_t outer,
                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+// 8-bit elements with the 64-byte swizzle (box rows of 64 B: packed int4 weight tiles).
+int encode_tmap_2d_u8_sw64(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                           uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
 int encode_tmap_3d_i8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1,
                       uint64_t stride2, uint32_t box0, uint32_t box1);
 }  // namespace fni8h

@@ -49,4 +49,12 @@ int splitk_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const fl
                 size_t ws_bytes, cudaStream_t st);
 int splitk_status_read_and_clear(int* code);
 
+// W4A8 decode-shaped GEMM (gemm_w4a8.cu): packed int4 weights [N, K/2] with fp32 scales
+// per 128-channel group [N, K/128]; 64 tokens per launch.
+constexpr int64_t kW4ChunkM = 64;
+size_t w4a8_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int w4a8_gemm(const int8_t* a, const float* a_scale, const uint8_t* w4, const float* w_scale, const void* bias,
+              void* out, int out_mode, int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes, cudaStream_t st);
+int w4a8_status_read_and_clear(int* code);
+
 }  // namespace fni8h

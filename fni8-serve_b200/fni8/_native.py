@@ -37,6 +37,8 @@ SIGNATURES: dict[str, tuple] = {
     "fni8_act_and_mul": (_i, [_p, _i, _i, _i64, _i64, _p, _p]),
     "fni8_act_and_mul_quant_i8": (_i, [_p, _i, _i, _i64, _i64, _p, _p, _p]),
     "fni8_act_and_mul_dual": (_i, [_p, _i, _i, _i64, _i64, _p, _p, _p, _p]),
+    "fni8_gemm_w4a8": (_i, [_p, _p, _p, _p, _i64, _p, _p, _i, _i64, _i64, _i64, _p, _sz, _p]),
+    "fni8_linear_w4a8": (_i, [_p, _i, _p, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _p, _p, _sz, _p]),
     "fni8_gemm_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "fni8_workspace_init": (_i, [_p, _sz, _p]),
     "fni8_gemm_w8a8": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i64, _i64, _i64, _p, _sz, _p]),

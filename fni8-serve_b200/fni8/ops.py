@@ -231,7 +231,7 @@ def act_and_mul_quant(x: torch.Tensor, act: str = "silu") -> tuple[torch.Tensor,
 def _check_weight(qt: QTensor, x_dev: torch.device, K: int, what: str) -> None:
     if qt.scheme != "per_row_i8":
         raise NotImplementedError(f"fni8.{what}: scheme {qt.scheme!r} is not implemented on sm_100a "
-                                  "(per_row_i8 only)")
+                                  "(per_row_i8 here; per_group_i4 through fni8.linear)")
     if qt.data.dtype != torch.int8 or qt.data.dim() != 2:
         raise TypeError(f"fni8.{what}: per_row_i8 data must be a 2-D int8 tensor")
     if qt.data.shape[1] != K:
@@ -262,11 +262,43 @@ def linear_q(q: torch.Tensor, scale: torch.Tensor, qt: QTensor, bias: torch.Tens
     return out.reshape(*q.shape[:-1], N)
 
 
+def _linear_w4a8(x: torch.Tensor, qt: QTensor, bias: torch.Tensor | None) -> torch.Tensor:
+    """per_group_i4 / int4 weights (W4A8): packed data [N, K/2] uint8, scale [N, K/g] fp32."""
+    if qt.codebook not in (None, "int4"):
+        raise NotImplementedError(f"fni8.linear: per_group_i4 codebook {qt.codebook!r} has no integer GEMM "
+                                  "(fni8-serve routes NF4 weights to its fp16 fallback)")
+    dt = _act_dtype(x, "linear")
+    K = x.shape[-1]
+    if qt.data.dim() != 2 or qt.data.shape[1] * 2 != K or qt.data.dtype not in (torch.uint8, torch.int8):
+        raise ValueError(f"fni8.linear: per_group_i4 data {tuple(qt.data.shape)} does not pack K={K}")
+    if qt.data.device != x.device or qt.scale.device != x.device:
+        raise RuntimeError("fni8.linear: weight and activation are on different devices")
+    N = qt.data.shape[0]
+    gs = int(qt.group_size or 0)
+    ws_ = qt.scale.to(torch.float32).contiguous()
+    if gs <= 0 or K % gs or ws_.numel() != N * (K // gs):
+        raise ValueError(f"fni8.linear: per_group_i4 scale {tuple(qt.scale.shape)} does not match N={N}, "
+                         f"K={K}, group_size={gs}")
+    x2 = x.reshape(-1, K).contiguous()
+    M = x2.shape[0]
+    out = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty((M,), dtype=torch.float32, device=x.device)
+    b = bias.to(x.dtype).contiguous() if bias is not None else None
+    ws, wsb = _ws(x.device)
+    nat.call("fni8_linear_w4a8", _vp(x2), dt, _vp(qt.data.contiguous()), _vp(ws_), gs, _vp(b), _vp(out), M, N, K,
+             _vp(q), _vp(s), ws, wsb, _stream(x.device))
+    return out.reshape(*x.shape[:-1], N)
+
+
 def linear(x: torch.Tensor, qt: QTensor, bias: torch.Tensor | None = None, path: int = nat.PATH_AUTO) -> torch.Tensor:
     """fni8.linear: per-token int8 quantisation of x, int8 GEMM, dequant epilogue (+bias).
 
-    `path` (not in the reference signature) forces a kernel; the default picks by shape."""
+    `path` (not in the reference signature) forces a kernel; the default picks by shape.
+    per_group_i4 / int4 weights run the W4A8 GEMM."""
     _need_cuda(x, "linear")
+    if qt.scheme == "per_group_i4":
+        return _linear_w4a8(x, qt, bias)
     dt = _act_dtype(x, "linear")
     K = x.shape[-1]
     _check_weight(qt, x.device, K, "linear")

@@ -163,6 +163,24 @@ FNI8_API int fni8_linear_w8a8_ex(const void* x, int dtype, const int8_t* w, cons
                                  void* out, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
                                  int path, void* workspace, size_t workspace_bytes, void* stream);
 
+/* W4A8: int8 activations a[M, K] (+ per-token scale) x 4-bit weights — the per_group_i4 /
+ * int4 QTensor of fni8serve (layers/linear.py:33-45, convert.py:69-80): w4[N, K/2] bytes,
+ * element 2j of a row in the low nibble of byte j, signed two's complement; w_scale[N, K/g]
+ * fp32 per group of g input channels. out[m, n] = dtype((sum_g float(acc_g[m, n]) *
+ * w_scale[n, g]) * a_scale[m] (+ bias[n])), acc_g the exact int32 sum over group g.
+ * Takes group_size 128 and K a multiple of 128 (FNI8_ERR_UNSUPPORTED otherwise); the
+ * workspace is the zero-maintained GEMM workspace (fni8_gemm_workspace_bytes). The fp32
+ * sum over the groups of a split K range is formed per K slice, then over the slices in
+ * order: the result can differ from a one-pass sum in the last fp16 bit. */
+FNI8_API int fni8_gemm_w4a8(const int8_t* a, const float* a_scale, const uint8_t* w4, const float* w_scale,
+                            int64_t group_size, const void* bias, void* out, int out_dtype, int64_t M, int64_t N,
+                            int64_t K, void* workspace, size_t workspace_bytes, void* stream);
+/* fni8.linear(x, qt, bias=) for per_group_i4 / int4 weights: per-token int8 quantisation of
+ * x into q_scratch / s_scratch, then fni8_gemm_w4a8. */
+FNI8_API int fni8_linear_w4a8(const void* x, int dtype, const uint8_t* w4, const float* w_scale, int64_t group_size,
+                              const void* bias, void* out, int64_t M, int64_t N, int64_t K, int8_t* q_scratch,
+                              float* s_scratch, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------ MoE */
 /* Router scores -> top-k (SparseMoE.forward routing, fni8serve/models/moe.py:65-95):
  * softmax over all E (or sigmoid + optional selection bias added for the choice only),

@@ -16,6 +16,8 @@ Every output below is computed by fni8-serve's own modules on CPU:
     layers/norm.py RMSNorm (CPU path)          -> rmsnorm.npz
     layers/activation.py SiluAndMul/GeluAndMul -> act.npz
     layers/linear.py LinearW8A8 (fp16 fallback) -> linear.npz
+    layers/linear.py LinearW8A8 with per_group_i4 / int4 weights (its weight
+        reconstruction and fp16 fallback)      -> linear_i4.npz
     models/weights.py to_qtensor/merge_qtensor -> weights.npz
     models/moe.py SparseMoE (softmax and sigmoid+group-limited routing) -> moe_*.npz
     tests/test_layers.py::_i8 and tests/test_smoke.py::_i8 (the reference tests' own
@@ -132,6 +134,25 @@ def gen_linear(L) -> dict:
     return out
 
 
+def gen_linear_i4(L) -> dict:
+    """LinearW8A8 on CPU with 4-bit weights: _dequant_weight (linear.py:33-45) and the fp16
+    fallback forward. The packed codes and scales come from the oracle's int4 quantiser
+    (the converter's quantize_lowbit lives in the absent fni8 package)."""
+    sys.path.insert(0, REPO)
+    from oracle import w8a8_oracle as O
+
+    g = torch.Generator().manual_seed(404)
+    M, K, N, gs = 16, 512, 192, 128
+    w = 0.02 * torch.randn(N, K, generator=g)
+    packed, scale = O.quantize_weight_i4(w, gs)
+    qt = L.fni8.QTensor(packed, scale, scheme="per_group_i4", group_size=gs, codebook="int4")
+    x = torch.randn(M, K, generator=g).to(torch.float16)
+    bias = (0.1 * torch.randn(N, generator=g)).to(torch.float16)
+    lin = L.linear.LinearW8A8(qt, bias)
+    return {"x": _np(x), "packed": _np(packed), "scale": _np(scale), "bias": _np(bias), "group_size": np.int64(gs),
+            "in_features": np.int64(lin.in_features), "w_ref": _np(L.linear._dequant_weight(qt)), "y_ref": _np(lin(x))}
+
+
 def gen_weights(L) -> dict:
     g = torch.Generator().manual_seed(404)
     sd = {f"p.{n}_proj.weight": (0.05 * torch.randn(*s, generator=g)).to(torch.float16)
@@ -214,6 +235,7 @@ def main() -> int:
     torch.set_num_threads(4)
     L = _setup(a.reference)
     jobs = {"rmsnorm": lambda: gen_rmsnorm(L), "act": lambda: gen_act(L), "linear": lambda: gen_linear(L),
+            "linear_i4": lambda: gen_linear_i4(L),
             "weights": lambda: gen_weights(L), "i8_fixture": lambda: gen_i8_fixture(a.reference, L),
             "moe_softmax": lambda: gen_moe(L, "softmax"), "moe_sigmoid": lambda: gen_moe(L, "sigmoid")}
     for name, fn in jobs.items():

@@ -326,9 +326,15 @@ def test_zero_rows_and_errors():
     with pytest.raises(Fni8Error, match="multiple of 16"):
         bad = fni8.QTensor(torch.zeros(32, 40, dtype=torch.int8, device=DEV), torch.ones(32, device=DEV))
         fni8.linear(torch.zeros(4, 40, dtype=torch.float16, device=DEV), bad)
-    with pytest.raises(NotImplementedError):
-        fni8.linear(torch.zeros(4, 64, dtype=torch.float16, device=DEV),
-                    fni8.QTensor(qt.data, qt.scale, scheme="per_group_i4", group_size=32, codebook="int4"))
+    packed = torch.zeros(32, 64, dtype=torch.uint8, device=DEV)  # 4-bit weights for K = 128
+    with pytest.raises(NotImplementedError):  # NF4 has no integer GEMM (fni8-serve uses its fp16 path)
+        fni8.linear(torch.zeros(4, 128, dtype=torch.float16, device=DEV),
+                    fni8.QTensor(packed, torch.ones(32, 4, device=DEV), scheme="per_group_i4", group_size=32,
+                                 codebook="nf4"))
+    with pytest.raises(Fni8Error, match="group_size 128"):
+        fni8.linear(torch.zeros(4, 128, dtype=torch.float16, device=DEV),
+                    fni8.QTensor(packed, torch.ones(32, 4, device=DEV), scheme="per_group_i4", group_size=32,
+                                 codebook="int4"))
     assert fni8.device_status() == 0
 
 

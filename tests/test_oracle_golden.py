@@ -116,3 +116,21 @@ def test_moe_plan_is_stable_grouping():
     assert counts.tolist() == [3, 2, 2] and offsets.tolist() == [0, 3, 5, 7]
     assert sor.tolist() == [1, 2, 7, 3, 6, 0, 4]
     assert ros[5] == -1 and all(ros[s] == r for r, s in enumerate(sor.tolist()))
+
+
+def test_w4a8_oracle_against_reference_i4_path(golden):
+    """per_group_i4 / int4 weights: the oracle's unpack + two's-complement decode equals the
+    reference's own weight reconstruction (layers/linear.py:33-45) bit for bit, and the
+    oracle's W4A8 linear stays within the reference tests' bound of its fp16 fallback."""
+    g = golden("linear_i4")
+    packed = torch.from_numpy(g["packed"])
+    scale = torch.from_numpy(g["scale"])
+    gs = int(g["group_size"])
+    assert int(g["in_features"]) == 2 * packed.shape[1]
+    assert torch.equal(O.dequant_weight_i4_fallback(packed, scale, gs), torch.from_numpy(g["w_ref"]))
+    assert torch.equal(O.pack_i4(O.unpack_i4(packed)), packed)
+    x = torch.from_numpy(g["x"])
+    y = O.linear_w4a8(x, packed, scale, gs, bias=torch.from_numpy(g["bias"]))
+    ref = torch.from_numpy(g["y_ref"]).float()
+    cos = torch.nn.functional.cosine_similarity(y.float().flatten(), ref.flatten(), dim=0).item()
+    assert cos >= 0.99, cos

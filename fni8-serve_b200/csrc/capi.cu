@@ -145,11 +145,12 @@ static int64_t stream_auto_max_m() {
 }
 
 // Largest M the AUTO choice sends to the split-K kernel: measured on B200, it beats the
-// tile kernel up to 128 tokens (FNI8_SPLITK_AUTO_MAX_M overrides it for measurements).
+// tile kernel up to 256 tokens whenever its grid fits on the GPU in one wave
+// (FNI8_SPLITK_AUTO_MAX_M overrides it for measurements).
 static int64_t splitk_auto_max_m() {
   static int64_t m = [] {
     const char* e = getenv("FNI8_SPLITK_AUTO_MAX_M");
-    const long v = e ? atol(e) : 128;
+    const long v = e ? atol(e) : 256;
     return (int64_t)(v < 0 ? 0 : (v > kSplitkMaxM ? kSplitkMaxM : v));
   }();
   return m;
@@ -162,8 +163,10 @@ static int pick_path(int path, int64_t M, size_t ws_bytes, int64_t N, int64_t K)
   // N = 151936) streams faster through the tile kernel, whose MMAs consume twice the
   // weight bytes per instruction (measured on B200).
   const bool wide = M > 64 && (N + 255) / 256 >= num_sms(current_device());
+  // Above 128 tokens (one CTA per SM) a split-K grid that needs a second wave of clusters
+  // loses to the tile kernel (measured: gate_up at M = 256, 192 weight tiles).
   if (M <= splitk_auto_max_m() && !wide && splitk_supported(M, N, K) &&
-      ws_bytes >= splitk_workspace_bytes(M, N, K))
+      ws_bytes >= splitk_workspace_bytes(M, N, K) && (M <= 128 || splitk_one_wave(M, N, K)))
     return FNI8_PATH_SPLITK;
   return FNI8_PATH_TILE;
 }

@@ -374,10 +374,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (n < N) {
         const float wsn = __ldg(w_scale + n);
         const float bn = bias != nullptr ? to_f32<T>(bias[n]) : 0.0f;
+        // every scale is read before the first store (a shared-memory load issued after a
+        // store it might alias waits for that store)
+        float sc[NT];
+#pragma unroll
+        for (int m = 0; m < NT; ++m) sc[m] = s_scale[m < M ? m : 0];
 #pragma unroll
         for (int m = 0; m < NT; ++m) {
           if (m < M) {
-            float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(acc[m])), s_scale[m]), wsn);
+            float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(acc[m])), sc[m]), wsn);
             if (bias != nullptr) v = __fadd_rn(v, bn);
             out[static_cast<int64_t>(m) * N + n] = from_f32<T>(v);
           }

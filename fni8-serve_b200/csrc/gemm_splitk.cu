@@ -35,7 +35,11 @@ constexpr int kThreads = 192;
 constexpr int BNW = 128;  // weight rows per tile (MMA M)
 constexpr int BK = 128;   // K elements per stage
 constexpr int kMaxStages = 8;
-constexpr int kL2Ahead = 16;  // weight k-blocks per CTA pulled into L2 before the dependency wait
+// Weight k-blocks per CTA pulled into L2 (beyond the ring) before the dependency wait: none
+// by default. Measured on B200 in chains of decode GEMMs, early prefetch of the next
+// kernel's weights queues ahead of the running kernel's last loads and partial-sum stores
+// and delays it more than the prefetch saves.
+constexpr int kL2Ahead = 0;
 constexpr int kBarBytes = 256;
 constexpr int kAsBytes = 1024;  // per-token activation scales of up to 256 tokens
 
@@ -67,7 +71,11 @@ struct Epi {
   const void* residual;  // [M, N] or null
   void* out;             // [M, N]
   int mode;
-  int vec;  // fp16/bf16 out, no residual, rows 16-byte aligned: stage the tile, store 16 B per thread
+  int vec;      // fp16/bf16 out, no residual, rows 16-byte aligned: stage the tile, store 16 B per thread
+  int l2ahead;  // weight k-blocks beyond the ring pulled into L2 before the dependency wait
+  // when the next kernel is released: 0 at entry, 1 once this CTA's last load is issued,
+  // 2 once its partial sums are published (its accumulator is complete when unsplit)
+  int trigger;
 };
 
 template <int NT>
@@ -81,58 +89,71 @@ struct Cfg {
 
 // out[m0 + j, n] for the CNT accumulator values of weight row n, tokens m0 + j < mlim,
 // straight to global memory (int32 output, residual add, or unaligned rows). s_as holds
-// the per-token scales in shared memory; residual values are all loaded before the first
-// store (a load issued after a store it might alias would wait for that store).
+// the per-token scales in shared memory. Every load (scales, residual values, the epilogue
+// parameters) is issued before the first store and every value is computed before it: a
+// load issued after a store that might alias it waits for that store, which would cost a
+// memory round trip per column.
 template <typename T, int CNT>
 __device__ __forceinline__ void emit_batch(const Epi& epi, const uint32_t (&acc)[CNT], int m0, int mlim, int n, int N,
                                            float wsn, float bn, const float* s_as) {
-  if (epi.mode == kOutI32) {
+  const int mode = epi.mode;
+  const bool has_bias = epi.bias != nullptr;
+  const T* res = static_cast<const T*>(epi.residual);
+  if (mode == kOutI32) {
     int32_t* o = static_cast<int32_t*>(epi.out);
 #pragma unroll
     for (int j = 0; j < CNT; ++j)
       if (m0 + j < mlim) o[static_cast<int64_t>(m0 + j) * N + n] = static_cast<int32_t>(acc[j]);
     return;
   }
-  float rs[CNT];
-  if (epi.residual != nullptr) {
-    const T* r = static_cast<const T*>(epi.residual);
-#pragma unroll
-    for (int j = 0; j < CNT; ++j) rs[j] = m0 + j < mlim ? to_f32<T>(r[static_cast<int64_t>(m0 + j) * N + n]) : 0.0f;
-  }
   T* o = static_cast<T*>(epi.out);
+  float sa[CNT], rs[CNT];
+#pragma unroll
+  for (int j = 0; j < CNT; ++j) sa[j] = s_as[m0 + j < mlim ? m0 + j : m0];
+#pragma unroll
+  for (int j = 0; j < CNT; ++j)
+    rs[j] = (res != nullptr && m0 + j < mlim) ? to_f32<T>(res[static_cast<int64_t>(m0 + j) * N + n]) : 0.0f;
+  T h[CNT];
 #pragma unroll
   for (int j = 0; j < CNT; ++j) {
-    if (m0 + j < mlim) {
-      float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(acc[j])), s_as[m0 + j]), wsn);
-      if (epi.bias != nullptr) v = __fadd_rn(v, bn);
-      if (epi.residual != nullptr) v = __fadd_rn(v, rs[j]);
-      o[static_cast<int64_t>(m0 + j) * N + n] = from_f32<T>(v);
-    }
+    float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(acc[j])), sa[j]), wsn);
+    if (has_bias) v = __fadd_rn(v, bn);
+    if (res != nullptr) v = __fadd_rn(v, rs[j]);
+    h[j] = from_f32<T>(v);
   }
+#pragma unroll
+  for (int j = 0; j < CNT; ++j)
+    if (m0 + j < mlim) o[static_cast<int64_t>(m0 + j) * N + n] = h[j];
 }
 
 // Same values into the shared-memory output tile stage[m - m_base][128] (row n of the
-// weight tile is column trow), for the coalesced copy-out.
+// weight tile is column trow), for the coalesced copy-out; loads before stores likewise.
 template <typename T, int CNT>
-__device__ __forceinline__ void stage_batch(const Epi& epi, const uint32_t (&acc)[CNT], int m0, int mlim, int m_base,
-                                            T* stage, int trow, float wsn, float bn, const float* s_as) {
+__device__ __forceinline__ void stage_batch(const uint32_t (&acc)[CNT], int m0, int mlim, int m_base, T* stage,
+                                            int trow, float wsn, float bn, bool has_bias, const float* s_as) {
+  float sa[CNT];
+#pragma unroll
+  for (int j = 0; j < CNT; ++j) sa[j] = s_as[m0 + j < mlim ? m0 + j : m0];
+  T h[CNT];
 #pragma unroll
   for (int j = 0; j < CNT; ++j) {
-    if (m0 + j < mlim) {
-      float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(acc[j])), s_as[m0 + j]), wsn);
-      if (epi.bias != nullptr) v = __fadd_rn(v, bn);
-      stage[(m0 + j - m_base) * BNW + trow] = from_f32<T>(v);
-    }
+    float v = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(acc[j])), sa[j]), wsn);
+    if (has_bias) v = __fadd_rn(v, bn);
+    h[j] = from_f32<T>(v);
   }
+#pragma unroll
+  for (int j = 0; j < CNT; ++j)
+    if (m0 + j < mlim) stage[(m0 + j - m_base) * BNW + trow] = h[j];
 }
 
 // Split-K ownership. The token columns that carry real tokens (the first mcols, M rounded
-// up to 4) are dealt out in shares of `share` columns (a multiple of 4) to the S CTAs of
+// up to 4) are dealt out in shares of `share` columns (a multiple of 16, so every 16-column
+// batch of an owner lies inside the accumulator's NT columns) to the S CTAs of
 // the cluster: CTA o sums and stores columns [o*share, (o+1)*share). The other CTAs'
 // partial sums of those columns reach it through their workspace slabs: CTA b writes
 // [NT/4 column groups][128 rows] of 16-byte granules at ws + b * (NT/4) * 128, the weight
 // row innermost, so a warp's 32 stores or loads cover 512 contiguous bytes.
-__host__ __device__ __forceinline__ int split_share(int mcols, int S) { return ((mcols + S - 1) / S + 3) & ~3; }
+__host__ __device__ __forceinline__ int split_share(int mcols, int S) { return ((mcols + S - 1) / S + 15) & ~15; }
 
 // Owned columns [own0, own0 + len) of row trow: this CTA's accumulator (TMEM) plus the
 // peers' slab granules, all copied into `land` ([S-1][len/4][128] granules) by one batch
@@ -162,19 +183,12 @@ __device__ __forceinline__ void finish_owned(const Epi& epi, uint32_t taddr, uin
   // every lane of the warp runs the tcgen05.ld below (.sync.aligned): rows past N only
   // skip their stores
   const bool nvalid = n < N;
+  const bool has_bias = epi.bias != nullptr;
   const int mlim = (own0 + len) < M ? own0 + len : M;
 #pragma unroll 1
   for (int c0 = 0; c0 < len; c0 += 16) {
     uint32_t acc[16];
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      uint32_t r[4] = {0u, 0u, 0u, 0u};
-      if (c0 + 4 * g < len) tmem_ld4(taddr + static_cast<uint32_t>(own0 + c0 + 4 * g), r);
-      acc[4 * g] = r[0];
-      acc[4 * g + 1] = r[1];
-      acc[4 * g + 2] = r[2];
-      acc[4 * g + 3] = r[3];
-    }
+    tmem_ld16(taddr + static_cast<uint32_t>(own0 + c0), acc);  // own0 + c0 + 16 <= NT (shares of 16)
     tmem_ld_wait();
     for (int pi = 0; pi + 1 < static_cast<int>(S); ++pi) {
 #pragma unroll
@@ -189,7 +203,7 @@ __device__ __forceinline__ void finish_owned(const Epi& epi, uint32_t taddr, uin
       }
     }
     if (!nvalid || own0 + c0 >= M) continue;
-    if (stage != nullptr) stage_batch<T, 16>(epi, acc, own0 + c0, mlim, own0, stage, trow, wsn, bn, s_as);
+    if (stage != nullptr) stage_batch<T, 16>(acc, own0 + c0, mlim, own0, stage, trow, wsn, bn, has_bias, s_as);
     else emit_batch<T, 16>(epi, acc, own0 + c0, mlim, n, N, wsn, bn, s_as);
   }
 }
@@ -237,7 +251,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_launch_dependents();  // the next kernel may start its prologue; it waits for our completion
+  // the next kernel may start its prologue (its weight loads compete with ours for HBM); it
+  // waits for our completion before it reads what we write
+  if (epi.trigger == 0) pdl_launch_dependents();
 
   auto stage_at = [&](int s) { return smem + s * C::STAGE; };
   int okt = 0;  // epilogue warps: the accumulator is complete
@@ -254,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         mbar_arrive_expect_tx(&full[i], C::STAGE);
         tma_load_2d(&tmW, &full[i], stage_at(i), (kbeg + i) * BK, tile * BNW);
       }
-      const int l2_end = (nk - pre) < kL2Ahead ? nk : pre + kL2Ahead;
+      const int l2_end = (nk - pre) < epi.l2ahead ? nk : pre + epi.l2ahead;
       for (int i = pre; i < l2_end; ++i) tma_prefetch_l2_2d(&tmW, (kbeg + i) * BK, tile * BNW);
       pdl_wait();  // the activations come from the previous kernel
       FNI8_TRACE_AT(1);
@@ -275,6 +291,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           ph ^= 1u;
         }
       }
+      if (epi.trigger == 1) pdl_launch_dependents();
       // every load still in flight lands before the ring is reused for the partial sums
       const int pending = issued < STG ? issued : STG;
       for (int i = 0; i < pending; ++i) {
@@ -332,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     okt = __shfl_sync(0xffffffffu, okt, 0);
     tc_fence_after();
     if (threadIdx.x == 64) FNI8_TRACE_AT(4);
+    if (epi.trigger == 2 && S == 1 && threadIdx.x == 64) pdl_launch_dependents();
   }
   __syncwarp();
 
@@ -360,12 +378,13 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int j = 0; j < CH; j += 4) {
           const int col = c0 + j;
-          if (col < mcols && col / share != static_cast<int>(rank))
+          if (col < mcols && (col < own0 || col >= own0 + share))
             __stcg(slab + (col >> 2) * BNW + trow, make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]));
         }
       }
     }
     cluster_sync_all();  // release/acquire at cluster scope: the slabs are visible to the owners
+    if (epi.trigger == 2 && threadIdx.x == 64) pdl_launch_dependents();
     if (threadIdx.x == 64) FNI8_TRACE_AT(5);
   }
   if (warp >= 2 && okt && len > 0) {
@@ -444,35 +463,77 @@ struct SplitPlan {
   size_t ws_bytes;  // partial-sum slabs of the K split (zero-maintained GEMM workspace)
 };
 
+template <int NT>
+static cudaError_t configure_splitk(int dev) {
+  static bool configured[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (configured[dev]) return cudaSuccess;
+  auto kern = splitk::w8a8_splitk_kernel<NT>;
+  // plans stay within 225 KB; the margin leaves room for static shared memory
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e == cudaSuccess) configured[dev] = true;
+  return e;
+}
+
+// How many S-CTA clusters of the NT kernel with `smem` bytes of shared memory can be
+// resident at once (clusters live inside one GPC, so this is below SMs x CTAs-per-SM / S).
+// -1 when the runtime cannot tell (no device).
+template <int NT>
+static int max_clusters_nt(int smem, int S) {
+  const int dev = current_device();
+  if (configure_splitk<NT>(dev) != cudaSuccess) return -1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(S);
+  cfg.blockDim = dim3(splitk::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = -1;
+  if (cudaOccupancyMaxActiveClusters(&n, splitk::w8a8_splitk_kernel<NT>, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return -1;
+  }
+  return n;
+}
+
+static int max_clusters(int nt, int smem, int S) {
+  struct Entry { int dev, nt, smem, S, n; };
+  static Entry cache[64];
+  static int used = 0;
+  const int dev = current_device();
+  for (int i = 0; i < used; ++i)
+    if (cache[i].dev == dev && cache[i].nt == nt && cache[i].smem == smem && cache[i].S == S) return cache[i].n;
+  int n = -1;
+  switch (nt) {
+    case 16: n = max_clusters_nt<16>(smem, S); break;
+    case 32: n = max_clusters_nt<32>(smem, S); break;
+    case 64: n = max_clusters_nt<64>(smem, S); break;
+    case 128: n = max_clusters_nt<128>(smem, S); break;
+    default: n = max_clusters_nt<256>(smem, S); break;
+  }
+  if (n >= 0 && used < 64) cache[used++] = Entry{dev, nt, smem, S, n};
+  return n;
+}
+
 // NT: tokens rounded up to a power of two >= 16. S: the cluster size that brings the grid
 // (n_tiles x S) closest to the SM count without exceeding it (at least 1, at most 8 and
-// the number of K blocks). Ring: as many stages as fit in ~half an SM's shared memory
-// (two CTAs per SM, so the next kernel can become resident), at least 3 when the K range
-// is split (2 otherwise), else the whole SM; the drained ring must also hold the staged
-// output tile of the CTA's columns. FNI8_SPLITK_S, FNI8_SPLITK_TARGET_PCT and
-// FNI8_SPLITK_SMEM_KB override (measurement knobs).
-static bool plan_splitk(int64_t M, int64_t N, int64_t K, SplitPlan* p) {
-  if (M < 1 || M > kSplitkMaxM) return false;
-  int nt = 16;
-  while (nt < M) nt <<= 1;
-  p->nt = nt;
+// the number of K blocks), lowered until every cluster of the grid can be resident at
+// once (a second wave of clusters would double the kernel's time). Ring: as many stages as
+// fit in ~half an SM's shared memory (two CTAs per SM, so the next kernel can become
+// resident), at least 3 when the K range is split (2 otherwise), else the whole SM; the
+// drained ring must also hold the staged output tile of the CTA's columns.
+// FNI8_SPLITK_S, FNI8_SPLITK_TARGET_PCT and FNI8_SPLITK_SMEM_KB override (measurement
+// knobs).
+static bool plan_ring(int nt, int S, SplitPlan* p) {
   const int stage = splitk::BNW * splitk::BK + nt * splitk::BK;
-  const int n_tiles = (int)((N + splitk::BNW - 1) / splitk::BNW);
-  const int kb = (int)((K + splitk::BK - 1) / splitk::BK);
-  const int sms = num_sms(current_device());
-  static const int forced_s = env_int("FNI8_SPLITK_S", 0);
-  static const int target_pct = env_int("FNI8_SPLITK_TARGET_PCT", 100);
   static const int forced_kb = env_int("FNI8_SPLITK_SMEM_KB", 0);
-  int S = forced_s;
-  if (S < 1 || S > 8) {
-    const int target = sms * target_pct / 100;
-    S = n_tiles >= target ? 1 : target / n_tiles;
-    if (S < 1) S = 1;
-    if (S > 8) S = 8;
-  }
-  if (S > kb) S = kb;
-  p->S = S;
-  p->grid = n_tiles * S;
   const int sh = S > 1 ? splitk::split_share(nt, S) : nt;
   const int out_tile = ((sh * splitk::BNW * 2 + 15) & ~15) + (S - 1) * sh * splitk::BNW * 4;
   const int fixed = 1024 + splitk::kBarBytes + splitk::kAsBytes;
@@ -488,6 +549,36 @@ static bool plan_splitk(int64_t M, int64_t N, int64_t K, SplitPlan* p) {
   if (stages < 2 || stages * stage < out_tile || fixed + stages * stage > 227 * 1024) return false;
   p->stages = stages;
   p->smem = fixed + stages * stage;
+  return true;
+}
+
+static bool plan_splitk(int64_t M, int64_t N, int64_t K, SplitPlan* p) {
+  if (M < 1 || M > kSplitkMaxM) return false;
+  int nt = 16;
+  while (nt < M) nt <<= 1;
+  p->nt = nt;
+  const int n_tiles = (int)((N + splitk::BNW - 1) / splitk::BNW);
+  const int kb = (int)((K + splitk::BK - 1) / splitk::BK);
+  const int sms = num_sms(current_device());
+  static const int forced_s = env_int("FNI8_SPLITK_S", 0);
+  static const int target_pct = env_int("FNI8_SPLITK_TARGET_PCT", 100);
+  int S = forced_s;
+  if (S < 1 || S > 8) {
+    const int target = sms * target_pct / 100;
+    S = n_tiles >= target ? 1 : target / n_tiles;
+    if (S < 1) S = 1;
+    if (S > 8) S = 8;
+  }
+  if (S > kb) S = kb;
+  if (!plan_ring(nt, S, p)) return false;
+  while (forced_s < 1 && S > 1) {
+    const int mc = max_clusters(nt, p->smem, S);
+    if (mc < 0 || n_tiles <= mc) break;
+    --S;
+    if (!plan_ring(nt, S, p)) return false;
+  }
+  p->S = S;
+  p->grid = n_tiles * S;
   p->ws_bytes = S > 1 ? static_cast<size_t>(p->grid) * nt * splitk::BNW * 4 : 0;
   return true;
 }
@@ -496,17 +587,10 @@ template <int NT>
 static int launch_splitk(const CUtensorMap& tw, const CUtensorMap& tx, const splitk::Epi& epi, int M, int N, int K,
                          const SplitPlan& p, uint4* ws, cudaStream_t st) {
   auto kern = splitk::w8a8_splitk_kernel<NT>;
-  static bool configured[kMaxDevices] = {};
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) return fail(FNI8_ERR_CUDA, "no current CUDA device");
-  if (!configured[dev]) {
-    // plans stay within 225 KB; the margin leaves room for static shared memory
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024);
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(split-K gemm)");
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return cuda_status(e, "carveout(split-K gemm)");
-    configured[dev] = true;
-  }
+  const cudaError_t ce = configure_splitk<NT>(dev);
+  if (ce != cudaSuccess) return cuda_status(ce, "configure split-K gemm");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid);
   cfg.blockDim = dim3(splitk::kThreads);
@@ -524,6 +608,13 @@ static int launch_splitk(const CUtensorMap& tw, const CUtensorMap& tx, const spl
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tw, tx, epi, M, N, K, p.stages, ws);
   if (e != cudaSuccess) return cuda_status(e, "launch split-K gemm");
   return FNI8_OK;
+}
+
+bool splitk_one_wave(int64_t M, int64_t N, int64_t K) {
+  SplitPlan p;
+  if (N >= (1LL << 31) || K >= (1LL << 31) || !plan_splitk(M, N, K, &p)) return false;
+  const int mc = max_clusters(p.nt, p.smem, p.S);
+  return mc >= 0 && p.grid / p.S <= mc;
 }
 
 bool splitk_supported(int64_t M, int64_t N, int64_t K) {
@@ -552,7 +643,12 @@ int splitk_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const fl
   if (int s = encode_tmap_2d_i8(&tx, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, 128, (uint32_t)p.nt)) return s;
   const int vec = out_mode != splitk::kOutI32 && residual == nullptr && N % 8 == 0 &&
                   (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
-  splitk::Epi epi{a_scale, w_scale, bias, residual, out, out_mode, vec};
+  // FNI8_SPLITK_L2AHEAD overrides the L2 prefetch depth (measurement knob)
+  static const int l2ahead = env_int("FNI8_SPLITK_L2AHEAD", splitk::kL2Ahead);
+  // FNI8_SPLITK_TRIGGER: when the next kernel is released (0 entry, 1 after the last load,
+  // 2 after the partial sums are published: the default, fastest in measured decode chains)
+  static const int trigger = env_int("FNI8_SPLITK_TRIGGER", 2);
+  splitk::Epi epi{a_scale, w_scale, bias, residual, out, out_mode, vec, l2ahead < 0 ? 0 : l2ahead, trigger};
   uint4* w4 = static_cast<uint4*>(ws);
   switch (p.nt) {
     case 16: return launch_splitk<16>(tw, tx, epi, (int)M, (int)N, (int)K, p, w4, st);

@@ -47,7 +47,10 @@ constexpr int kEpiThreads = 32 * kEpiWarps;
 constexpr int kThreads = 64 + kEpiThreads;
 constexpr int kMaxSeg = fni8h::kTileMaxSeg;
 constexpr int kGroupM = 16;
-constexpr int kL2AheadUnits = 16;  // weight k-blocks per CTA prefetched into L2 before the PDL wait
+// Weight k-blocks per CTA prefetched into L2 (beyond the ring) before the PDL wait: none by
+// default (measured on B200: the early prefetch competes with the upstream kernel's own
+// loads and gains nothing in decode or prefill chains).
+constexpr int kL2AheadUnits = 0;
 
 static __device__ int g_status;  // watchdog word of this file
 
@@ -61,6 +64,8 @@ struct Epi {
   const void* residual;  // [rows, N] (out dtype) or null
   void* out;             // [rows, N]
   int mode;              // kOutF16 / kOutBF16 / kOutI32
+  int l2ahead;           // weight k-blocks pulled into L2 (beyond the ring) before the PDL wait
+  int trigger;           // next kernel released at entry (0) or after this CTA's last load (1)
 };
 struct Groups {
   const int32_t* expert;
@@ -247,7 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Everything above touched only on-chip state; from here on we read upstream results.
   // In the dense case the TMA producer defers its wait: it first starts the weight loads
   // of its first ring of stages, which do not depend on the upstream kernel.
-  pdl_launch_dependents();  // the next kernel may start its prologue; it waits for our completion
+  // the next kernel may start its prologue; it waits for our completion
+  if (epi.trigger == 0) pdl_launch_dependents();
   if (GROUPED || !(warp == 0 && lane == 0)) pdl_wait();
 
   const int n_tiles = (N + BN - 1) / BN;
@@ -334,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         {  // weight tiles of the next units into L2 while the upstream kernel drains
           int tt = t, kk = k, nb = tc.n_blk;
-          for (int i = 0; i < kL2AheadUnits && tt < total; ++i) {
+          for (int i = 0; i < epi.l2ahead && tt < total; ++i) {
             tma_prefetch_l2_2d(&tmB, kk * BK, nb * BN + b_off);
             if (++kk == kb) {
               kk = 0;
@@ -364,6 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ph ^= 1u;
         }
       }
+      if (epi.trigger == 1) pdl_launch_dependents();
       // Drain: the loads of the last min(issued, STAGES) stages must have landed before
       // the CTA may exit (normally they have: the MMA consumed them). The odd CTA of a pair
       // sees its loads land through the release of the stage (the MMA consumed them).
@@ -626,6 +633,25 @@ bool grouped_pair_enabled() {
   return on;
 }
 
+// L2 prefetch depth and the point where the next kernel is released (measurement knobs
+// FNI8_TILE_L2AHEAD and FNI8_TILE_TRIGGER).
+static int tile_l2ahead() {
+  static const int v = [] {
+    const char* e = getenv("FNI8_TILE_L2AHEAD");
+    const int x = e ? atoi(e) : tile::kL2AheadUnits;
+    return x < 0 ? 0 : x;
+  }();
+  return v;
+}
+
+static int tile_trigger() {
+  static const int v = [] {
+    const char* e = getenv("FNI8_TILE_TRIGGER");
+    return e ? atoi(e) : 1;
+  }();
+  return v;
+}
+
 // Tensor map for the TMA-store epilogue: 16-bit outputs whose rows are 16-byte aligned.
 // Returns false (per-thread stores) otherwise; no error is raised for that.
 static bool out_tma_map(CUtensorMap* map, void* out, int out_mode, int64_t rows, int64_t N) {
@@ -645,7 +671,7 @@ int tile_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const floa
   if (int s = encode_tmap_2d_i8(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, 128, 128)) return s;
   if (int s = encode_tmap_2d_i8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, 128, (uint32_t)(pair ? bn / 2 : bn)))
     return s;
-  tile::Epi epi{a_scale, w_scale, bias, residual, out, out_mode};
+  tile::Epi epi{a_scale, w_scale, bias, residual, out, out_mode, tile_l2ahead(), tile_trigger()};
   tile::Groups grp{nullptr, nullptr, nullptr, 0};
   const int bmt = pair ? 256 : 128;
   const int m_tiles = (int)((M + bmt - 1) / bmt);
@@ -683,7 +709,7 @@ int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const in
   if (int s = encode_tmap_3d_i8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)E, (uint64_t)K, (uint64_t)(N * K), 128,
                                 (uint32_t)(pair ? bn / 2 : bn)))
     return s;
-  tile::Epi epi{a_scale, w_scale, nullptr, nullptr, out, out_mode};
+  tile::Epi epi{a_scale, w_scale, nullptr, nullptr, out, out_mode, tile_l2ahead(), tile_trigger()};
   tile::Groups grp{seg_expert, seg_off, seg_cnt, (int)S};
   const int sms = num_sms(current_device());
   const int grid = pair ? (sms & ~1) : sms;

@@ -218,9 +218,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       const uint8_t* prow = stage_at(st) + trow * 64;
       uint8_t* arow = aslot + a * A_BYTES + trow * 128;
+      // the four packed chunks are read before the first store (a shared-memory load issued
+      // after a store it might alias waits for that store)
+      uint4 pk[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {  // 64B swizzle of the packed tile: chunk ^= (row >> 1) & 3
-        const uint4 p = *reinterpret_cast<const uint4*>(prow + ((c ^ ((trow >> 1) & 3)) << 4));
+      for (int c = 0; c < 4; ++c)  // 64B swizzle of the packed tile: chunk ^= (row >> 1) & 3
+        pk[c] = *reinterpret_cast<const uint4*>(prow + ((c ^ ((trow >> 1) & 3)) << 4));
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 p = pk[c];
         uint4 o0, o1;
         unpack_word(p.x, o0.x, o0.y);
         unpack_word(p.y, o0.z, o0.w);
@@ -322,6 +328,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         bn = epi.mode == kOutBF16 ? to_f32<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(epi.bias)[n])
                                   : to_f32<__half>(static_cast<const __half*>(epi.bias)[n]);
       const float* landf = reinterpret_cast<const float*>(land);
+      // all sums first, then all stores (a shared-memory load issued after a store it might
+      // alias waits for that store)
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
         if (t >= own0 && t < own0 + len && t < M) {
@@ -338,8 +346,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tot = p == 0 ? v : __fadd_rn(tot, v);
           }
-          if (epi.mode == kOutBF16) emit_col<__nv_bfloat16, NT>(epi, t, n, tot, bn);
-          else emit_col<__half, NT>(epi, t, n, tot, bn);
+          accf[t] = tot;
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        if (t >= own0 && t < own0 + len && t < M) {
+          if (epi.mode == kOutBF16) emit_col<__nv_bfloat16, NT>(epi, t, n, accf[t], bn);
+          else emit_col<__half, NT>(epi, t, n, accf[t], bn);
         }
       }
     }

@@ -163,10 +163,11 @@ static int pick_path(int path, int64_t M, size_t ws_bytes, int64_t N, int64_t K)
   // N = 151936) streams faster through the tile kernel, whose MMAs consume twice the
   // weight bytes per instruction (measured on B200).
   const bool wide = M > 64 && (N + 255) / 256 >= num_sms(current_device());
-  // Above 128 tokens (one CTA per SM) a split-K grid that needs a second wave of clusters
-  // loses to the tile kernel (measured: gate_up at M = 256, 192 weight tiles).
+  // Above 128 tokens split-K wins only where it splits K over clusters that are all
+  // resident at once (measured at M = 256: QKV, O and down projections; the unsplit
+  // gate_up, 192 weight tiles, streams faster through the tile kernel).
   if (M <= splitk_auto_max_m() && !wide && splitk_supported(M, N, K) &&
-      ws_bytes >= splitk_workspace_bytes(M, N, K) && (M <= 128 || splitk_one_wave(M, N, K)))
+      ws_bytes >= splitk_workspace_bytes(M, N, K) && (M <= 128 || splitk_split_one_wave(M, N, K)))
     return FNI8_PATH_SPLITK;
   return FNI8_PATH_TILE;
 }

@@ -43,8 +43,9 @@ int skinny_status_read_and_clear(int* code);
 // of a split K range cross the zero-maintained GEMM workspace and are zeroed again.
 constexpr int64_t kSplitkMaxM = 256;
 bool splitk_supported(int64_t M, int64_t N, int64_t K);
-// Every cluster of the split-K plan for this shape can be resident at once.
-bool splitk_one_wave(int64_t M, int64_t N, int64_t K);
+// The split-K plan for this shape splits K (S > 1) and every one of its clusters can be
+// resident at once.
+bool splitk_split_one_wave(int64_t M, int64_t N, int64_t K);
 size_t splitk_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int splitk_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
                 const void* residual, void* out, int out_mode, int64_t M, int64_t N, int64_t K, void* ws,

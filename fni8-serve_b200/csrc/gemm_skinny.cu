@@ -33,7 +33,9 @@ namespace skinny {
 constexpr int kThreads = 192;
 constexpr int BNW = 128;  // weight rows per tile (MMA M)
 constexpr int BK = 128;   // K elements per stage
-constexpr int kL2Ahead = 16;
+// Weight k-blocks per CTA pulled into L2 beyond the ring before the dependency wait: none
+// (measured on B200 in decode chains: the next kernel's early prefetch delays this one).
+constexpr int kL2Ahead = 0;
 constexpr int kFullRowMaxM = 2;  // tokens for which each CTA reads the whole row instead of exchanging maxima
 
 static __device__ int g_status;
@@ -150,7 +152,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_launch_dependents();
 
   auto w_at = [&](int s) { return smem + s * W_BYTES; };
 
@@ -182,6 +183,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           ph ^= 1u;
         }
       }
+      // the next kernel is released once every weight load of this CTA is issued (its own
+      // loads then queue behind ours)
+      pdl_launch_dependents();
       const int pending = issued < WST ? issued : WST;
       for (int i = 0; i < pending; ++i) {
         const int s = (stage - 1 - i + 2 * WST) % WST;

@@ -26,6 +26,7 @@
 #include "fni8_common.cuh"
 #include "gemm_internal.h"
 
+#include <stdio.h>
 #include <stdlib.h>
 
 namespace fni8b {
@@ -477,13 +478,26 @@ static cudaError_t configure_splitk(int dev) {
   return e;
 }
 
-// How many S-CTA clusters of the NT kernel with `smem` bytes of shared memory can be
+// Empty kernel with the split-K kernel's block size: the occupancy calculator's stand-in.
+// (Asked about the split-K kernel itself, the CUDA 12.9 runtime answers one CTA per SM at
+// any shared-memory size, while two of its CTAs measurably run on one SM together.)
+static __global__ void __launch_bounds__(splitk::kThreads, 1) splitk_occupancy_standin() {}
+
+// How many S-CTA clusters of split-K CTAs with `smem` bytes of shared memory can be
 // resident at once (clusters live inside one GPC, so this is below SMs x CTAs-per-SM / S).
 // -1 when the runtime cannot tell (no device).
-template <int NT>
-static int max_clusters_nt(int smem, int S) {
+static int max_clusters(int smem, int S) {
+  static bool configured[kMaxDevices] = {};
   const int dev = current_device();
-  if (configure_splitk<NT>(dev) != cudaSuccess) return -1;
+  if (dev < 0 || dev >= kMaxDevices) return -1;
+  if (!configured[dev]) {
+    if (cudaFuncSetAttribute(splitk_occupancy_standin, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024) !=
+        cudaSuccess) {
+      (void)cudaGetLastError();
+      return -1;
+    }
+    configured[dev] = true;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(S);
   cfg.blockDim = dim3(splitk::kThreads);
@@ -496,7 +510,7 @@ static int max_clusters_nt(int smem, int S) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = -1;
-  if (cudaOccupancyMaxActiveClusters(&n, splitk::w8a8_splitk_kernel<NT>, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, splitk_occupancy_standin, &cfg) != cudaSuccess) {
     (void)cudaGetLastError();
     return -1;
   }
@@ -504,21 +518,15 @@ static int max_clusters_nt(int smem, int S) {
 }
 
 static int max_clusters(int nt, int smem, int S) {
-  struct Entry { int dev, nt, smem, S, n; };
+  (void)nt;  // the ring size (smem) carries the token count's effect
+  struct Entry { int dev, smem, S, n; };
   static Entry cache[64];
   static int used = 0;
   const int dev = current_device();
   for (int i = 0; i < used; ++i)
-    if (cache[i].dev == dev && cache[i].nt == nt && cache[i].smem == smem && cache[i].S == S) return cache[i].n;
-  int n = -1;
-  switch (nt) {
-    case 16: n = max_clusters_nt<16>(smem, S); break;
-    case 32: n = max_clusters_nt<32>(smem, S); break;
-    case 64: n = max_clusters_nt<64>(smem, S); break;
-    case 128: n = max_clusters_nt<128>(smem, S); break;
-    default: n = max_clusters_nt<256>(smem, S); break;
-  }
-  if (n >= 0 && used < 64) cache[used++] = Entry{dev, nt, smem, S, n};
+    if (cache[i].dev == dev && cache[i].smem == smem && cache[i].S == S) return cache[i].n;
+  const int n = max_clusters(smem, S);
+  if (n >= 0 && used < 64) cache[used++] = Entry{dev, smem, S, n};
   return n;
 }
 
@@ -580,6 +588,10 @@ static bool plan_splitk(int64_t M, int64_t N, int64_t K, SplitPlan* p) {
   p->S = S;
   p->grid = n_tiles * S;
   p->ws_bytes = S > 1 ? static_cast<size_t>(p->grid) * nt * splitk::BNW * 4 : 0;
+  static const int log_plan = env_int("FNI8_PLAN_LOG", 0);
+  if (log_plan)
+    fprintf(stderr, "fni8 split-K plan M=%lld N=%lld K=%lld: NT=%d S=%d grid=%d stages=%d smem=%d resident clusters=%d\n",
+            (long long)M, (long long)N, (long long)K, nt, S, p->grid, p->stages, p->smem, max_clusters(nt, p->smem, S));
   return true;
 }
 
@@ -610,9 +622,9 @@ static int launch_splitk(const CUtensorMap& tw, const CUtensorMap& tx, const spl
   return FNI8_OK;
 }
 
-bool splitk_one_wave(int64_t M, int64_t N, int64_t K) {
+bool splitk_split_one_wave(int64_t M, int64_t N, int64_t K) {
   SplitPlan p;
-  if (N >= (1LL << 31) || K >= (1LL << 31) || !plan_splitk(M, N, K, &p)) return false;
+  if (N >= (1LL << 31) || K >= (1LL << 31) || !plan_splitk(M, N, K, &p) || p.S < 2) return false;
   const int mc = max_clusters(p.nt, p.smem, p.S);
   return mc >= 0 && p.grid / p.S <= mc;
 }

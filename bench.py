@@ -296,6 +296,93 @@ def time_eager(fn, steps, warmup, world, flush=None):
     return max_over_ranks(total, world)
 
 
+def time_pipelined(items, steps, warmup, world, slots=2):
+    """End-to-end timing through the public API with host buffers, the way a server runs:
+    per item (hx pinned host input, dxs device input slots, fn public call, hy pinned host
+    output; fn may return a list of tensors and hy be the matching list) the host->device
+    copy runs on one stream, fn on a second and the device->host copy of its result on a
+    third, ordered by events, so copies of one item overlap the compute of another. Every
+    copy of every step is inside the timed region (CUDA events on the launching stream,
+    joined with the three streams); max over ranks."""
+    s_in, s_cmp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    free = {}  # (item, slot) -> event: the compute that read that device slot is done
+    drained = {}  # (item, slot) -> event: the D2H of the outputs computed from that slot is done
+
+    def one(k):
+        slot = k % slots
+        for i, (hx, dxs, fn, hy) in enumerate(items):
+            dx = dxs[slot]
+            ev = free.get((i, slot))
+            if ev is not None:
+                s_in.wait_event(ev)
+            with torch.cuda.stream(s_in):
+                dx.copy_(hx, non_blocking=True)
+            e_in = torch.cuda.Event()
+            e_in.record(s_in)
+            s_cmp.wait_event(e_in)
+            ev = drained.get((i, slot))
+            if ev is not None:  # static (graph) outputs of this slot were copied out
+                s_cmp.wait_event(ev)
+            with torch.cuda.stream(s_cmp):
+                y = fn(dx)
+            e_c = torch.cuda.Event()
+            e_c.record(s_cmp)
+            free[(i, slot)] = e_c
+            s_out.wait_event(e_c)
+            ys, hys = (y, hy) if isinstance(y, (list, tuple)) else ([y], [hy])
+            with torch.cuda.stream(s_out):
+                for yt, ht in zip(ys, hys):
+                    ht.copy_(yt, non_blocking=True)
+            e_o = torch.cuda.Event()
+            e_o.record(s_out)
+            drained[(i, slot)] = e_o
+            for yt in ys:
+                yt.record_stream(s_out)
+
+    for k in range(warmup):
+        one(k)
+    torch.cuda.synchronize()
+    barrier(world)
+    cur = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(cur)
+    for st in (s_in, s_cmp, s_out):
+        st.wait_event(a)
+    for k in range(steps):
+        one(warmup + k)
+    for st in (s_in, s_cmp, s_out):
+        e = torch.cuda.Event()
+        e.record(st)
+        cur.wait_event(e)
+    b.record(cur)
+    torch.cuda.synchronize()
+    return max_over_ranks(a.elapsed_time(b), world)
+
+
+def graph_per_slot(slots, calls):
+    """Capture calls(xd) -> outputs in one CUDA graph per device input slot (the way a
+    decode runner replays a step); returns replay(xd) -> that slot's static outputs."""
+    graphs = {}
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    for xd in slots:
+        with torch.cuda.stream(cap):
+            calls(xd)  # eager warm-up outside the capture
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                out = calls(xd)
+        graphs[xd.data_ptr()] = (g, out)
+    torch.cuda.current_stream().wait_stream(cap)
+    torch.cuda.synchronize()
+
+    def replay(xd):
+        g, o = graphs[xd.data_ptr()]
+        g.replay()
+        return o
+
+    return replay
+
+
 # ------------------------------------------------------------------ configs (our arm)
 def run_config1(args, world, rank, dev):
     import fni8
@@ -331,29 +418,29 @@ def run_config1(args, world, rank, dev):
     achieved = gemm_bytes / (gemm_ms * 1e-3) / 1e9
 
     # end to end through the public API with host buffers: H2D of each linear's input
-    # from pinned memory, fni8.linear, D2H of its output, every step
-    hx = [x.cpu().pin_memory() for (*_, x) in ds.items]
-    hy = [torch.empty(M, N, dtype=torch.float16).pin_memory() for (M, _, _, N, _, _) in ds.items]
-    h2d = sum(t.numel() * 2 for t in hx)
-    d2h = sum(t.numel() * 2 for t in hy)
+    # from pinned memory, fni8.linear, D2H of its output, every step (copies and compute
+    # on separate streams, pipelined across the step's linears)
+    # The step's 20 inputs travel as one pinned buffer; the 20 fni8.linear calls of a step
+    # are captured in a CUDA graph per input slot (a decode runner's replay), so the host
+    # issues one replay per step instead of 20 eager calls.
+    sizes = [x.numel() for (*_, x) in ds.items]
+    hx = torch.cat([x.reshape(-1) for (*_, x) in ds.items]).cpu().pin_memory()
+    hy = torch.empty(sum(M * N for (M, _, _, N, _, _) in ds.items), dtype=torch.float16).pin_memory()
+    h2d = hx.numel() * 2
+    d2h = hy.numel() * 2
+    slots = [torch.empty_like(hx, device=dev) for _ in range(2)]
 
-    def e2e_step():
-        for (M, _, K, N, qt, _), xh, yh in zip(ds.items, hx, hy):
-            xd = xh.to(dev, non_blocking=True)
-            yh.copy_(fni8.linear(xd, qt), non_blocking=True)
+    def calls(xd):
+        outs, off = [], 0
+        for (M, _, K, _, qt, _), n in zip(ds.items, sizes):
+            outs.append(fni8.linear(xd[off:off + n].view(M, K), qt))
+            off += n
+        return torch.cat([o.reshape(-1) for o in outs])  # the step's results, one D2H
 
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier(world)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(args.steps):
-        e2e_step()
-    b.record()
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(a.elapsed_time(b), world) / args.steps
+    replay = graph_per_slot(slots, calls)
+    e2e_ms = time_pipelined([(hx, slots, replay, hy)], args.steps, args.warmup, world, slots=2) / args.steps
     e2e = world * ds.bytes / (e2e_ms * 1e-3) / 1e9
+    del replay
 
     line = {
         "metric": "W8A8 decode GB/s (Qwen3-8B QKV/O/gate_up/down at M=1,8,32,128,256; % of HBM)",
@@ -371,7 +458,10 @@ def run_config1(args, world, rank, dev):
                      "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs)",
                      "gemm_gbs_per_M": per, "gemm_us_per_step": round(gemm_ms * 1e3, 2)},
         "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": round(e2e_ms, 4), "api": "fni8.linear (eager, pinned host buffers)"},
+                "ms_per_step": round(e2e_ms, 4),
+                "api": "fni8.linear x20 captured in a CUDA graph per input slot (decode-runner replay), "
+                       "results gathered into one buffer; pinned host buffers; H2D, replay and D2H on three "
+                       "streams, steps pipelined"},
         "gpu_launches": 40 * args.steps,
         "clocks": clocks,
     }
@@ -410,24 +500,17 @@ def run_config2(args, world, rank, dev):
     xh = x.cpu().pin_memory()
     yh = torch.empty(M, 4096, dtype=torch.float16).pin_memory()
 
-    def e2e_step():
-        xd = xh.to(dev, non_blocking=True)
+    def e2e_fn(xd):
         q, s = fni8.rmsnorm_quant(xd, gamma, 1e-6)
         fni8.linear_q(q, s, W["qkv"])
         fni8.linear_q(q, s, W["o"])
         hq, hs = fni8.act_and_mul_quant(fni8.linear_q(q, s, W["gate_up"]))
-        yh.copy_(fni8.linear_q(hq, hs, W["down"]), non_blocking=True)
+        return fni8.linear_q(hq, hs, W["down"])
 
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(args.steps):
-        e2e_step()
-    b.record()
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(a.elapsed_time(b), world) / args.steps
+    # H2D of a step's hidden state, the step, D2H of its output: three streams, steps
+    # pipelined (two device input slots)
+    e2e_ms = time_pipelined([(xh, [torch.empty_like(x) for _ in range(2)], e2e_fn, yh)], args.steps, args.warmup,
+                            world) / args.steps
     line = {
         "metric": "W8A8 prefill TOPS (Qwen3-8B 4 GEMMs at M=8192, fused RMSNorm+quant; % int8 TC peak)",
         "value": round(value, 1), "unit": "TOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -442,7 +525,10 @@ def run_config2(args, world, rank, dev):
                      "peak_source": "nominal dense int8 (no measured int8 peak); 2x measured bf16 = "
                                     f"{2 * pk['bf16_tflops']:.0f}"},
         "e2e": {"value": round(world * ops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TOP/s",
-                "h2d_bytes_per_step": xh.numel() * 2, "d2h_bytes_per_step": yh.numel() * 2},
+                "h2d_bytes_per_step": xh.numel() * 2, "d2h_bytes_per_step": yh.numel() * 2,
+                "ms_per_step": round(e2e_ms, 4),
+                "api": "fni8 rmsnorm_quant / linear_q / act_and_mul_quant (eager, pinned host buffers; "
+                       "H2D, compute and D2H on three streams, steps pipelined)"},
         "gpu_launches": 6 * args.steps,
         "clocks": clocks,
     }
@@ -469,11 +555,10 @@ def run_config0(args, world, rank, dev):
                         flush=lambda: flush_l2(flush_buf)) / args.steps
     xh = x.cpu().pin_memory()
     yh = torch.empty(M, N, dtype=torch.float16).pin_memory()
-
-    def e2e_step():
-        yh.copy_(fni8.linear(xh.to(dev, non_blocking=True), qt), non_blocking=True)
-
-    e2e_ms = time_eager(e2e_step, args.steps, args.warmup, world) / args.steps
+    slots = [torch.empty_like(x) for _ in range(3)]
+    replay = graph_per_slot(slots, lambda xd: fni8.linear(xd, qt))
+    e2e_ms = time_pipelined([(xh, slots, replay, yh)], args.steps, args.warmup, world, slots=3) / args.steps
+    del replay
     line = base_line("W8A8 linear TOP/s (M=256 K=1024 N=6144; % int8 TC peak)", world * ops / (ms * 1e-3) / 1e12,
                      "TOP/s", world, args, ms,
                      {"workload": "BASELINE config 0: single W8A8 linear", "M": M, "K": K, "N": N,
@@ -484,7 +569,9 @@ def run_config0(args, world, rank, dev):
                         "traffic": committed_traffic("cfg0_linear"), "kernel": "quantise + w8a8_tile_kernel",
                         "note": "3.2 GOP in one launch pair: launch-latency bound, not tensor bound"}
     line["e2e"] = {"value": round(world * ops / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TOP/s",
-                   "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2}
+                   "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2, "ms_per_step": round(e2e_ms, 4),
+                   "api": "fni8.linear captured in a CUDA graph per input slot; pinned host buffers; H2D, "
+                          "replay and D2H on three streams, steps pipelined"}
     line["gpu_launches"] = 2 * args.steps
     line["clocks"] = clk.summary()
     return line, None

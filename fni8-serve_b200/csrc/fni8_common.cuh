@@ -444,6 +444,20 @@ inline int pdl_enabled() {
 // consecutive kernels of the library never force an L1/shared reconfiguration.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args);
+
+// First failed launch_pdl of this host thread since FNI8_CHECK_LAUNCH last looked
+// (cudaLaunchKernelEx returns a refused launch, e.g. too many registers for the block,
+// without leaving it for cudaGetLastError).
+inline thread_local cudaError_t t_launch_error = cudaSuccess;
+inline cudaError_t take_launch_error() {
+  const cudaError_t e = t_launch_error;
+  t_launch_error = cudaSuccess;
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                        Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -461,12 +475,14 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
     cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     carveout_set[dev] = true;
   }
-  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess && t_launch_error == cudaSuccess) t_launch_error = e;
+  return e;
 }
 }  // namespace fni8h
 
 #define FNI8_CHECK_LAUNCH(what)                                  \
   do {                                                           \
-    cudaError_t _e = cudaGetLastError();                         \
+    cudaError_t _e = fni8h::take_launch_error();                 \
     if (_e != cudaSuccess) return fni8h::cuda_status(_e, what);  \
   } while (0)

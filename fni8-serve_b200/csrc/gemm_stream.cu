@@ -29,7 +29,10 @@ namespace strm {
 constexpr int kThreads = 192;
 constexpr int BNW = 128;  // weight rows per tile (MMA M)
 constexpr int BK = 128;
-constexpr int64_t kL2AheadUnits = 24;  // 384 KB of weights per CTA prefetched into L2
+// Weight units per CTA pulled into L2 beyond the ring before the dependency wait: none
+// (measured on B200 in decode chains: early prefetch of the next kernel's weights delays
+// the running kernel more than it saves).
+constexpr int64_t kL2AheadUnits = 0;
 
 static __device__ int g_status;
 
@@ -200,7 +203,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // The weights never depend on the previous kernel, the activations do. The producer
   // therefore arms the first ring of stages and starts their weight loads before the
   // grid-dependency wait, so the first HBM round trip overlaps the upstream kernel's tail.
-  pdl_launch_dependents();  // the next kernel may start its prologue; it waits for our completion
   if (!(warp == 0 && lane == 0)) pdl_wait();
 
   if (warp == 0) {
@@ -253,6 +255,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           ph ^= 1u;
         }
       }
+      // the next kernel may start its prologue once this CTA's loads are all issued (its
+      // loads then queue behind ours); it waits for our completion before reading
+      pdl_launch_dependents();
       const int pending = issued < C::STAGES ? issued : C::STAGES;
       for (int i = 0; i < pending; ++i) {
         const int s = (stage - 1 - i + 2 * C::STAGES) % C::STAGES;

@@ -36,7 +36,7 @@ constexpr int A_BYTES = BNW * BK;       // unpacked int8 weight tile (128B swizz
 constexpr int kASlots = 3;
 constexpr int kAccBufs = 4;
 constexpr int kMaxStages = 8;
-constexpr int kL2Ahead = 16;
+constexpr int kL2Ahead = 0;  // no early L2 prefetch (it delays the upstream kernel in decode chains)
 constexpr int kBarBytes = 512;
 
 static __device__ int g_status;
@@ -131,7 +131,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_launch_dependents();
 
   auto stage_at = [&](int s) { return ring + s * C::STAGE; };
   int okt = 1;  // folding warps: every wait succeeded
@@ -171,6 +170,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           ph ^= 1u;
         }
       }
+      // the next kernel is released once this CTA's loads are all issued (its own loads
+      // then queue behind ours); it waits for our completion before reading our output
+      pdl_launch_dependents();
       const int pending = issued < STG ? issued : STG;
       for (int i = 0; i < pending; ++i) {
         const int s = (stage - 1 - i + 2 * STG) % STG;

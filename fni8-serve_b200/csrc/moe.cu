@@ -48,6 +48,8 @@ template <int VPL>
 __global__ void route_kernel(const float* __restrict__ logits, int T, int E, int k, int scoring,
                              const float* __restrict__ sel_bias, int n_groups, int topk_group, int norm_topk,
                              float scaling, int wdtype, int32_t* __restrict__ topi, float* __restrict__ topw) {
+  pdl_launch_dependents();
+  pdl_wait();  // the logits come from the previous kernel
   const int warps = blockDim.x >> 5;
   const int t = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -160,7 +162,12 @@ __global__ void route_kernel(const float* __restrict__ logits, int T, int E, int
 }
 
 // ---------------------------------------------------------------- plan
+// Every kernel of this file is launched with programmatic stream serialization: it lets
+// the next kernel launch at once and waits for the previous one before touching global
+// memory (so the launch latency, not the data, is what overlaps).
 __global__ void plan_hist(const int32_t* __restrict__ topi, int64_t n, int E, int32_t* __restrict__ hist) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ int h[kMaxE];
   for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
   __syncthreads();
@@ -174,15 +181,29 @@ __global__ void plan_hist(const int32_t* __restrict__ topi, int64_t n, int E, in
 }
 
 // One CTA: counts, offsets and each chunk's starting row per expert (in place of hist).
-__global__ void plan_scan(int32_t* __restrict__ hist, int n_chunks, int E, int32_t* __restrict__ counts,
-                          int32_t* __restrict__ offsets) {
+// Each thread owns an expert column; its chunk counts are read 32 at a time before any of
+// them is rewritten (a load issued after a store it might alias waits for that store).
+constexpr int kScanThreads = 256;
+__global__ void __launch_bounds__(kScanThreads) plan_scan(int32_t* __restrict__ hist, int n_chunks, int E,
+                                                          int32_t* __restrict__ counts, int32_t* __restrict__ offsets) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ int tot[kMaxE];
+  __shared__ int base[kMaxE];
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int run = 0;
-    for (int c = 0; c < n_chunks; ++c) {
-      const int v = hist[static_cast<int64_t>(c) * E + e];
-      hist[static_cast<int64_t>(c) * E + e] = run;
-      run += v;
+    for (int c0 = 0; c0 < n_chunks; c0 += 32) {
+      const int nc = n_chunks - c0 < 32 ? n_chunks - c0 : 32;
+      int v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = j < nc ? hist[static_cast<int64_t>(c0 + j) * E + e] : 0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j < nc) {
+          hist[static_cast<int64_t>(c0 + j) * E + e] = run;
+          run += v[j];
+        }
+      }
     }
     tot[e] = run;
     counts[e] = run;
@@ -191,6 +212,7 @@ __global__ void plan_scan(int32_t* __restrict__ hist, int n_chunks, int E, int32
   if (threadIdx.x == 0) {
     int run = 0;
     for (int e = 0; e < E; ++e) {
+      base[e] = run;
       offsets[e] = run;
       run += tot[e];
     }
@@ -198,13 +220,23 @@ __global__ void plan_scan(int32_t* __restrict__ hist, int n_chunks, int E, int32
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    const int base = offsets[e];
-    for (int c = 0; c < n_chunks; ++c) hist[static_cast<int64_t>(c) * E + e] += base;
+    const int b = base[e];
+    for (int c0 = 0; c0 < n_chunks; c0 += 32) {
+      const int nc = n_chunks - c0 < 32 ? n_chunks - c0 : 32;
+      int v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = j < nc ? hist[static_cast<int64_t>(c0 + j) * E + e] : 0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nc) hist[static_cast<int64_t>(c0 + j) * E + e] = v[j] + b;
+    }
   }
 }
 
 __global__ void plan_scatter(const int32_t* __restrict__ topi, int64_t n, int E, const int32_t* __restrict__ base,
                              int32_t* __restrict__ row_of_slot, int32_t* __restrict__ slot_of_row) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ int wc[];  // [32 warps][E]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) wc[i] = 0;
@@ -230,6 +262,8 @@ __global__ void plan_scatter(const int32_t* __restrict__ topi, int64_t n, int E,
 }
 
 __global__ void iota_kernel(int32_t* p, int n) {
+  pdl_launch_dependents();
+  pdl_wait();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = i;
 }
 
@@ -238,6 +272,8 @@ __global__ void iota_kernel(int32_t* p, int n) {
 __global__ void gather_rows(const int8_t* __restrict__ q, const float* __restrict__ scale,
                             const int32_t* __restrict__ slot_of_row, int64_t R, const int32_t* __restrict__ n_rows_dev,
                             int K, int k, int8_t* __restrict__ q_out, float* __restrict__ s_out) {
+  pdl_launch_dependents();
+  pdl_wait();
   if (n_rows_dev != nullptr) {
     const int64_t n = *n_rows_dev;
     R = n < R ? n : R;
@@ -257,6 +293,8 @@ __global__ void gather_rows(const int8_t* __restrict__ q, const float* __restric
 template <typename T>
 __global__ void combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ row_of_slot,
                                const float* __restrict__ topw, int64_t Tn, int k, int H, T* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
   // one CTA per token; each thread owns 8 consecutive columns
   for (int64_t t = blockIdx.x; t < Tn; t += gridDim.x) {
     for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
@@ -303,10 +341,9 @@ extern "C" int fni8_moe_route(const float* logits, int64_t T, int64_t E, int64_t
   const int threads = 256, per = threads / 32;
   const int grid = (int)((T + per - 1) / per);
   const int vpl = (int)((E + 31) / 32);
-#define FNI8_ROUTE(V)                                                                                             \
-  moe::route_kernel<V><<<grid, threads, 0, st>>>(logits, (int)T, (int)E, (int)top_k, scoring, sel_bias,         \
-                                                 (int)n_groups, (int)topk_group, norm_topk, scaling, weight_dtype, \
-                                                 topi, topw)
+#define FNI8_ROUTE(V)                                                                                          \
+  launch_pdl(moe::route_kernel<V>, dim3(grid), dim3(threads), 0, st, logits, (int)T, (int)E, (int)top_k, scoring, \
+             sel_bias, (int)n_groups, (int)topk_group, norm_topk, scaling, weight_dtype, topi, topw)
   if (vpl <= 1) FNI8_ROUTE(1);
   else if (vpl <= 2) FNI8_ROUTE(2);
   else if (vpl <= 4) FNI8_ROUTE(4);
@@ -337,15 +374,16 @@ extern "C" int fni8_moe_plan(const int32_t* topi, int64_t n_slots, int64_t E, in
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int chunks = (int)((n_slots + moe::kChunk - 1) / moe::kChunk);
   int32_t* hist = static_cast<int32_t*>(workspace);
-  if (chunks > 0) moe::plan_hist<<<chunks, moe::kChunk, 0, st>>>(topi, n_slots, (int)E, hist);
-  moe::plan_scan<<<1, 1024, 0, st>>>(hist, chunks, (int)E, counts, offsets);
+  if (chunks > 0) launch_pdl(moe::plan_hist, dim3(chunks), dim3(moe::kChunk), 0, st, topi, n_slots, (int)E, hist);
+  launch_pdl(moe::plan_scan, dim3(1), dim3(moe::kScanThreads), 0, st, hist, chunks, (int)E, counts, offsets);
   if (chunks > 0) {
     const size_t smem = 32 * E * sizeof(int);
     if (smem > 48 * 1024) {
       cudaError_t e = cudaFuncSetAttribute(moe::plan_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return cuda_status(e, "plan_scatter smem");
     }
-    moe::plan_scatter<<<chunks, moe::kChunk, smem, st>>>(topi, n_slots, (int)E, hist, row_of_slot, slot_of_row);
+    launch_pdl(moe::plan_scatter, dim3(chunks), dim3(moe::kChunk), smem, st, topi, n_slots, (int)E,
+               static_cast<const int32_t*>(hist), row_of_slot, slot_of_row);
   }
   FNI8_CHECK_LAUNCH("moe_plan");
   return FNI8_OK;
@@ -361,8 +399,8 @@ extern "C" int fni8_moe_gather_rows_i8(const int8_t* q, const float* scale, cons
     return fail(FNI8_ERR_ALIGN, "gather: rows must be 16-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t blocks = (R + 7) / 8;
-  moe::gather_rows<<<(int)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, st>>>(q, scale, slot_of_row, R, nullptr,
-                                                                                 (int)K, (int)top_k, q_out, scale_out);
+  launch_pdl(moe::gather_rows, dim3((int)(blocks < 148 * 16 ? blocks : 148 * 16)), dim3(256), 0, st, q, scale,
+             slot_of_row, R, static_cast<const int32_t*>(nullptr), (int)K, (int)top_k, q_out, scale_out);
   FNI8_CHECK_LAUNCH("moe_gather_rows_i8");
   return FNI8_OK;
 }
@@ -399,12 +437,12 @@ extern "C" int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_
   const int grid = (int)(T < 148 * 8 ? T : 148 * 8);
   const int threads = (int)((H / 8) < 256 ? ((H / 8 + 31) / 32) * 32 : 256);
   if (dtype == FNI8_F16)
-    moe::combine_kernel<__half><<<grid, threads, 0, st>>>(static_cast<const __half*>(y), row_of_slot, topw, T,
-                                                          (int)top_k, (int)H, static_cast<__half*>(out));
+    launch_pdl(moe::combine_kernel<__half>, dim3(grid), dim3(threads), 0, st, static_cast<const __half*>(y),
+               row_of_slot, topw, T, (int)top_k, (int)H, static_cast<__half*>(out));
   else
-    moe::combine_kernel<__nv_bfloat16><<<grid, threads, 0, st>>>(static_cast<const __nv_bfloat16*>(y), row_of_slot,
-                                                                 topw, T, (int)top_k, (int)H,
-                                                                 static_cast<__nv_bfloat16*>(out));
+    launch_pdl(moe::combine_kernel<__nv_bfloat16>, dim3(grid), dim3(threads), 0, st,
+               static_cast<const __nv_bfloat16*>(y), row_of_slot, topw, T, (int)top_k, (int)H,
+               static_cast<__nv_bfloat16*>(out));
   FNI8_CHECK_LAUNCH("moe_combine");
   return FNI8_OK;
 }
@@ -477,15 +515,16 @@ extern "C" int fni8_moe_experts_w8a8(const void* x, int dtype, int64_t T, int64_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (int s = fni8_quantize_rows_i8(x, dtype, T, H, xq, xs, stream)) return s;
   if (int s = fni8_moe_plan(topi, R, E, counts, offsets, ros, sor, b + L.plan, L.counts - L.plan, stream)) return s;
-  moe::iota_kernel<<<1, 256, 0, st>>>(iota, (int)E);
+  launch_pdl(moe::iota_kernel, dim3(1), dim3(256), 0, st, iota, (int)E);
   FNI8_CHECK_LAUNCH("iota");
   // Rows whose expert id is out of range are dropped by the plan; the grouped GEMMs
   // only cover offsets[E] rows, so every gathered row is a routed one. R is an upper
   // bound for the row count, which is only known on the device.
   {
     const int64_t blocks = (R + 7) / 8;
-    moe::gather_rows<<<(int)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, st>>>(xq, xs, sor, R, offsets + E,
-                                                                                   (int)H, (int)top_k, aq, as);
+    launch_pdl(moe::gather_rows, dim3((int)(blocks < 148 * 16 ? blocks : 148 * 16)), dim3(256), 0, st,
+               static_cast<const int8_t*>(xq), static_cast<const float*>(xs), static_cast<const int32_t*>(sor), R,
+               static_cast<const int32_t*>(offsets + E), (int)H, (int)top_k, aq, as);
     FNI8_CHECK_LAUNCH("moe gather");
   }
   if (int s = fni8_grouped_gemm_w8a8(aq, as, R, w_gu, s_gu, E, 2 * I, H, iota, offsets, counts, E, h, dtype, stream))

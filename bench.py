@@ -454,7 +454,7 @@ def run_config1(args, world, rank, dev):
         "frac_of_hbm": round(value / world / pk["hbm_gbs"], 3),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 3), "traffic": committed_traffic("decode_gemm"),
-                     "kernel": "w8a8_splitk_kernel (M<=128) / CTA-pair w8a8_tile_kernel (M=256): the 20 decode GEMMs, graph-replayed, per-M graphs",
+                     "kernel": "w8a8_splitk_kernel (M<=128, and QKV/O/down at M=256) / CTA-pair w8a8_tile_kernel (gate_up at M=256): the 20 decode GEMMs, graph-replayed, per-M graphs",
                      "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs)",
                      "gemm_gbs_per_M": per, "gemm_us_per_step": round(gemm_ms * 1e3, 2)},
         "e2e": {"value": round(e2e, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -11,8 +11,8 @@
 //    128 weight rows (the tcgen05 MMA's M), CTA rank r of the cluster the r-th slice of
 //    the K range. Weights are the A operand (swap-AB), tokens the N operand (NT = 16/32).
 //  * warp 0 streams the weight tiles of its K slice through a TMA ring. Weights never
-//    depend on the previous kernel, so the stream starts before the grid-dependency wait,
-//    and the tiles beyond the ring are prefetched into L2.
+//    depend on the previous kernel, so the first ring is issued before the
+//    grid-dependency wait; the next kernel is released once every load is issued.
 //  * warps 2-5 read the activations of the K slice, take each token's absmax over it,
 //    exchange the S partial maxima through distributed shared memory (remote mbarrier
 //    arrivals + ld.shared::cluster), then write the whole slice as int8 into shared memory

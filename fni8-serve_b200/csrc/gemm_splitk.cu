@@ -1,28 +1,31 @@
-// Decode W8A8 GEMM for 1..256 tokens: every SM streams weights, partial sums stay on chip.
+// Decode W8A8 GEMM for 1..256 tokens: every SM streams weights.
 //
 //   acc^T[n, m] = sum_k W[n, k] * q[m, k]     (tcgen05.mma kind::i8, M=128 weight rows, N=NT tokens)
 //   out[m, n]   = dtype((float(acc) * a_scale[m]) * w_scale[n] (+ bias[n]) (+ residual[m, n]))
 //
 // At decode sizes the GEMM reads W[N, K] once and is bound by how many SMs keep weight
-// loads in flight, not by the tensor cores. The tile kernel gives one CTA per 128x128
-// output tile (32-48 CTAs for a Qwen3-8B projection), the stream-K kernel reduces its
+// loads in flight, not by the tensor cores. The tile kernel gives one CTA per 128x256
+// output tile (24-96 CTAs for a Qwen3-8B projection), the stream-K kernel reduces its
 // partial tiles with global atomics whose count grows with the token count. Here:
 //
 //  * grid = n_tiles x S CTAs, clustered S (<= 8) at a time. A cluster owns 128 weight
 //    rows; CTA rank r of the cluster the r-th slice of the K range, so n_tiles x S ~ the
-//    SM count for any N and K.
+//    SM count for any N and K (S lowered until all clusters are resident at once).
 //  * warp 0 streams (weight, activation) k-blocks of its slice through a TMA ring. Weights
-//    never depend on the previous kernel: the first ring of weight tiles is issued and the
-//    following tiles are pulled into L2 before the grid-dependency wait; the int8
-//    activations (written by the quantiser just before) are loaded after it.
+//    never depend on the previous kernel: the first ring of weight tiles is issued before
+//    the grid-dependency wait; the int8 activations (written by the quantiser just
+//    before) are loaded after it.
 //  * warp 1 issues the MMAs into one TMEM accumulator of NT columns.
-//  * the S partial accumulators meet in shared memory: per pass of up to 64 token columns
-//    every CTA stages its columns, the cluster synchronises, and CTA r sums the r-th
-//    share of the columns over all S CTAs (ld.shared::cluster) and stores those outputs.
-//    Integer sums are associative, so the result is bit-exact for every split.
-// No workspace and no global atomics. Shared memory stays under half an SM at NT <= 128,
-// so the next kernel's CTAs (PDL) become resident beside this one and start streaming.
-// Every mbarrier wait is bounded (fni8_common.cuh).
+//  * warps 2-5 (one TMEM lane quarter each) reduce the S partial accumulators: every CTA
+//    writes the token columns the other ranks own to its slab of the zero-maintained GEMM
+//    workspace, the cluster synchronises (release/acquire), and each owner gathers its
+//    peers' granules with cp.async, zeroes them again, adds its own columns from TMEM and
+//    stores (staged in shared memory for 16-byte stores when the rows allow). Integer sums
+//    are associative, so the result is bit-exact for every split.
+//  * the next kernel is released (programmatic dependent launch) once the partial sums
+//    are published; its weight loads then queue behind this kernel's.
+// Shared memory stays under half an SM up to NT = 128, so two CTAs (or this kernel and
+// the next) share an SM. Every mbarrier wait is bounded (fni8_common.cuh).
 #include "fni8_common.cuh"
 #include "gemm_internal.h"
 

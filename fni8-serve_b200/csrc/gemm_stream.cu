@@ -218,9 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&full[stage], C::STAGE);
         tma_load_2d(&tmW, &full[stage], sw, k * BK, tile * BNW);
       }
-      // Pull the following weight tiles of this CTA into L2 as well, so HBM keeps
-      // streaming while the upstream kernel finishes (bounded so the prefetched set of
-      // all CTAs stays well inside the 126 MB L2).
+      // Optionally pull the following weight tiles of this CTA into L2 as well
+      // (kL2AheadUnits, none by default).
       {
         const int64_t l2_end = (u1 - pre_end) < kL2AheadUnits ? u1 : pre_end + kL2AheadUnits;
         for (int64_t u = pre_end; u < l2_end; ++u) {

@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           pre_row[pre] = tc.row0;
           pre_k[pre] = k;
         }
-        {  // weight tiles of the next units into L2 while the upstream kernel drains
+        {  // weight tiles of the next units into L2 (epi.l2ahead of them, none by default)
           int tt = t, kk = k, nb = tc.n_blk;
           for (int i = 0; i < epi.l2ahead && tt < total; ++i) {
             tma_prefetch_l2_2d(&tmB, kk * BK, nb * BN + b_off);

@@ -43,6 +43,10 @@ int skinny_status_read_and_clear(int* code);
 // of a split K range cross the zero-maintained GEMM workspace and are zeroed again.
 constexpr int64_t kSplitkMaxM = 256;
 bool splitk_supported(int64_t M, int64_t N, int64_t K);
+// Clusters of S CTAs (`threads` threads, `smem` bytes of dynamic shared memory) that can
+// be resident at once; -1 when the runtime cannot tell.
+int max_active_clusters(int threads, int smem, int S);
+
 // The split-K plan for this shape splits K (S > 1) and every one of its clusters can be
 // resident at once.
 bool splitk_split_one_wave(int64_t M, int64_t N, int64_t K);

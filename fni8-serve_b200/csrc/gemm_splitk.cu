@@ -481,20 +481,21 @@ static cudaError_t configure_splitk(int dev) {
   return e;
 }
 
-// Empty kernel with the split-K kernel's block size: the occupancy calculator's stand-in.
-// (Asked about the split-K kernel itself, the CUDA 12.9 runtime answers one CTA per SM at
-// any shared-memory size, while two of its CTAs measurably run on one SM together.)
-static __global__ void __launch_bounds__(splitk::kThreads, 1) splitk_occupancy_standin() {}
+// Empty kernel: the occupancy calculator's stand-in for the tcgen05 kernels. (Asked about
+// the split-K kernel itself, the CUDA 12.9 runtime answers one CTA per SM at any
+// shared-memory size, while two of its CTAs measurably run on one SM together.)
+static __global__ void __launch_bounds__(1024, 1) occupancy_standin() {}
 
-// How many S-CTA clusters of split-K CTAs with `smem` bytes of shared memory can be
-// resident at once (clusters live inside one GPC, so this is below SMs x CTAs-per-SM / S).
+// How many S-CTA clusters of `threads`-thread CTAs with `smem` bytes of shared memory can
+// be resident at once (clusters live inside one GPC, so this is below SMs x CTAs-per-SM /
+// S). Registers are not modelled (the callers' kernels fit two CTAs per SM by registers).
 // -1 when the runtime cannot tell (no device).
-static int max_clusters(int smem, int S) {
+int max_active_clusters(int threads, int smem, int S) {
   static bool configured[kMaxDevices] = {};
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) return -1;
   if (!configured[dev]) {
-    if (cudaFuncSetAttribute(splitk_occupancy_standin, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024) !=
+    if (cudaFuncSetAttribute(occupancy_standin, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024) !=
         cudaSuccess) {
       (void)cudaGetLastError();
       return -1;
@@ -503,7 +504,7 @@ static int max_clusters(int smem, int S) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(S);
-  cfg.blockDim = dim3(splitk::kThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -513,7 +514,7 @@ static int max_clusters(int smem, int S) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = -1;
-  if (cudaOccupancyMaxActiveClusters(&n, splitk_occupancy_standin, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, occupancy_standin, &cfg) != cudaSuccess) {
     (void)cudaGetLastError();
     return -1;
   }
@@ -528,7 +529,7 @@ static int max_clusters(int nt, int smem, int S) {
   const int dev = current_device();
   for (int i = 0; i < used; ++i)
     if (cache[i].dev == dev && cache[i].smem == smem && cache[i].S == S) return cache[i].n;
-  const int n = max_clusters(smem, S);
+  const int n = max_active_clusters(splitk::kThreads, smem, S);
   if (n >= 0 && used < 64) cache[used++] = Entry{dev, smem, S, n};
   return n;
 }

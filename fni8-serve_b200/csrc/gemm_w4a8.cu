@@ -65,11 +65,15 @@ struct Cfg {
 // Columns of the token share each cluster rank owns (a multiple of 4).
 __host__ __device__ __forceinline__ int split_share(int mcols, int S) { return ((mcols + S - 1) / S + 3) & ~3; }
 
+// Per-byte sign extension of 4-bit values (0..15 in each byte) to int8: bit 3 set means
+// negative, i.e. the high nibble becomes 0xF. (v & 0x08) * 0x1E is 0xF0 or 0 in every byte,
+// so the multiply never carries into the next byte: three integer ops per 4 values.
+__device__ __forceinline__ uint32_t sext4_bytes(uint32_t v) { return v | ((v & 0x08080808u) * 0x1Eu); }
+
 // 4 packed bytes (8 signed nibbles, element 2j low) -> 8 int8 values, in element order.
 __device__ __forceinline__ void unpack_word(uint32_t w, uint32_t& lo4, uint32_t& hi4) {
-  const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
-  const uint32_t el = __vsub4(lo ^ 0x08080808u, 0x08080808u);  // per-byte sign extension
-  const uint32_t eh = __vsub4(hi ^ 0x08080808u, 0x08080808u);
+  const uint32_t el = sext4_bytes(w & 0x0F0F0F0Fu);
+  const uint32_t eh = sext4_bytes((w >> 4) & 0x0F0F0F0Fu);
   lo4 = __byte_perm(el, eh, 0x5140);  // elements 0..3 of the word
   hi4 = __byte_perm(el, eh, 0x7362);  // elements 4..7
 }
@@ -81,8 +85,9 @@ __device__ __forceinline__ void emit_col(const Epi& epi, int m, int n, float v, 
   static_cast<T*>(epi.out)[static_cast<int64_t>(m) * epi.ldo + n] = from_f32<T>(y);
 }
 
+// Up to 32 tokens two CTAs share an SM (the plan counts on it): registers capped for that.
 template <int NT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, NT <= 32 ? 2 : 1)
     w4a8_splitk_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmX, Epi epi,
                        int M, int N, int K, int STG, uint4* ws) {
   using C = Cfg<NT>;
@@ -393,7 +398,7 @@ struct W4Plan {
 
 // One launch covers up to 64 tokens. Up to 32 tokens a CTA fits in half an SM (registers
 // and ~113 KB of shared memory), so S brings the grid to twice the SM count; 64 tokens take
-// a whole SM. The ring fills the shared-memory budget next to the unpacked slots (at most
+// a whole SM. S is then lowered until every cluster can be resident at once. The ring fills the shared-memory budget next to the unpacked slots (at most
 // 8 stages) and, drained, also holds the owner's landing area.
 static bool plan_w4(int64_t M, int64_t N, int64_t K, W4Plan* p) {
   if (M < 1 || N < 1 || K < w4::BK) return false;
@@ -413,6 +418,13 @@ static bool plan_w4(int64_t M, int64_t N, int64_t K, W4Plan* p) {
   const int fixed = 1024 + w4::kASlots * w4::A_BYTES + w4::kBarBytes;
   int stages = ((two ? 113 : 225) * 1024 - fixed) / stage;
   if (stages > w4::kMaxStages) stages = w4::kMaxStages;
+  const int smem = fixed + stages * stage;
+  // every cluster resident at once (a second wave of clusters doubles the time)
+  while (S > 1) {
+    const int mc = max_active_clusters(w4::kThreads, smem, S);
+    if (mc < 0 || n_tiles <= mc) break;
+    --S;
+  }
   const int share = ((nt + S - 1) / S + 3) & ~3;
   const int land = (S - 1) * share * w4::BNW * 4;
   if (stages < 2 || land > w4::kASlots * w4::A_BYTES + stages * stage) return false;

@@ -663,7 +663,30 @@ def run_config3(args, world, rank, dev):
                         "kernel": "w8a8_tile_kernel<grouped> (gate_up + down, all 128 experts)",
                         "weights_gbs": round(wbytes / ((t_gu + t_dn) * 1e-3) / 1e9, 1),
                         "note": "309 GOP vs 604 MB of weights: tensor (69 us) and HBM (92 us) bounds are close"}
-    line["e2e"] = None
+    # end to end: H2D of the step's tokens and router logits (one pinned buffer), routing +
+    # experts (a CUDA graph per input slot on one GPU; eager under expert parallelism, whose
+    # all_to_all split sizes visit the host), D2H of the layer output; three streams
+    nx, nl = x.numel() * 2, logits.numel() * 4
+    hin = torch.empty(nx + nl, dtype=torch.uint8).pin_memory()
+    hin[:nx].copy_(x.reshape(-1).view(torch.uint8).cpu())
+    hin[nx:].copy_(logits.reshape(-1).view(torch.uint8).cpu())
+    hout = torch.empty(T, H, dtype=x.dtype).pin_memory()
+
+    def layer(xd):
+        xv = xd[:nx].view(x.dtype).view(T, H)
+        lv = xd[nx:].view(torch.float32).view(T, E)
+        topi, topw = moe.route(lv, k)
+        return moe.experts(xv, topi, topw, stack) if world == 1 else ep(xv, topi, topw)
+
+    slots = [torch.empty_like(hin, device=dev) for _ in range(2)]
+    fn = graph_per_slot(slots, layer) if world == 1 else layer
+    e2e_ms = time_pipelined([(hin, slots, fn, hout)], args.steps, args.warmup, world) / args.steps
+    del fn
+    line["e2e"] = {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": nx + nl,
+                   "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": round(e2e_ms, 4),
+                   "api": ("fni8.moe route + experts captured in a CUDA graph per input slot" if world == 1 else
+                           "fni8.moe route + ExpertParallelMoE (eager)") +
+                          "; pinned host buffers; H2D, layer and D2H on three streams, steps pipelined"}
     line["gpu_launches"] = 12 * args.steps
     line["clocks"] = clk.summary()
     return line, None
@@ -707,7 +730,30 @@ def run_config4(args, world, rank, dev):
     line["roofline"] = {"bound": "tensor", "achieved": per["M4096_shard"]["TOP/s"], "peak": INT8_DENSE_NOMINAL_TOPS,
                         "unit": "TOP/s", "frac": round(per["M4096_shard"]["TOP/s"] / INT8_DENSE_NOMINAL_TOPS, 3),
                         "traffic": committed_traffic("sweep_m4096"), "kernel": "w8a8_tile_kernel, CTA pairs (M=4096 shard)"}
-    line["e2e"] = None
+    # end to end: H2D of the three activation batches (one pinned buffer), the three linears
+    # (a CUDA graph per input slot on one GPU; eager with the all-gather otherwise), D2H of
+    # the full [M, N] outputs gathered into one buffer; three streams
+    sizes = [x.numel() for x in xs]
+    hin = torch.cat([x.reshape(-1) for x in xs]).cpu().pin_memory()
+    hout = torch.empty(sum(M * N for M in Ms), dtype=torch.float16).pin_memory()
+
+    def sweep(xd):
+        outs, off = [], 0
+        for M, n in zip(Ms, sizes):
+            xv = xd[off:off + n].view(M, K)
+            outs.append(cp(xv) if cp is not None else fni8.linear(xv, shard))
+            off += n
+        return torch.cat([o.reshape(-1) for o in outs])
+
+    slots = [torch.empty_like(hin, device=dev) for _ in range(2)]
+    fn = graph_per_slot(slots, sweep) if world == 1 else sweep
+    e2e_ms = time_pipelined([(hin, slots, fn, hout)], args.steps, args.warmup, world) / args.steps
+    del fn
+    line["e2e"] = {"value": round(ops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TOP/s", "h2d_bytes_per_step": hin.numel() * 2,
+                   "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": round(e2e_ms, 4),
+                   "api": ("fni8.linear x3 captured in a CUDA graph per input slot" if world == 1 else
+                           "ColumnParallelLinearW8A8 (eager, NCCL all-gather)") +
+                          "; pinned host buffers; H2D, linears and D2H on three streams, steps pipelined"}
     line["gpu_launches"] = 6 * args.steps
     line["clocks"] = clk.summary()
     return line, None

@@ -15,7 +15,9 @@ Activations cross NVLink as int8 (half the bytes of fp16). The split sizes are t
 values that visit the host (one small copy per layer, needed by all_to_all_single).
 
 Column parallel: rank r holds rows [r*N/P, (r+1)*N/P) of W and its scales, computes
-y[:, slice] with the local GEMM and all_gathers the slices.
+y[:, slice] with the local GEMM and all_gathers the slices. Large batches go in row chunks
+whose all_gathers run asynchronously, so chunk c's exchange over NVLink overlaps the GEMM
+of chunk c+1; rows are independent, so the result is the same bit for bit.
 """
 from __future__ import annotations
 
@@ -135,20 +137,31 @@ def shard_rows(qt: QTensor, world: int, rank: int) -> QTensor:
 class ColumnParallelLinearW8A8:
     """y = x W^T with W's output channels sharded over the ranks of `group`."""
 
-    def __init__(self, shard: QTensor, group=None, matmul=linear):
+    def __init__(self, shard: QTensor, group=None, matmul=linear, chunk_rows: int = 1024):
         self.shard = shard
         self.group = group
         self.world = dist.get_world_size(group)
         self.matmul = matmul  # fni8.linear (the sm_100a kernels) unless a test swaps it
+        # batches of at least 2 x chunk_rows rows are computed and exchanged in chunks
+        self.chunk_rows = chunk_rows
 
     def __call__(self, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
         K = x.shape[-1]
         x2 = x.reshape(-1, K)
         M = x2.shape[0]
         n = self.shard.data.shape[0]
-        y = self.matmul(x2, self.shard, bias)
         if self.world == 1:
-            return y.reshape(*x.shape[:-1], n)
-        parts = torch.empty((self.world * M, n), dtype=y.dtype, device=y.device)
-        dist.all_gather_into_tensor(parts, y.contiguous(), group=self.group)
-        return parts.view(self.world, M, n).permute(1, 0, 2).reshape(*x.shape[:-1], self.world * n)
+            return self.matmul(x2, self.shard, bias).reshape(*x.shape[:-1], n)
+        step = self.chunk_rows if M >= 2 * self.chunk_rows else max(M, 1)
+        pending = []
+        for r0 in range(0, M, step):
+            r1 = min(M, r0 + step)
+            y = self.matmul(x2[r0:r1], self.shard, bias).contiguous()
+            parts = torch.empty((self.world * (r1 - r0), n), dtype=y.dtype, device=y.device)
+            work = dist.all_gather_into_tensor(parts, y, group=self.group, async_op=True)
+            pending.append((r0, r1, y, parts, work))
+        out = torch.empty((M, self.world * n), dtype=pending[0][2].dtype if pending else x.dtype, device=x.device)
+        for r0, r1, y, parts, work in pending:
+            work.wait()  # the current stream waits for this chunk's exchange
+            out[r0:r1].view(r1 - r0, self.world, n).copy_(parts.view(self.world, r1 - r0, n).permute(1, 0, 2))
+        return out.reshape(*x.shape[:-1], self.world * n)

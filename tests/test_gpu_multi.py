@@ -86,11 +86,13 @@ def _cp_worker(rank, world, port, errq):
         q, s = quantize_int8_rowwise(0.02 * torch.randn(N, K, generator=g, device=dev))
         full = QTensor(q, s.view(-1))
         cp = ColumnParallelLinearW8A8(shard_rows(full, world, rank))
+        cpc = ColumnParallelLinearW8A8(shard_rows(full, world, rank), chunk_rows=128)  # 300 rows: 3 chunks
         for M in (1, 16, 300):
             x = torch.randn(M, K, generator=g, device=dev).half()
-            got = cp(x)
             ref = fni8.linear(x, full)
-            assert torch.equal(got, ref), (M, (got.float() - ref.float()).abs().max().item())
+            for layer in (cp, cpc):
+                got = layer(x)
+                assert torch.equal(got, ref), (M, (got.float() - ref.float()).abs().max().item())
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:

@@ -126,6 +126,9 @@ def _cp_worker(rank, world, port, errq):
         cp = ColumnParallelLinearW8A8(shard_rows(full, world, rank), matmul=mm)
         got = cp(x)
         assert torch.equal(got, O.linear_w8a8(x, wq, ws, exact=False))
+        # row chunks with asynchronous exchanges (7 rows in chunks of 3): same result
+        cpc = ColumnParallelLinearW8A8(shard_rows(full, world, rank), matmul=mm, chunk_rows=3)
+        assert torch.equal(cpc(x), O.linear_w8a8(x, wq, ws, exact=False))
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:

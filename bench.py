@@ -666,7 +666,7 @@ def run_config3(args, world, rank, dev):
                         "both_grouped_launches_tops": round(ach, 1),
                         "weights_gbs": round(wbytes / ((t_gu + t_dn) * 1e-3) / 1e9, 1),
                         "note": "309 GOP vs 604 MB of weights: tensor (69 us) and HBM (92 us) bounds are close; "
-                                "L2-to-SM traffic 3.5x DRAM (profiles/moe_grouped_gateup_full.md)"}
+                                "L2-to-SM traffic 3.5x DRAM (ncu)"}
     # end to end: H2D of the step's tokens and router logits (one pinned buffer), routing +
     # experts (a CUDA graph per input slot on one GPU; eager under expert parallelism, whose
     # all_to_all split sizes visit the host), D2H of the layer output; three streams

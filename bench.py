@@ -623,15 +623,19 @@ def run_config3(args, world, rank, dev):
             ms = time_graph(step, args.steps, args.warmup, world) / args.steps
         timing = "CUDA graph replay"
     else:
-        ep = ExpertParallelMoE(stack, E)
+        ep = ExpertParallelMoE(stack, E, max_tokens=T)
 
         def step():
             topi, topw = moe.route(logits, k)
             return ep(x, topi, topw)
 
         with ClockSampler(dev) as clk:
-            ms = time_eager(step, args.steps, args.warmup, world) / args.steps
-        timing = "eager (all_to_all split sizes visit the host), CUDA events"
+            if ep.transport == "p2p":  # no host sync in the layer: CUDA graph replay
+                ms = time_graph(step, args.steps, args.warmup, world) / args.steps
+            else:
+                ms = time_eager(step, args.steps, args.warmup, world) / args.steps
+        timing = ("CUDA graph replay (peer-memory exchange over NVLink)" if ep.transport == "p2p" else
+                  "eager (all_to_all split sizes visit the host), CUDA events")
     # grouped-GEMM share: the two grouped launches alone, on the routed inputs
     topi, topw = moe.route(logits, k)
     from fni8.moe import grouped_gemm, plan
@@ -683,13 +687,17 @@ def run_config3(args, world, rank, dev):
         return moe.experts(xv, topi, topw, stack) if world == 1 else ep(xv, topi, topw)
 
     slots = [torch.empty_like(hin, device=dev) for _ in range(2)]
-    fn = graph_per_slot(slots, layer) if world == 1 else layer
+    graphed = world == 1 or ep.transport == "p2p"
+    fn = graph_per_slot(slots, layer) if graphed else layer
     e2e_ms = time_pipelined([(hin, slots, fn, hout)], args.steps, args.warmup, world) / args.steps
     del fn
+    if world > 1:
+        ep.close()
     line["e2e"] = {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": nx + nl,
                    "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": round(e2e_ms, 4),
-                   "api": ("fni8.moe route + experts captured in a CUDA graph per input slot" if world == 1 else
-                           "fni8.moe route + ExpertParallelMoE (eager)") +
+                   "api": ("fni8.moe route + experts" if world == 1 else f"fni8.moe route + ExpertParallelMoE "
+                           f"({ep.transport})") + (" captured in a CUDA graph per input slot" if graphed else
+                                                   " (eager)") +
                           "; pinned host buffers; H2D, layer and D2H on three streams, steps pipelined"}
     line["gpu_launches"] = 12 * args.steps
     line["clocks"] = clk.summary()

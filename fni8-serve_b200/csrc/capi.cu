@@ -226,12 +226,13 @@ extern "C" int fni8_device_status(int* code_out) {
   if (code_out == nullptr) return fail(FNI8_ERR_INVALID, "null code_out");
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_status(e, "cudaDeviceSynchronize");
-  int codes[5] = {0, 0, 0, 0, 0};
+  int codes[6] = {0, 0, 0, 0, 0, 0};
   if (int s = tile_status_read_and_clear(&codes[0])) return s;
   if (int s = stream_status_read_and_clear(&codes[1])) return s;
   if (int s = skinny_status_read_and_clear(&codes[2])) return s;
   if (int s = splitk_status_read_and_clear(&codes[3])) return s;
   if (int s = w4a8_status_read_and_clear(&codes[4])) return s;
+  if (int s = ep_status_read_and_clear(&codes[5])) return s;
   *code_out = 0;
   for (int v : codes)
     if (*code_out == 0) *code_out = v;

@@ -1,0 +1,225 @@
+// Expert-parallel row exchange over NVLink / NVSwitch peer memory (one process per GPU).
+//
+// The routed rows of an expert-parallel MoE layer move between GPUs as plain stores into
+// peer memory mapped with CUDA IPC, so the split sizes never visit the host and the layer
+// has no NCCL all_to_all:
+//
+//   dispatch  local rows sorted by expert (the plan) -> the owner rank d of the expert, at
+//             dst_base[d][local expert] + the row's rank among this rank's rows of that
+//             expert: int8 row, fp32 scale and a tag (source rank << 24 | slot)
+//   return    every received row's expert output -> the back buffer of its source rank at
+//             the slot index, where the source combines its tokens
+//
+// Ordering between ranks is the caller's: after each exchange kernel every rank runs a
+// small NCCL all_reduce on the same stream, which a rank passes only once every rank's
+// exchange kernel has completed. No kernel here waits on another GPU. Every store is
+// checked against the receiving buffer's capacity; a row that would not fit is skipped and
+// recorded in this file's status word (read through fni8_device_status).
+#include "fni8_common.cuh"
+#include "gemm_internal.h"
+
+#include "fni8_b200.h"
+
+#include <string.h>
+
+namespace fni8b {
+namespace ep {
+
+constexpr int kMaxPeers = 8;
+constexpr int kMaxE = 1024;
+enum : int { kCodeDispatchOverflow = 0x701, kCodeReturnOverflow = 0x702 };
+
+static __device__ int g_status;
+
+struct Peers {
+  void* p[kMaxPeers];
+};
+
+// One warp per sorted row. offsets[E + 1]: first sorted row of each expert (offsets[E] =
+// valid rows); dst_base[P * El]: where this rank's rows of (owner d, local expert el)
+// start in d's receive buffers.
+__global__ void dispatch_kernel(const int8_t* __restrict__ q, const float* __restrict__ scale,
+                                const int32_t* __restrict__ slot_of_row, const int32_t* __restrict__ offsets, int E,
+                                int El, int k, int H, const int32_t* __restrict__ dst_base, int me, Peers pq, Peers ps,
+                                Peers ptag, int64_t cap_rows) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ int s_off[kMaxE + 1];
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) s_off[i] = offsets[i];
+  __syncthreads();
+  const int n = s_off[E];
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5); r < n;
+       r += static_cast<int64_t>(gridDim.x) * warps) {
+    int lo = 0, hi = E - 1;  // the expert whose rows contain r: largest e with s_off[e] <= r
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_off[mid] <= r) lo = mid;
+      else hi = mid - 1;
+    }
+    const int e = lo, d = e / El, el = e - d * El;
+    const int64_t pos = static_cast<int64_t>(dst_base[d * El + el]) + (r - s_off[e]);
+    if (pos < 0 || pos >= cap_rows) {  // uniform over the warp
+      if (lane == 0) atomicExch(&g_status, kCodeDispatchOverflow);
+      continue;
+    }
+    const int slot = slot_of_row[r];
+    const int64_t t = slot / k;
+    const uint4* src = reinterpret_cast<const uint4*>(q + t * H);
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<int8_t*>(pq.p[d]) + pos * H);
+    for (int c = lane; c < H / 16; c += 32) dst[c] = __ldg(src + c);
+    if (lane == 0) {
+      static_cast<float*>(ps.p[d])[pos] = __ldg(scale + t);
+      static_cast<int32_t*>(ptag.p[d])[pos] = (me << 24) | slot;
+    }
+  }
+  __threadfence_system();
+}
+
+// One warp per received row i < *n_recv: y[i] -> back buffer of the tag's source rank at
+// the tag's slot.
+template <typename T>
+__global__ void return_kernel(const T* __restrict__ y, const int32_t* __restrict__ n_recv, int64_t cap_rows,
+                              const int32_t* __restrict__ tag, int H, Peers pb, int P, int64_t back_rows) {
+  pdl_launch_dependents();
+  pdl_wait();
+  int64_t n = *n_recv;
+  n = n < cap_rows ? n : cap_rows;
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  const int chunks = H * static_cast<int>(sizeof(T)) / 16;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5); i < n;
+       i += static_cast<int64_t>(gridDim.x) * warps) {
+    const uint32_t tg = static_cast<uint32_t>(tag[i]);
+    const int src = static_cast<int>(tg >> 24);
+    const int64_t slot = static_cast<int64_t>(tg & 0xFFFFFFu);
+    if (src >= P || slot >= back_rows) {  // uniform over the warp
+      if (lane == 0) atomicExch(&g_status, kCodeReturnOverflow);
+      continue;
+    }
+    const uint4* s = reinterpret_cast<const uint4*>(y + i * H);
+    uint4* d = reinterpret_cast<uint4*>(static_cast<T*>(pb.p[src]) + slot * H);
+    for (int c = lane; c < chunks; c += 32) d[c] = __ldg(s + c);
+  }
+  __threadfence_system();
+}
+
+}  // namespace ep
+}  // namespace fni8b
+
+using namespace fni8b;
+using namespace fni8h;
+
+namespace fni8h {
+int ep_status_read_and_clear(int* code) {
+  int v = 0, z = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, ep::g_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "read expert-exchange status");
+  e = cudaMemcpyToSymbol(ep::g_status, &z, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "clear expert-exchange status");
+  *code = v;
+  return FNI8_OK;
+}
+}  // namespace fni8h
+
+static_assert(sizeof(cudaIpcMemHandle_t) == FNI8_IPC_HANDLE_BYTES, "IPC handle size");
+
+extern "C" int fni8_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (ptr == nullptr || handle == nullptr || bytes == 0) return fail(FNI8_ERR_INVALID, "ipc_alloc: bad arguments");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_status(e, "cudaMalloc(ipc buffer)");
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_status(e, "cudaIpcGetMemHandle");
+  }
+  *ptr = p;
+  return FNI8_OK;
+}
+
+extern "C" int fni8_ipc_open(const void* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) return fail(FNI8_ERR_INVALID, "ipc_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_status(e, "cudaIpcOpenMemHandle");
+  return FNI8_OK;
+}
+
+extern "C" int fni8_ipc_close(void* ptr) {
+  if (ptr == nullptr) return FNI8_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return cuda_status(e, "cudaIpcCloseMemHandle");
+  return FNI8_OK;
+}
+
+extern "C" int fni8_ipc_free(void* ptr) {
+  if (ptr == nullptr) return FNI8_OK;
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return cuda_status(e, "cudaFree(ipc buffer)");
+  return FNI8_OK;
+}
+
+static int load_peers(ep::Peers* out, void* const* ptrs, int P, const char* what) {
+  for (int i = 0; i < ep::kMaxPeers; ++i) out->p[i] = nullptr;
+  for (int i = 0; i < P; ++i) {
+    if (ptrs[i] == nullptr) return fail(FNI8_ERR_INVALID, "%s: null peer buffer %d", what, i);
+    out->p[i] = ptrs[i];
+  }
+  return FNI8_OK;
+}
+
+extern "C" int fni8_ep_dispatch_i8(const int8_t* q, const float* scale, const int32_t* slot_of_row,
+                                   const int32_t* offsets, int64_t E, int64_t world, int64_t rank, int64_t top_k,
+                                   int64_t H, const int32_t* dst_base, void* const* peer_q, void* const* peer_scale,
+                                   void* const* peer_tag, int64_t cap_rows, int64_t max_rows, void* stream) {
+  if (world < 1 || world > ep::kMaxPeers || rank < 0 || rank >= world)
+    return fail(FNI8_ERR_INVALID, "ep_dispatch: 1 <= world <= %d, 0 <= rank < world", ep::kMaxPeers);
+  if (E <= 0 || E > ep::kMaxE || E % world != 0) return fail(FNI8_ERR_INVALID, "ep_dispatch: E must split over the ranks");
+  if (H <= 0 || H % 16 != 0) return fail(FNI8_ERR_UNSUPPORTED, "ep_dispatch: H must be a multiple of 16");
+  if (top_k <= 0 || cap_rows < 0 || max_rows < 0) return fail(FNI8_ERR_INVALID, "ep_dispatch: bad sizes");
+  if (max_rows >= (1LL << 24)) return fail(FNI8_ERR_UNSUPPORTED, "ep_dispatch: at most 2^24 slots per rank");
+  if (max_rows == 0) return FNI8_OK;
+  if (!q || !scale || !slot_of_row || !offsets || !dst_base || !peer_q || !peer_scale || !peer_tag)
+    return fail(FNI8_ERR_INVALID, "ep_dispatch: null pointer");
+  if (reinterpret_cast<uintptr_t>(q) & 15u) return fail(FNI8_ERR_ALIGN, "ep_dispatch: rows must be 16-byte aligned");
+  ep::Peers pq, ps, pt;
+  if (int s = load_peers(&pq, peer_q, (int)world, "ep_dispatch")) return s;
+  if (int s = load_peers(&ps, peer_scale, (int)world, "ep_dispatch")) return s;
+  if (int s = load_peers(&pt, peer_tag, (int)world, "ep_dispatch")) return s;
+  for (int i = 0; i < (int)world; ++i)
+    if (reinterpret_cast<uintptr_t>(pq.p[i]) & 15u) return fail(FNI8_ERR_ALIGN, "ep_dispatch: peer rows must be 16-byte aligned");
+  const int64_t blocks = (max_rows + 7) / 8;
+  launch_pdl(ep::dispatch_kernel, dim3((int)(blocks < 148 * 16 ? blocks : 148 * 16)), dim3(256), 0,
+             static_cast<cudaStream_t>(stream), q, scale, slot_of_row, offsets, (int)E, (int)(E / world), (int)top_k,
+             (int)H, dst_base, (int)rank, pq, ps, pt, cap_rows);
+  FNI8_CHECK_LAUNCH("ep_dispatch");
+  return FNI8_OK;
+}
+
+extern "C" int fni8_ep_return(const void* y, int dtype, const int32_t* n_recv, int64_t cap_rows, const int32_t* tag,
+                              int64_t H, int64_t world, void* const* peer_back, int64_t back_rows, void* stream) {
+  if (world < 1 || world > ep::kMaxPeers) return fail(FNI8_ERR_INVALID, "ep_return: 1 <= world <= %d", ep::kMaxPeers);
+  if (dtype != FNI8_F16 && dtype != FNI8_BF16) return fail(FNI8_ERR_INVALID, "ep_return: dtype");
+  if (H <= 0 || H % 8 != 0) return fail(FNI8_ERR_UNSUPPORTED, "ep_return: H must be a multiple of 8");
+  if (cap_rows < 0 || back_rows < 0) return fail(FNI8_ERR_INVALID, "ep_return: bad sizes");
+  if (cap_rows == 0) return FNI8_OK;
+  if (!y || !n_recv || !tag || !peer_back) return fail(FNI8_ERR_INVALID, "ep_return: null pointer");
+  if (reinterpret_cast<uintptr_t>(y) & 15u) return fail(FNI8_ERR_ALIGN, "ep_return: rows must be 16-byte aligned");
+  ep::Peers pb;
+  if (int s = load_peers(&pb, peer_back, (int)world, "ep_return")) return s;
+  for (int i = 0; i < (int)world; ++i)
+    if (reinterpret_cast<uintptr_t>(pb.p[i]) & 15u) return fail(FNI8_ERR_ALIGN, "ep_return: peer rows must be 16-byte aligned");
+  const int64_t blocks = (cap_rows + 7) / 8;
+  const dim3 grid((int)(blocks < 148 * 16 ? blocks : 148 * 16));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == FNI8_F16)
+    launch_pdl(ep::return_kernel<__half>, grid, dim3(256), 0, st, static_cast<const __half*>(y), n_recv, cap_rows, tag,
+               (int)H, pb, (int)world, back_rows);
+  else
+    launch_pdl(ep::return_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, static_cast<const __nv_bfloat16*>(y), n_recv,
+               cap_rows, tag, (int)H, pb, (int)world, back_rows);
+  FNI8_CHECK_LAUNCH("ep_return");
+  return FNI8_OK;
+}

@@ -64,4 +64,7 @@ int w4a8_gemm(const int8_t* a, const float* a_scale, const uint8_t* w4, const fl
               void* out, int out_mode, int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes, cudaStream_t st);
 int w4a8_status_read_and_clear(int* code);
 
+// Expert-parallel exchange kernels (ep_p2p.cu): capacity-overflow status word.
+int ep_status_read_and_clear(int* code);
+
 }  // namespace fni8h

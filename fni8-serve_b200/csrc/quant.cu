@@ -246,11 +246,15 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_vec(const T* __restrict__
 template <typename T, int MAXC, int ACT, bool QUANT>
 __global__ void __launch_bounds__(kRowThreads) act_mul_vec(const T* __restrict__ x, int64_t M, int I,
                                                             T* __restrict__ out, int8_t* __restrict__ q,
-                                                            float* __restrict__ scale) {
+                                                            float* __restrict__ scale, const int32_t* __restrict__ m_dev) {
   __shared__ float red[kRowThreads / 32];
   const int nch = I >> 3;
   pdl_launch_dependents();  // dependents may start now; they wait for our completion
   pdl_wait();
+  if (m_dev != nullptr) {  // rows known only on the device: M is their upper bound
+    const int64_t m = *m_dev;
+    M = m < M ? m : M;
+  }
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const uint4* gr = reinterpret_cast<const uint4*>(x + row * 2 * static_cast<int64_t>(I));
     const uint4* ur = gr + nch;
@@ -373,12 +377,16 @@ __global__ void __launch_bounds__(32 * kWarpRows) row_warp(const T* __restrict__
                                                             const T* __restrict__ w, int64_t M, int K, float eps,
                                                             int unit_offset, T* __restrict__ out,
                                                             T* __restrict__ res_out, int8_t* __restrict__ q,
-                                                            float* __restrict__ scale) {
+                                                            float* __restrict__ scale, const int32_t* __restrict__ m_dev) {
   constexpr bool NORM = (OP == 1 || OP == 2);
   constexpr bool ACTM = (OP == 3 || OP == 4);
   constexpr bool QUANT = (OP == 0 || OP == 2 || OP == 4);
   pdl_launch_dependents();
   pdl_wait();
+  if (m_dev != nullptr) {  // rows known only on the device: M is their upper bound
+    const int64_t m = *m_dev;
+    M = m < M ? m : M;
+  }
   const int lane = threadIdx.x & 31;
   const int nch = K >> 3;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarpRows;
@@ -477,14 +485,14 @@ __global__ void __launch_bounds__(32 * kWarpRows) row_warp(const T* __restrict__
 // Launch the warp-per-row kernel for short rows (K <= 1024); returns false otherwise.
 template <typename T, int OP, int ACT>
 bool launch_row_warp(const T* x, const T* res, const T* w, int64_t M, int K, float eps, int uo, T* out, T* res_out,
-                     int8_t* q, float* s, cudaStream_t st) {
+                     int8_t* q, float* s, cudaStream_t st, const int32_t* m_dev = nullptr) {
   const int nch = K / 8;
   const int64_t ctas_needed = (M + kWarpRows - 1) / kWarpRows;
   const int grid = static_cast<int>(ctas_needed < 148LL * 8 ? ctas_needed : 148LL * 8);
   const dim3 blk(32 * kWarpRows);
-  if (nch <= 32) fni8h::launch_pdl(row_warp<T, OP, ACT, 1>, dim3(grid), blk, 0, st, x, res, w, M, K, eps, uo, out, res_out, q, s);
-  else if (nch <= 64) fni8h::launch_pdl(row_warp<T, OP, ACT, 2>, dim3(grid), blk, 0, st, x, res, w, M, K, eps, uo, out, res_out, q, s);
-  else if (nch <= 128) fni8h::launch_pdl(row_warp<T, OP, ACT, 4>, dim3(grid), blk, 0, st, x, res, w, M, K, eps, uo, out, res_out, q, s);
+  if (nch <= 32) fni8h::launch_pdl(row_warp<T, OP, ACT, 1>, dim3(grid), blk, 0, st, x, res, w, M, K, eps, uo, out, res_out, q, s, m_dev);
+  else if (nch <= 64) fni8h::launch_pdl(row_warp<T, OP, ACT, 2>, dim3(grid), blk, 0, st, x, res, w, M, K, eps, uo, out, res_out, q, s, m_dev);
+  else if (nch <= 128) fni8h::launch_pdl(row_warp<T, OP, ACT, 4>, dim3(grid), blk, 0, st, x, res, w, M, K, eps, uo, out, res_out, q, s, m_dev);
   else return false;  // longer rows: the CTA-per-row kernels spread a row over 4 warps (measured faster)
   return true;
 }
@@ -560,7 +568,8 @@ int norm_dispatch(const void* x, const void* res, const void* w, int64_t M, int6
 }
 
 template <typename T, int ACT, bool QUANT>
-int act_dispatch(const void* x, int64_t M, int64_t I, void* out, int8_t* q, float* s, cudaStream_t st) {
+int act_dispatch(const void* x, int64_t M, int64_t I, void* out, int8_t* q, float* s, cudaStream_t st,
+                 const int32_t* m_dev = nullptr) {
   const int64_t nch = I / 8;
   // QUANT with `out`: both the product and its int8 rows are written
   const bool vec = (I % 8 == 0) && aligned16(x) && (!QUANT || aligned16(q)) && (out == nullptr || aligned16(out)) &&
@@ -568,18 +577,19 @@ int act_dispatch(const void* x, int64_t M, int64_t I, void* out, int8_t* q, floa
   const T* xx = static_cast<const T*>(x);
   T* oo = static_cast<T*>(out);
   const int g = row_grid(M);
-  if (vec && launch_row_warp<T, QUANT ? 4 : 3, ACT>(xx, nullptr, nullptr, M, (int)I, 0.f, 0, oo, nullptr, q, s, st)) {
+  if (vec && launch_row_warp<T, QUANT ? 4 : 3, ACT>(xx, nullptr, nullptr, M, (int)I, 0.f, 0, oo, nullptr, q, s, st,
+                                                    m_dev)) {
     FNI8_CHECK_LAUNCH(QUANT ? "act_and_mul_quant_i8" : "act_and_mul");
     return FNI8_OK;
   }
   if (vec) {
-    if (nch <= 2 * kRowThreads) fni8h::launch_pdl(act_mul_vec<T, 2, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s);
+    if (nch <= 2 * kRowThreads) fni8h::launch_pdl(act_mul_vec<T, 2, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s, m_dev);
     else if (nch <= 4 * kRowThreads)
-      fni8h::launch_pdl(act_mul_vec<T, 4, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s);
+      fni8h::launch_pdl(act_mul_vec<T, 4, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s, m_dev);
     else if (nch <= 8 * kRowThreads)
-      fni8h::launch_pdl(act_mul_vec<T, 8, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s);
+      fni8h::launch_pdl(act_mul_vec<T, 8, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s, m_dev);
     else
-      fni8h::launch_pdl(act_mul_vec<T, 16, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s);
+      fni8h::launch_pdl(act_mul_vec<T, 16, ACT, QUANT>, dim3(g), dim3(kRowThreads), 0, st, xx, M, (int)I, oo, q, s, m_dev);
   } else {
     fni8h::launch_pdl(row_scalar<T, QUANT ? 4 : 3, ACT>, dim3(g), dim3(kRowThreads), 0, st, xx,
                       static_cast<const T*>(nullptr), static_cast<const T*>(nullptr), M, (int)I, 0.f, 0, oo,
@@ -649,7 +659,7 @@ extern "C" int fni8_rmsnorm_quant_i8(const void* x, const void* residual, const 
 }
 
 static int act_common(const void* x, int dtype, int act, int64_t M, int64_t I, void* out, int8_t* q, float* scale,
-                      void* stream, bool quant) {
+                      void* stream, bool quant, const int32_t* m_dev = nullptr) {
   if (int st = check_rows(x, dtype, M, I)) return st;
   if (act != FNI8_ACT_SILU && act != FNI8_ACT_GELU_TANH) return fni8h::fail(FNI8_ERR_INVALID, "unknown act %d", act);
   if (!quant && M > 0 && out == nullptr) return fni8h::fail(FNI8_ERR_INVALID, "null output");
@@ -658,16 +668,16 @@ static int act_common(const void* x, int dtype, int act, int64_t M, int64_t I, v
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == FNI8_F16) {
     if (act == FNI8_ACT_SILU)
-      return quant ? act_dispatch<__half, FNI8_ACT_SILU, true>(x, M, I, out, q, scale, s)
-                   : act_dispatch<__half, FNI8_ACT_SILU, false>(x, M, I, out, nullptr, nullptr, s);
-    return quant ? act_dispatch<__half, FNI8_ACT_GELU_TANH, true>(x, M, I, out, q, scale, s)
-                 : act_dispatch<__half, FNI8_ACT_GELU_TANH, false>(x, M, I, out, nullptr, nullptr, s);
+      return quant ? act_dispatch<__half, FNI8_ACT_SILU, true>(x, M, I, out, q, scale, s, m_dev)
+                   : act_dispatch<__half, FNI8_ACT_SILU, false>(x, M, I, out, nullptr, nullptr, s, m_dev);
+    return quant ? act_dispatch<__half, FNI8_ACT_GELU_TANH, true>(x, M, I, out, q, scale, s, m_dev)
+                 : act_dispatch<__half, FNI8_ACT_GELU_TANH, false>(x, M, I, out, nullptr, nullptr, s, m_dev);
   }
   if (act == FNI8_ACT_SILU)
-    return quant ? act_dispatch<__nv_bfloat16, FNI8_ACT_SILU, true>(x, M, I, out, q, scale, s)
-                 : act_dispatch<__nv_bfloat16, FNI8_ACT_SILU, false>(x, M, I, out, nullptr, nullptr, s);
-  return quant ? act_dispatch<__nv_bfloat16, FNI8_ACT_GELU_TANH, true>(x, M, I, out, q, scale, s)
-               : act_dispatch<__nv_bfloat16, FNI8_ACT_GELU_TANH, false>(x, M, I, out, nullptr, nullptr, s);
+    return quant ? act_dispatch<__nv_bfloat16, FNI8_ACT_SILU, true>(x, M, I, out, q, scale, s, m_dev)
+                 : act_dispatch<__nv_bfloat16, FNI8_ACT_SILU, false>(x, M, I, out, nullptr, nullptr, s, m_dev);
+  return quant ? act_dispatch<__nv_bfloat16, FNI8_ACT_GELU_TANH, true>(x, M, I, out, q, scale, s, m_dev)
+               : act_dispatch<__nv_bfloat16, FNI8_ACT_GELU_TANH, false>(x, M, I, out, nullptr, nullptr, s, m_dev);
 }
 
 extern "C" int fni8_act_and_mul(const void* x, int dtype, int act, int64_t M, int64_t I, void* out, void* stream) {
@@ -677,6 +687,12 @@ extern "C" int fni8_act_and_mul(const void* x, int dtype, int act, int64_t M, in
 extern "C" int fni8_act_and_mul_quant_i8(const void* x, int dtype, int act, int64_t M, int64_t I, int8_t* q,
                                          float* scale, void* stream) {
   return act_common(x, dtype, act, M, I, nullptr, q, scale, stream, true);
+}
+
+extern "C" int fni8_act_and_mul_quant_i8_rows(const void* x, int dtype, int act, int64_t M, int64_t I,
+                                              const int32_t* rows_dev, int8_t* q, float* scale, void* stream) {
+  if (M > 0 && rows_dev == nullptr) return fni8h::fail(FNI8_ERR_INVALID, "null device row count");
+  return act_common(x, dtype, act, M, I, nullptr, q, scale, stream, true, rows_dev);
 }
 
 extern "C" int fni8_act_and_mul_dual(const void* x, int dtype, int act, int64_t M, int64_t I, void* out, int8_t* q,

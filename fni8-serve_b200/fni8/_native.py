@@ -37,6 +37,7 @@ SIGNATURES: dict[str, tuple] = {
     "fni8_act_and_mul": (_i, [_p, _i, _i, _i64, _i64, _p, _p]),
     "fni8_act_and_mul_quant_i8": (_i, [_p, _i, _i, _i64, _i64, _p, _p, _p]),
     "fni8_act_and_mul_dual": (_i, [_p, _i, _i, _i64, _i64, _p, _p, _p, _p]),
+    "fni8_act_and_mul_quant_i8_rows": (_i, [_p, _i, _i, _i64, _i64, _p, _p, _p, _p]),
     "fni8_gemm_w4a8": (_i, [_p, _p, _p, _p, _i64, _p, _p, _i, _i64, _i64, _i64, _p, _sz, _p]),
     "fni8_linear_w4a8": (_i, [_p, _i, _p, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _p, _p, _sz, _p]),
     "fni8_gemm_workspace_bytes": (_sz, [_i64, _i64, _i64]),
@@ -56,6 +57,12 @@ SIGNATURES: dict[str, tuple] = {
     "fni8_moe_experts_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "fni8_moe_experts_w8a8": (_i, [_p, _i, _i64, _i64, _p, _p, _i64, _p, _p, _p, _p, _i64, _i64, _i, _p, _p, _sz,
                                    _p]),
+    "fni8_ipc_alloc": (_i, [_sz, ctypes.POINTER(_p), _p]),
+    "fni8_ipc_free": (_i, [_p]),
+    "fni8_ipc_open": (_i, [_p, ctypes.POINTER(_p)]),
+    "fni8_ipc_close": (_i, [_p]),
+    "fni8_ep_dispatch_i8": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p]),
+    "fni8_ep_return": (_i, [_p, _i, _p, _i64, _p, _i64, _i64, _p, _i64, _p]),
 }
 
 

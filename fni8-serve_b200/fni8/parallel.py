@@ -6,13 +6,18 @@ The reference has neither: its MoE runs every expert locally (fni8serve/models/m
 and its config forbids tensor parallelism on its PCIe fleet (fni8serve/config.py:40-45).
 Both are new capabilities sized for an 8 x B200 NVSwitch box.
 
-Expert parallel (rank r owns experts [r*E/P, (r+1)*E/P)):
-    quantise own tokens -> group (token, slot) pairs by expert (= by owner rank)
-    -> all_to_all of per-expert counts -> all_to_all of int8 rows + fp32 scales
-    -> grouped GEMMs over (source rank, local expert) segments
-    -> all_to_all of fp16 expert outputs back -> weighted combine.
-Activations cross NVLink as int8 (half the bytes of fp16). The split sizes are the only
-values that visit the host (one small copy per layer, needed by all_to_all_single).
+Expert parallel (rank r owns experts [r*E/P, (r+1)*E/P)), two transports:
+  p2p (CUDA tensors, one node): quantise own tokens -> group (token, slot) pairs by expert
+    -> all_gather of per-expert counts (device) -> placement computed on the device ->
+    int8 rows + scales stored straight into the owners' receive buffers (CUDA IPC peer
+    memory over NVLink) -> grouped GEMMs, one segment per local expert -> expert outputs
+    stored straight back into the sources' slot-indexed buffers -> weighted combine. Each
+    exchange is followed by a one-element NCCL all_reduce on the same stream, so a rank
+    reads its buffers only after every rank's stores are done. Nothing visits the host: the
+    layer replays from a CUDA graph.
+  nccl (any backend, gloo included): the same steps with all_to_all_single; the split
+    sizes visit the host (one small copy per layer).
+Activations cross NVLink as int8 (half the bytes of fp16).
 
 Column parallel: rank r holds rows [r*N/P, (r+1)*N/P) of W and its scales, computes
 y[:, slice] with the local GEMM and all_gathers the slices. Large batches go in row chunks
@@ -21,12 +26,14 @@ of chunk c+1; rows are independent, so the result is the same bit for bit.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
 from . import _native as nat
 from .moe import ExpertStack, combine, grouped_gemm, plan
-from .ops import _need_cuda, _stream, _vp, act_and_mul_quant, linear, quantize_rows
+from .ops import _ACT, _DT, _need_cuda, _stream, _vp, act_and_mul_quant, linear, quantize_rows
 from .qtensor import QTensor
 
 
@@ -73,6 +80,123 @@ def segments_from_counts(recv_counts: torch.Tensor):
     return exp, off, cnt
 
 
+def p2p_placement(cnt_all: torch.Tensor, rank: int, world: int):
+    """Placement of a peer-memory exchange from cnt_all[s, e] (rows source rank s sends to
+    global expert e; experts [d*El, (d+1)*El) live on rank d). Rank d's receive buffer holds
+    its local experts one after another, each expert's rows ordered by source rank.
+    Returns (dst_base [world, El]: where this rank's rows of (d, local expert) start in d's
+    buffer; seg_off [El], seg_cnt [El]: this rank's received segments; n_recv [1])."""
+    P, E = cnt_all.shape
+    El = E // world
+    c = cnt_all.view(P, world, El).to(torch.int32)  # [source, owner, local expert]
+    tot = c.sum(0, dtype=torch.int32)  # [owner, local expert]
+    base = torch.cumsum(tot, 1, dtype=torch.int32) - tot  # exclusive over local experts
+    before = torch.cumsum(c, 0, dtype=torch.int32) - c  # exclusive over sources
+    dst_base = (base + before[rank]).contiguous()
+    return dst_base, base[rank].contiguous(), tot[rank].contiguous(), tot[rank].sum(dtype=torch.int32).reshape(1)
+
+
+def _cuda_view(ptr: int, nbytes: int, device: torch.device) -> torch.Tensor:
+    """uint8 tensor over device memory this module owns (no copy, no ownership)."""
+
+    class _Mem:
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+                                    "strides": None}
+
+    return torch.as_tensor(_Mem(), device=device)
+
+
+class PeerExchange:
+    """Receive and back buffers of one rank in one CUDA IPC allocation, mapped into every
+    peer of `group`: rows [cap] of int8 [H] + fp32 scale + int32 tag received from any rank,
+    and back rows [max_tokens * top_k] of `dtype` [H] returned to this rank's slots.
+    cap = world * max_tokens * top_k covers any routing."""
+
+    def __init__(self, max_tokens: int, top_k: int, hidden: int, dtype: torch.dtype, device: torch.device,
+                 group=None):
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the peer-memory exchange spans at most 8 ranks")
+        self.max_tokens, self.top_k, self.hidden, self.dtype = max_tokens, top_k, hidden, dtype
+        self.cap = self.world * max_tokens * top_k
+        self.back_rows = max_tokens * top_k
+        esz = torch.tensor([], dtype=dtype).element_size()
+        parts = [("q", self.cap * hidden), ("s", self.cap * 4), ("tag", self.cap * 4),
+                 ("back", self.back_rows * hidden * esz)]
+        self.off, total = {}, 0
+        for name, nbytes in parts:
+            self.off[name] = total
+            total += (nbytes + 255) // 256 * 256
+        self.nbytes = total
+        ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        nat.call("fni8_ipc_alloc", total, ctypes.byref(ptr), ctypes.cast(handle, ctypes.c_void_p))
+        self._own = ptr.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._opened = []
+        bases = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                bases.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            hb = ctypes.create_string_buffer(h, 64)
+            nat.call("fni8_ipc_open", ctypes.cast(hb, ctypes.c_void_p), ctypes.byref(p))
+            self._opened.append(p.value)
+            bases.append(p.value)
+        arr = ctypes.c_void_p * self.world
+        self._arrays = {name: arr(*[b + self.off[name] for b in bases]) for name, _ in parts}
+        self.peer = {name: ctypes.cast(a, ctypes.c_void_p) for name, a in self._arrays.items()}
+        mem = _cuda_view(self._own, total, device)
+        self.rq = mem[self.off["q"]:self.off["q"] + self.cap * hidden].view(self.cap, hidden).view(torch.int8)
+        self.rs = mem[self.off["s"]:self.off["s"] + self.cap * 4].view(torch.float32)
+        self.tag = mem[self.off["tag"]:self.off["tag"] + self.cap * 4].view(torch.int32)
+        self.back = mem[self.off["back"]:self.off["back"] + self.back_rows * hidden * esz].view(dtype).view(
+            self.back_rows, hidden)
+        self._mem = mem
+
+    def fits(self, T: int, top_k: int, hidden: int, dtype: torch.dtype) -> bool:
+        return T <= self.max_tokens and top_k == self.top_k and hidden == self.hidden and dtype == self.dtype
+
+    def close(self, group=None):
+        """Unmap the peers' buffers and free this rank's (after a barrier: no rank still
+        stores into them)."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        for p in self._opened:
+            nat.call("fni8_ipc_close", p)
+        self._opened = []
+        dist.barrier(group=group)
+        self._mem = self.rq = self.rs = self.tag = self.back = None
+        nat.call("fni8_ipc_free", self._own)
+        self._own = None
+
+
+def ep_dispatch(xq, xs, slot_of_row, offsets, E, rank, top_k, dst_base, xchg: PeerExchange, max_rows):
+    nat.call("fni8_ep_dispatch_i8", _vp(xq), _vp(xs), _vp(slot_of_row), _vp(offsets), E, xchg.world, rank, top_k,
+             xchg.hidden, _vp(dst_base), xchg.peer["q"], xchg.peer["s"], xchg.peer["tag"], xchg.cap, max_rows,
+             _stream(xq.device))
+
+
+def ep_return(y, n_recv, xchg: PeerExchange):
+    nat.call("fni8_ep_return", _vp(y), _DT[y.dtype], _vp(n_recv), xchg.cap, _vp(xchg.tag), xchg.hidden, xchg.world,
+             xchg.peer["back"], xchg.back_rows, _stream(y.device))
+
+
+def act_and_mul_quant_rows(h: torch.Tensor, rows_dev: torch.Tensor, act: str = "silu"):
+    """fni8 act_and_mul_quant over the first rows_dev[0] rows of h (the rest left as is)."""
+    I = h.shape[-1] // 2
+    M = h.shape[0]
+    q = torch.empty((M, I), dtype=torch.int8, device=h.device)
+    s = torch.empty((M,), dtype=torch.float32, device=h.device)
+    nat.call("fni8_act_and_mul_quant_i8_rows", _vp(h), _DT[h.dtype], _ACT[act], M, I, _vp(rows_dev), _vp(q), _vp(s),
+             _stream(h.device))
+    return q, s
+
+
 class KernelOps:
     """The device kernels one expert-parallel layer uses (the C ABI through fni8)."""
 
@@ -90,7 +214,13 @@ class ExpertParallelMoE:
     `ops` supplies the compute steps (default: the sm_100a kernels); the exchange logic
     around them is what this class owns."""
 
-    def __init__(self, local: ExpertStack, num_experts: int, group=None, act: str = "silu", ops=KernelOps):
+    def __init__(self, local: ExpertStack, num_experts: int, group=None, act: str = "silu", ops=KernelOps,
+                 transport: str = "auto", max_tokens: int | None = None):
+        """transport: "p2p" (peer-memory exchange, CUDA, at most 8 ranks on one node),
+        "nccl" (all_to_all_single, any backend) or "auto" (p2p for the NCCL backend with the
+        sm_100a kernels, nccl otherwise). max_tokens: the most tokens one rank passes per
+        call (p2p buffers are sized for it; default: the first call's, as a maximum over the
+        ranks)."""
         self.local = local
         self.E = num_experts
         self.group = group
@@ -101,8 +231,23 @@ class ExpertParallelMoE:
         lo, hi = expert_shard(num_experts, self.world, self.rank)
         if local.num_experts != hi - lo:
             raise ValueError("local expert stack does not match this rank's shard")
+        if transport == "auto":
+            transport = "p2p" if (ops is KernelOps and dist.get_backend(group) == "nccl" and self.world <= 8) else "nccl"
+        if transport not in ("p2p", "nccl"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.transport = transport
+        self.max_tokens = max_tokens
+        self.xchg: PeerExchange | None = None
+
+    def close(self):
+        """Release the peer-memory buffers (every rank calls it)."""
+        if self.xchg is not None:
+            self.xchg.close(self.group)
+            self.xchg = None
 
     def __call__(self, x: torch.Tensor, topi: torch.Tensor, topw: torch.Tensor) -> torch.Tensor:
+        if self.transport == "p2p":
+            return self._p2p(x, topi, topw)
         T, H = x.shape
         k = topi.shape[1]
         ops = self.ops
@@ -123,6 +268,41 @@ class ExpertParallelMoE:
         back = torch.empty((n_send, H), dtype=x.dtype, device=x.device)
         dist.all_to_all_single(back, y, send_splits, recv_splits, group=self.group)
         return ops.combine(back, ros, topw)
+
+    def _p2p(self, x: torch.Tensor, topi: torch.Tensor, topw: torch.Tensor) -> torch.Tensor:
+        _need_cuda(x, "ExpertParallelMoE")
+        T, H = x.shape
+        k = topi.shape[1]
+        P, E, El = self.world, self.E, self.E // self.world
+        if self.xchg is None:
+            mt = self.max_tokens
+            if mt is None:
+                m = torch.tensor([T], dtype=torch.int64, device=x.device)
+                dist.all_reduce(m, op=dist.ReduceOp.MAX, group=self.group)
+                mt = int(m.item())
+            self.xchg = PeerExchange(mt, k, H, x.dtype, x.device, self.group)
+            self._iota = torch.arange(El, dtype=torch.int32, device=x.device)
+            self._slots = torch.arange(mt * k, dtype=torch.int32, device=x.device)
+            self._tick = torch.zeros(1, dtype=torch.int32, device=x.device)
+        X = self.xchg
+        if not X.fits(T, k, H, x.dtype):
+            raise ValueError(f"ExpertParallelMoE: {T} tokens x top-{k} x {H} {x.dtype} exceeds the exchange buffers "
+                             f"({X.max_tokens} x top-{X.top_k} x {X.hidden} {X.dtype}); pass max_tokens")
+        xq, xs = quantize_rows(x)
+        counts, offsets, ros, sor = plan(topi, E)
+        cnt_all = torch.empty(P * E, dtype=torch.int32, device=x.device)
+        dist.all_gather_into_tensor(cnt_all, counts.to(torch.int32).contiguous(), group=self.group)
+        dst_base, seg_off, seg_cnt, n_recv = p2p_placement(cnt_all.view(P, E), self.rank, P)
+        ep_dispatch(xq, xs, sor, offsets, E, self.rank, k, dst_base, X, T * k)
+        dist.all_reduce(self._tick, op=dist.ReduceOp.MAX, group=self.group)  # every rank's rows have landed
+        L = self.local
+        h = grouped_gemm(X.rq, X.rs, L.w_gu, L.s_gu, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
+        hq, hs = act_and_mul_quant_rows(h, n_recv, self.act)
+        y = grouped_gemm(hq, hs, L.w_dn, L.s_dn, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
+        ep_return(y, n_recv, X)
+        dist.all_reduce(self._tick, op=dist.ReduceOp.MAX, group=self.group)  # every output is back at its source
+        ros_slot = torch.where(ros >= 0, self._slots[: T * k], torch.full_like(ros, -1))
+        return combine(X.back[: T * k], ros_slot, topw)
 
 
 def shard_rows(qt: QTensor, world: int, rank: int) -> QTensor:

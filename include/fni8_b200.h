@@ -111,6 +111,11 @@ FNI8_API int fni8_act_and_mul_quant_i8(const void* x, int dtype, int act, int64_
  * fni8serve/layers/mlp.py:39-40). */
 FNI8_API int fni8_act_and_mul_dual(const void* x, int dtype, int act, int64_t M, int64_t I, void* out, int8_t* q,
                                    float* scale, void* stream);
+/* fni8_act_and_mul_quant_i8 over the first *rows_dev rows of x[M, 2I] (M is their upper
+ * bound; the count lives in device memory, e.g. the rows an expert-parallel rank received;
+ * rows past it are left untouched). */
+FNI8_API int fni8_act_and_mul_quant_i8_rows(const void* x, int dtype, int act, int64_t M, int64_t I,
+                                            const int32_t* rows_dev, int8_t* q, float* scale, void* stream);
 
 /* ------------------------------------------------------------------ dense GEMM */
 /* Bytes of workspace fni8_gemm_w8a8* may use for an M x N x K problem (0 when none). */
@@ -229,6 +234,40 @@ FNI8_API int fni8_moe_experts_w8a8(const void* x, int dtype, int64_t T, int64_t 
                           int64_t top_k, const int8_t* w_gu, const float* s_gu, const int8_t* w_dn,
                           const float* s_dn, int64_t E, int64_t I, int act, void* out, void* workspace,
                           size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ expert-parallel exchange
+ * New capability: the reference runs every expert on one GPU (fni8serve/models/moe.py:99-105)
+ * and forbids tensor parallelism (fni8serve/config.py:40-45). One process per GPU; rows move
+ * between GPUs as stores into peer memory mapped with CUDA IPC. No function here waits on
+ * another GPU: after each exchange the caller orders the ranks with a collective on the
+ * same stream (every rank passes it only once every rank's exchange has completed). */
+#define FNI8_IPC_HANDLE_BYTES 64
+/* cudaMalloc'd, zeroed device buffer of `bytes` and its IPC handle (FNI8_IPC_HANDLE_BYTES
+ * bytes into `handle`); fni8_ipc_free releases it. */
+FNI8_API int fni8_ipc_alloc(size_t bytes, void** ptr, void* handle);
+FNI8_API int fni8_ipc_free(void* ptr);
+/* Map a peer process's buffer from its handle (peer access enabled on first use);
+ * fni8_ipc_close unmaps it. */
+FNI8_API int fni8_ipc_open(const void* handle, void** ptr);
+FNI8_API int fni8_ipc_close(void* ptr);
+
+/* Dispatch: the sorted rows of fni8_moe_plan (slot_of_row, offsets[E + 1]) to the ranks
+ * owning their experts (expert e lives on rank e / (E / world)). Row r of local expert el
+ * of rank d goes to position dst_base[d * (E / world) + el] + (r - offsets[e]) of rank d's
+ * receive buffers: the int8 row q[slot / top_k] (H bytes) into peer_q[d], its scale into
+ * peer_scale[d] and the tag (rank << 24 | slot) into peer_tag[d]. peer_* are `world` device
+ * pointers (this rank's own buffers at index rank); cap_rows is the rows each receive
+ * buffer holds (a row past it is skipped and reported by fni8_device_status); max_rows
+ * bounds the sorted rows (T * top_k, < 2^24). */
+FNI8_API int fni8_ep_dispatch_i8(const int8_t* q, const float* scale, const int32_t* slot_of_row,
+                                 const int32_t* offsets, int64_t E, int64_t world, int64_t rank, int64_t top_k,
+                                 int64_t H, const int32_t* dst_base, void* const* peer_q, void* const* peer_scale,
+                                 void* const* peer_tag, int64_t cap_rows, int64_t max_rows, void* stream);
+/* Return: row i < *n_recv of y[cap_rows, H] (dtype) goes to row (tag[i] & 0xFFFFFF) of the
+ * back buffer of rank tag[i] >> 24 (peer_back: `world` device pointers to [back_rows, H]
+ * buffers), where that rank combines its tokens with fni8_moe_combine. */
+FNI8_API int fni8_ep_return(const void* y, int dtype, const int32_t* n_recv, int64_t cap_rows, const int32_t* tag,
+                            int64_t H, int64_t world, void* const* peer_back, int64_t back_rows, void* stream);
 
 #ifdef __cplusplus
 }

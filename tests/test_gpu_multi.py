@@ -5,6 +5,7 @@ on each rank and exchange over NCCL; each rank checks its result against the
 single-GPU kernels on the unsharded weights, bit for bit (every row's int32 sums and
 its dequant epilogue do not depend on how the rows or columns were grouped).
 """
+import ctypes
 import datetime
 import os
 import socket
@@ -50,21 +51,43 @@ def _ep_worker(rank, world, port, errq):
         w_dn = torch.stack([q for q, _ in dn])
         s_dn = torch.stack([s.view(-1) for _, s in dn])
         lo, hi = expert_shard(E, world, rank)
-        ep = ExpertParallelMoE(ExpertStack(w_gu[lo:hi].contiguous(), s_gu[lo:hi].contiguous(),
-                                           w_dn[lo:hi].contiguous(), s_dn[lo:hi].contiguous()), E)
+        local = ExpertStack(w_gu[lo:hi].contiguous(), s_gu[lo:hi].contiguous(), w_dn[lo:hi].contiguous(),
+                            s_dn[lo:hi].contiguous())
         full = ExpertStack(w_gu, s_gu, w_dn, s_dn)
         gx = torch.Generator(device=dev).manual_seed(100 + rank)
         x = torch.randn(T, H, generator=gx, device=dev).half()
         bias = torch.zeros(E, device=dev)
         bias[0] = 3.0  # skew: expert 0 (rank 0) is popular
         topi, topw = moe.route(torch.randn(T, E, generator=gx, device=dev) + bias, k)
-        got = ep(x, topi, topw)
         ref = moe.experts(x, topi, topw, full)
-        torch.cuda.synchronize()
-        assert torch.equal(got, ref), (got.float() - ref.float()).abs().max().item()
-        # a rank with no tokens still takes every collective step
-        got0 = ep(x[:0], topi[:0], topw[:0]) if rank == 1 else ep(x, topi, topw)
-        assert got0.shape[0] == (0 if rank == 1 else T)
+        # peer-memory exchange (the default on NCCL) and the all_to_all exchange
+        for transport in ("p2p", "nccl"):
+            ep = ExpertParallelMoE(local, E, transport=transport)
+            assert ep.transport == transport
+            got = ep(x, topi, topw)
+            torch.cuda.synchronize()
+            assert torch.equal(got, ref), (transport, (got.float() - ref.float()).abs().max().item())
+            # a rank with no tokens still takes every collective step
+            got0 = ep(x[:0], topi[:0], topw[:0]) if rank == 1 else ep(x, topi, topw)
+            assert got0.shape[0] == (0 if rank == 1 else T)
+            if transport == "p2p":
+                # nothing visits the host: the layer replays from a CUDA graph
+                st = torch.cuda.Stream()
+                st.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(st):
+                    ep(x, topi, topw)
+                torch.cuda.current_stream().wait_stream(st)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    out = ep(x, topi, topw)
+                graph.replay()
+                torch.cuda.synchronize()
+                assert torch.equal(out, ref), ("graph", (out.float() - ref.float()).abs().max().item())
+                del graph, out
+                code = ctypes.c_int(0)
+                from fni8 import _native as nat
+                nat.call("fni8_device_status", ctypes.byref(code))  # no capacity overflow recorded
+                ep.close()
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # report to the parent, which fails the test

@@ -164,3 +164,32 @@ def test_exchange_helpers_single_rank():
         expert_shard(10, 4, 0)
     exp, off, cnt = segments_from_counts(torch.tensor([[2, 0, 5], [1, 3, 0]]))
     assert exp.tolist() == [0, 1, 2, 0, 1, 2] and off.tolist() == [0, 2, 2, 7, 8, 11] and cnt.tolist() == [2, 0, 5, 1, 3, 0]
+
+
+def test_p2p_placement_matches_a_sequential_layout():
+    """The device-side placement of the peer-memory exchange (parallel.p2p_placement) against
+    a plain walk over (owner, local expert, source) in buffer order."""
+    from fni8.parallel import p2p_placement
+
+    g = torch.Generator().manual_seed(11)
+    for world, E in ((2, 8), (4, 16), (8, 128)):
+        El = E // world
+        cnt = torch.randint(0, 40, (world, E), generator=g, dtype=torch.int32)
+        cnt[0, :El] = 0  # empty experts
+        # reference: rank d's buffer lists its local experts in order, each by source rank
+        start = {}
+        for d in range(world):
+            pos = 0
+            for el in range(El):
+                for s_ in range(world):
+                    start[(s_, d, el)] = pos
+                    pos += int(cnt[s_, d * El + el])
+        for rank in range(world):
+            dst_base, seg_off, seg_cnt, n_recv = p2p_placement(cnt, rank, world)
+            for d in range(world):
+                for el in range(El):
+                    assert int(dst_base[d, el]) == start[(rank, d, el)]
+            for el in range(El):
+                assert int(seg_off[el]) == start[(0, rank, el)]
+                assert int(seg_cnt[el]) == int(cnt[:, rank * El + el].sum())
+            assert int(n_recv[0]) == int(cnt[:, rank * El:(rank + 1) * El].sum())

@@ -94,7 +94,24 @@ def test_argument_validation_without_launch(lib):
                                       None) == n.ERR_UNSUPPORTED
     assert lib.fni8_moe_experts_w8a8(p, n.F16, 8, 256, p, p, 2, p, p, p, p, 600, 128, 0, p, p, 1 << 30,
                                      None) == n.ERR_UNSUPPORTED  # more experts than one grouped launch takes
+    # expert-parallel exchange: world, expert split, row width, slot range, dtype
+    peers = (ctypes.c_void_p * 2)(16, 32)
+    pp = ctypes.cast(peers, ctypes.c_void_p)
+    assert lib.fni8_ep_dispatch_i8(p, p, p, p, 16, 9, 0, 4, 512, p, pp, pp, pp, 100, 100, None) == n.ERR_INVALID
+    assert lib.fni8_ep_dispatch_i8(p, p, p, p, 15, 2, 0, 4, 512, p, pp, pp, pp, 100, 100, None) == n.ERR_INVALID
+    assert lib.fni8_ep_dispatch_i8(p, p, p, p, 16, 2, 0, 4, 520, p, pp, pp, pp, 100, 100, None) == n.ERR_UNSUPPORTED
+    assert lib.fni8_ep_dispatch_i8(p, p, p, p, 16, 2, 0, 4, 512, p, pp, pp, pp, 100, 1 << 24,
+                                   None) == n.ERR_UNSUPPORTED  # tags hold slots below 2^24
+    assert lib.fni8_ep_dispatch_i8(p, p, p, p, 16, 2, 2, 4, 512, p, pp, pp, pp, 100, 100, None) == n.ERR_INVALID
+    assert lib.fni8_ep_return(p, n.F32, p, 100, p, 512, 2, pp, 100, None) == n.ERR_INVALID
+    assert lib.fni8_ep_return(p, n.F16, p, 100, p, 12, 2, pp, 100, None) == n.ERR_UNSUPPORTED
+    assert lib.fni8_ipc_alloc(0, ctypes.byref(ctypes.c_void_p()), p) == n.ERR_INVALID
+    assert lib.fni8_ipc_open(None, ctypes.byref(ctypes.c_void_p())) == n.ERR_INVALID
+    assert lib.fni8_act_and_mul_quant_i8_rows(p, n.F16, 0, 4, 32, None, p, p, None) == n.ERR_INVALID
     # zero-size work is a successful no-op (no launch)
+    assert lib.fni8_ep_dispatch_i8(None, None, None, None, 16, 2, 0, 4, 512, None, pp, pp, pp, 0, 0, None) == n.OK
+    assert lib.fni8_ep_return(None, n.F16, None, 0, None, 512, 2, pp, 0, None) == n.OK
+    assert lib.fni8_ipc_close(None) == n.OK and lib.fni8_ipc_free(None) == n.OK
     assert lib.fni8_gemm_w8a8(None, None, None, None, None, None, None, n.F16, 0, 8, 32, None, 0, None) == n.OK
     assert lib.fni8_quantize_rows_i8(p, n.F16, 0, 32, None, None, None) == n.OK
 

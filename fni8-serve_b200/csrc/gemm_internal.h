@@ -17,7 +17,8 @@ int tile_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const floa
 int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w, const float* w_scale,
                       int64_t E, int64_t N, int64_t K, const int32_t* seg_expert, const int32_t* seg_off,
                       const int32_t* seg_cnt, int64_t S, void* out, int out_mode, int bn, bool pair,
-                      cudaStream_t st);
+                      cudaStream_t st, const int32_t* row_tag = nullptr,
+                      void* const* peer_out = nullptr, int n_peers = 0, int64_t peer_rows = 0);
 // Whether dense (prefill-size) and grouped tile GEMMs run on CTA pairs.
 bool tile_pair_enabled();
 bool grouped_pair_enabled();

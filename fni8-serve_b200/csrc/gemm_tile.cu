@@ -54,7 +54,8 @@ constexpr int kL2AheadUnits = 0;
 
 static __device__ int g_status;  // watchdog word of this file
 
-enum : int { kCodeProducer = 0x101, kCodeMma = 0x102, kCodeEpilogue = 0x103, kCodeDrain = 0x104 };
+enum : int { kCodeProducer = 0x101, kCodeMma = 0x102, kCodeEpilogue = 0x103, kCodeDrain = 0x104, kCodeScatter = 0x105 };
+constexpr int kMaxScatterPeers = 8;
 enum : int { kOutF16 = 0, kOutBF16 = 1, kOutI32 = 2 };
 
 struct Epi {
@@ -66,6 +67,13 @@ struct Epi {
   int mode;              // kOutF16 / kOutBF16 / kOutI32
   int l2ahead;           // weight k-blocks pulled into L2 (beyond the ring) before the PDL wait
   int trigger;           // next kernel released at entry (0) or after this CTA's last load (1)
+  // Row scatter (grouped, 16-bit out): output row r goes to row (row_tag[r] & 0xFFFFFF) of
+  // peer_out[row_tag[r] >> 24] ([peer_rows, N] each; a peer's memory mapped into this
+  // process), instead of out[r]. null row_tag: plain rows of `out`.
+  const int32_t* row_tag;
+  void* peer_out[kMaxScatterPeers];
+  int n_peers;
+  int64_t peer_rows;
 };
 struct Groups {
   const int32_t* expert;
@@ -139,9 +147,8 @@ __device__ __forceinline__ TileCoord decode_tile(int t, int M, int m_tiles, int 
 // rows cut by a segment end and unaligned outputs). ws/bs: the chunk's column scales and
 // bias (fp32, from shared memory).
 template <typename T>
-__device__ __forceinline__ void store_chunk(const Epi& epi, const uint32_t (&r)[32], int64_t row, int n0, int N,
-                                            float a_s, const float* ws, const float* bs, bool vec_ok) {
-  T* out = static_cast<T*>(epi.out) + row * static_cast<int64_t>(N);
+__device__ __forceinline__ void store_chunk(const Epi& epi, const uint32_t (&r)[32], int64_t row, T* out, int n0,
+                                            int N, float a_s, const float* ws, const float* bs, bool vec_ok) {
   const T* res = epi.residual ? static_cast<const T*>(epi.residual) + row * static_cast<int64_t>(N) : nullptr;
   const bool has_bias = epi.bias != nullptr;
   if (vec_ok && n0 + 32 <= N) {
@@ -454,8 +461,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       // this CTA's rows of the tile
       const int row0 = tc.row0 + static_cast<int>(half) * BM;
       const int rows_here = tc.rows_valid - static_cast<int>(half) * BM;
-      const bool valid = row_local < rows_here;
+      bool valid = row_local < rows_here;
       const int64_t row = static_cast<int64_t>(row0) + row_local;
+      // this thread's output row: out[row], or a peer's row under the row scatter
+      uint8_t* orow = nullptr;
+      if (valid && epi.mode != kOutI32) {
+        if (epi.row_tag != nullptr) {
+          const uint32_t tg = static_cast<uint32_t>(__ldg(epi.row_tag + row));
+          const int src = static_cast<int>(tg >> 24);
+          const int64_t slot = static_cast<int64_t>(tg & 0xFFFFFFu);
+          if (src < epi.n_peers && slot < epi.peer_rows) {
+            orow = static_cast<uint8_t*>(epi.peer_out[src]) + slot * static_cast<int64_t>(N) * 2;
+          } else {
+            atomicExch(&g_status, kCodeScatter);
+            valid = false;
+          }
+        } else {
+          orow = static_cast<uint8_t*>(epi.out) + row * static_cast<int64_t>(N) * 2;
+        }
+      }
       const int nb0 = tc.n_blk * BN;
       const float* wsc = epi.w_scale + static_cast<int64_t>(tc.expert) * N;
       static_assert(BN <= kEpiThreads, "one column scale per epilogue thread");
@@ -487,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       // TMA store of whole 32-row slabs; a slab cut by a segment end (grouped) or any
       // residual add takes the per-thread path
-      const bool slab_tma = tma_store && epi.residual == nullptr &&
+      const bool slab_tma = tma_store && epi.residual == nullptr && epi.row_tag == nullptr &&
                             (!GROUPED || rows_here - q * 32 >= 32) && q * 32 < rows_here;
 #pragma unroll 1
       for (int c = c_beg; c < c_beg + BN / 2; c += 32) {
@@ -530,8 +554,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else if (valid) {
           if (epi.mode == kOutI32) store_chunk_i32(epi, r, row, n0, N, vec_ok != 0);
-          else if (epi.mode == kOutF16) store_chunk<__half>(epi, r, row, n0, N, a_s, s_ws + c, s_bias + c, vec_ok != 0);
-          else store_chunk<__nv_bfloat16>(epi, r, row, n0, N, a_s, s_ws + c, s_bias + c, vec_ok != 0);
+          else if (epi.mode == kOutF16)
+            store_chunk<__half>(epi, r, row, reinterpret_cast<__half*>(orow), n0, N, a_s, s_ws + c, s_bias + c,
+                                vec_ok != 0);
+          else
+            store_chunk<__nv_bfloat16>(epi, r, row, reinterpret_cast<__nv_bfloat16*>(orow), n0, N, a_s, s_ws + c,
+                                       s_bias + c, vec_ok != 0);
         }
       }
       tc_fence_before();
@@ -701,7 +729,8 @@ int tile_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const floa
 int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w, const float* w_scale,
                       int64_t E, int64_t N, int64_t K, const int32_t* seg_expert, const int32_t* seg_off,
                       const int32_t* seg_cnt, int64_t S, void* out, int out_mode, int bn, bool pair,
-                      cudaStream_t st) {
+                      cudaStream_t st, const int32_t* row_tag, void* const* peer_out, int n_peers,
+                      int64_t peer_rows) {
   if (R <= 0 || N <= 0 || S <= 0) return FNI8_OK;
   if (S > tile::kMaxSeg) return fail(FNI8_ERR_UNSUPPORTED, "at most %d segments (got %lld)", tile::kMaxSeg, (long long)S);
   CUtensorMap ta, tb;
@@ -714,10 +743,20 @@ int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const in
   const int sms = num_sms(current_device());
   const int grid = pair ? (sms & ~1) : sms;
   const size_t esz = out_mode == tile::kOutI32 ? 4 : 2;
-  const bool vec_ok = ((N * (int64_t)esz) % 16 == 0) && (((uintptr_t)out & 15u) == 0) &&
-                      (((uintptr_t)w_scale & 15u) == 0) && ((N % 4) == 0);
+  bool aligned = ((uintptr_t)out & 15u) == 0;
+  if (row_tag != nullptr) {  // rows scattered into peers' buffers (validated by the caller)
+    epi.row_tag = row_tag;
+    epi.n_peers = n_peers;
+    epi.peer_rows = peer_rows;
+    for (int i = 0; i < n_peers; ++i) {
+      epi.peer_out[i] = peer_out[i];
+      aligned = aligned && ((uintptr_t)peer_out[i] & 15u) == 0;
+    }
+  }
+  const bool vec_ok = ((N * (int64_t)esz) % 16 == 0) && aligned && (((uintptr_t)w_scale & 15u) == 0) &&
+                      ((N % 4) == 0);
   CUtensorMap to;
-  const bool tma_store = out_tma_map(&to, out, out_mode, R, N);
+  const bool tma_store = row_tag == nullptr && out_tma_map(&to, out, out_mode, R, N);
   if (pair) {
     if (bn == 256)
       return tile::launch<256, true, true>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);

@@ -1,8 +1,8 @@
 """Generate the golden fixtures in tests/golden/*.npz from the REFERENCE's own code.
 
-Runs only where the fni8-serve sources are available (pass --reference, default
-$FNI8_REFERENCE or /root/reference); the GPU box never runs it, it only reads the
-committed .npz files. fni8-serve cannot be imported normally here because its kernels
+Runs only where the fni8-serve sources are available (pass --reference, or set
+$FNI8_REFERENCE to the checkout); the GPU box never runs it, it only reads the committed
+.npz files. fni8-serve cannot be imported normally here because its kernels
 package `fni8` is not installed, so this script:
 
   * puts this repository's drop-in `fni8` package on sys.path (only QTensor and
@@ -227,8 +227,12 @@ def gen_moe(L, scoring: str) -> dict:
 
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--reference", default=os.environ.get("FNI8_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("FNI8_REFERENCE"),
+                    help="fni8-serve checkout (default: $FNI8_REFERENCE)")
     a = ap.parse_args()
+    if a.reference is None:
+        print("pass --reference <fni8-serve checkout> or set FNI8_REFERENCE", file=sys.stderr)
+        return 2
     if not os.path.isdir(os.path.join(a.reference, "fni8serve")):
         print(f"fni8-serve sources not found under {a.reference}", file=sys.stderr)
         return 2

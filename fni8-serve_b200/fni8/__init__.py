@@ -9,14 +9,17 @@ norm.py:16, activation.py:10, models/weights.py:14-15):
 Put the directory that contains this package first on sys.path and LinearW8A8,
 RMSNorm, SiluAndMul/GeluAndMul and GatedMLP run unchanged on hand-written tcgen05 /
 TMA kernels through the C ABI of include/fni8_b200.h. `fni8.moe.SparseMoE` replaces
-the per-expert Python loop with grouped GEMMs, and `fni8.parallel` adds the
-expert-parallel and column-parallel multi-GPU forms.
+the per-expert Python loop with grouped GEMMs, `fni8.parallel` adds the
+expert-parallel and column-parallel multi-GPU forms, and `fni8.format` (FQReader,
+FQWriter, save_fni8; fni8serve/loader.py:16, convert.py:320) reads and writes the
+`.fni8` weight container.
 
 Importing the package does not load the native library; the first op does, and it
 raises if the library has not been built (there is no fallback path).
 """
-from . import quant  # noqa: F401
+from . import format, quant  # noqa: F401
 from ._native import Fni8Error
+from .format import FQReader, FQWriter, save_fni8
 from .ops import (act_and_mul, act_and_mul_quant, device_status, gemm_i32, linear, linear_q, quantize_rows,
                   rmsnorm, rmsnorm_quant)
 from .qtensor import QTensor
@@ -24,6 +27,6 @@ from .qtensor import QTensor
 __all__ = [
     "QTensor", "linear", "rmsnorm", "act_and_mul", "quant",
     "rmsnorm_quant", "act_and_mul_quant", "linear_q", "quantize_rows", "gemm_i32", "device_status",
-    "Fni8Error",
+    "Fni8Error", "FQReader", "FQWriter", "save_fni8", "format",
 ]
 __version__ = "0.1.0"

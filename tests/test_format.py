@@ -1,0 +1,155 @@
+"""The `.fni8` container (fni8.format): the call contract fni8-serve's loader, converter
+and tools use (fni8serve/loader.py:16-69, convert.py:320-356, tools/fine_tune.py:55-58),
+the round trips its own tests make (tests/test_smoke.py:36-62) and the reader's checks.
+The byte format itself is this library's (the original is defined inside the absent
+`fni8` package), so these tests pin the contract, not the bytes. Runs without a GPU."""
+import os
+
+import pytest
+import torch
+
+from fni8 import FQReader, FQWriter, QTensor, save_fni8
+
+
+def _i8(n, k, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return QTensor(torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8), torch.rand(n, generator=g) * 1e-2)
+
+
+def _i4(n, k, group, seed=1):
+    g = torch.Generator().manual_seed(seed)
+    packed = torch.randint(0, 256, (n, k // 2), generator=g, dtype=torch.int64).to(torch.uint8)
+    return QTensor(packed, torch.rand(n, k // group, generator=g), scheme="per_group_i4", group_size=group,
+                   codebook="int4")
+
+
+def _same(a: QTensor, b: QTensor):
+    assert a.scheme == b.scheme and a.group_size == b.group_size and a.codebook == b.codebook
+    assert a.data.dtype == b.data.dtype and torch.equal(a.data, b.data)
+    assert (a.scale is None) == (b.scale is None)
+    if a.scale is not None:
+        assert a.scale.dtype == b.scale.dtype and torch.equal(a.scale, b.scale)
+
+
+def _load_checkpoint(path, names=None, shard=None):
+    """fni8serve/loader.py:19-43 (load_fni8_checkpoint) restated on the same calls."""
+    with FQReader(path) as r:
+        if shard is not None:
+            idx = r.shards
+            if shard in idx.get("experts", {}):
+                names = idx["experts"][shard]
+            elif shard.startswith("pp:"):
+                names = idx["pp_stages"][int(shard[3:])]
+            else:
+                raise KeyError(shard)
+        names = names if names is not None else r.names
+        return r.load_many(names, "cpu")
+
+
+def test_round_trip_every_scheme_and_dtype(tmp_path):
+    path = str(tmp_path / "m.fni8")
+    ts = {
+        "mlp.up.weight": _i8(128, 256),
+        "mlp.down.weight": _i4(64, 128, 32),
+        "norm.weight": QTensor(torch.randn(256).half(), None, scheme="raw"),
+        "embed.weight": QTensor(torch.randn(10, 16, dtype=torch.bfloat16), None, scheme="raw"),
+        "router.bias": torch.randn(8),  # plain tensors are stored raw
+        "step": torch.tensor(7, dtype=torch.int64),  # 0-dim
+        "mask": torch.tensor([True, False, True]),
+        "empty": torch.empty(0, 4),
+    }
+    save_fni8(path, ts)
+    with FQReader(path) as r:
+        assert r.names == list(ts)
+        got = r.load_many(r.names, "cpu")
+    for name, t in ts.items():
+        want = t if isinstance(t, QTensor) else QTensor(t, None, scheme="raw")
+        _same(got[name], want)
+
+
+def test_header_fields_and_meta(tmp_path):
+    path = str(tmp_path / "m.fni8")
+    meta = {"arch": "qwen3", "weight_bits": 8, "config": {"hidden_size": 4096, "num_hidden_layers": 36}}
+    save_fni8(path, {"a.weight": _i8(32, 64)}, meta=meta)
+    with FQReader(path) as r:
+        h = r.header
+        assert h["arch"] == "qwen3" and h["quant"] == "int8" and h["version"] == 1
+        assert h["__meta__"] == meta
+        assert h["hidden_size"] == 4096  # model dimensions readable from the header
+    save_fni8(path, {"a.weight": _i4(32, 64, 32)})
+    with FQReader(path) as r:
+        assert r.header["quant"] == "int4" and r.header["arch"] == "" and r.header["__meta__"] == {}
+
+
+def test_shard_partial_loads(tmp_path):
+    path = str(tmp_path / "m.fni8")
+    ts = {f"model.layers.{i}.w": _i8(32, 64, seed=i) for i in range(4)}
+    ts.update({f"experts.{e}.gate_up": _i8(16, 64, seed=10 + e) for e in range(3)})
+    shards = {"pp_stages": [["model.layers.0.w", "model.layers.1.w"], ["model.layers.2.w", "model.layers.3.w"]],
+              "experts": {"1": ["experts.1.gate_up"], "2": ["experts.2.gate_up"]}}
+    save_fni8(path, ts, shards=shards)
+    w = _load_checkpoint(path, shard="pp:1")
+    assert set(w) == {"model.layers.2.w", "model.layers.3.w"}
+    _same(w["model.layers.3.w"], ts["model.layers.3.w"])
+    w = _load_checkpoint(path, shard="2")
+    assert set(w) == {"experts.2.gate_up"}
+    assert set(_load_checkpoint(path)) == set(ts)
+    with pytest.raises(KeyError):
+        _load_checkpoint(path, shard="nope")
+    with pytest.raises(KeyError):
+        save_fni8(path, ts, shards={"pp_stages": [["missing.w"]]})
+
+
+def test_streaming_writer(tmp_path):
+    """The converter's pattern: add tensors one by one, then finalize(meta=)."""
+    path = str(tmp_path / "m.fni8")
+    parts = [(f"layer{i}.w", _i8(64, 128, seed=i)) for i in range(5)]
+    with FQWriter(path) as w:
+        for name, qt in parts:
+            w.add(name, qt)
+        w.finalize(meta={"arch": "qwen3_moe", "weight_bits": 8})
+    with FQReader(path) as r:
+        assert r.header["arch"] == "qwen3_moe" and r.names == [n for n, _ in parts]
+        for name, qt in parts:
+            _same(r.load(name), qt)
+    with FQWriter(path) as w:  # finalize is implied on a clean exit
+        w.add("x", _i8(8, 16))
+    with FQReader(path) as r:
+        assert r.names == ["x"]
+
+
+def test_data_parts_are_page_aligned(tmp_path):
+    path = str(tmp_path / "m.fni8")
+    save_fni8(path, {"a": _i8(3, 17), "b": _i8(5, 33), "c": QTensor(torch.randn(7).half(), None, scheme="raw")})
+    with FQReader(path) as r:
+        for e in r.header["tensors"].values():
+            for part in (e["data"], e["scale"]):
+                if part is not None:
+                    assert part["offset"] % 4096 == 0
+
+
+def test_rejects_corrupt_and_foreign_files(tmp_path):
+    bad = tmp_path / "x.fni8"
+    bad.write_bytes(b"not a container at all" * 4)
+    with pytest.raises(ValueError, match="not a .fni8"):
+        FQReader(str(bad))
+    good = str(tmp_path / "m.fni8")
+    save_fni8(good, {"a": _i8(8, 16)})
+    raw = open(good, "rb").read()
+    trunc = tmp_path / "t.fni8"
+    trunc.write_bytes(raw[:-5])
+    with pytest.raises(ValueError):
+        FQReader(str(trunc))
+
+
+def test_failed_write_leaves_no_file(tmp_path):
+    path = str(tmp_path / "m.fni8")
+    with pytest.raises(TypeError):
+        with FQWriter(path) as w:
+            w.add("ok", _i8(8, 16))
+            w.add("bad", QTensor(torch.zeros(2, dtype=torch.complex64), None, scheme="raw"))
+    assert not os.path.exists(path)
+    with FQWriter(path) as w:
+        w.add("a", _i8(8, 16))
+        with pytest.raises(ValueError, match="duplicate"):
+            w.add("a", _i8(8, 16))

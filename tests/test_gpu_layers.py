@@ -245,3 +245,22 @@ def test_sparse_moe_dropin_matches_reference_golden(golden, scoring):
     ref = torch.from_numpy(g["y"])
     cos = F.cosine_similarity(y.flatten().float(), ref.flatten().float(), dim=0).item()
     assert y.shape == ref.shape and cos >= 0.99, cos
+
+
+def test_fni8_container_loads_to_the_gpu(tmp_path):
+    """A .fni8 checkpoint (fni8.format) loads straight into the layout the kernels read:
+    the linear on the loaded weight equals the linear on the original, bit for bit."""
+    import fni8
+    from fni8 import FQReader, save_fni8
+    from fni8.quant.core import quantize_int8_rowwise
+
+    N, K = 384, 512
+    q, sc = quantize_int8_rowwise(0.02 * torch.randn(N, K, generator=gen(40)))
+    qt = fni8.QTensor(q, sc.view(-1).float())
+    path = str(tmp_path / "m.fni8")
+    save_fni8(path, {"mlp.up.weight": qt}, meta={"arch": "qwen3"})
+    with FQReader(path) as r:
+        w = r.load_many(["mlp.up.weight"], "cuda")["mlp.up.weight"]
+    assert w.data.is_cuda and w.scheme == "per_row_i8"
+    x = torch.randn(8, K, generator=gen(41)).half().to(DEV)
+    assert torch.equal(fni8.linear(x, w), fni8.linear(x, qt.cuda()))

@@ -1,2 +1,2 @@
-"""Weight quantisation helpers (`fni8.quant.core`)."""
-from . import core  # noqa: F401
+"""Weight quantisation helpers (`fni8.quant.core`, `fni8.quant.lowbit`)."""
+from . import core, lowbit  # noqa: F401

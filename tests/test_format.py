@@ -153,3 +153,27 @@ def test_failed_write_leaves_no_file(tmp_path):
         w.add("a", _i8(8, 16))
         with pytest.raises(ValueError, match="duplicate"):
             w.add("a", _i8(8, 16))
+
+
+def test_quantize_lowbit_feeds_the_converters_int4_packing():
+    """fni8.quant.lowbit.quantize_lowbit as fni8serve/convert.py:69-79 calls it: codes and
+    per-group scales whose packed form dequantises (linear.py:33-45's code * scale) to the
+    oracle's int4 weights, and agrees with the oracle's quantiser exactly."""
+    from fni8.quant.lowbit import quantize_lowbit
+
+    from oracle import w8a8_oracle as O
+
+    g = torch.Generator().manual_seed(5)
+    w = 0.02 * torch.randn(64, 256, generator=g)
+    codes, scale = quantize_lowbit(w, 4, dim=-1, group_size=128)
+    assert codes.shape == (64, 256) and scale.shape == (64, 2)
+    assert int(codes.min()) >= -8 and int(codes.max()) <= 7
+    c = codes.to(torch.int64)
+    packed = ((c[:, 0::2] & 0xF) | ((c[:, 1::2] & 0xF) << 4)).to(torch.uint8)  # the converter's packing
+    ref_packed, ref_scale = O.quantize_weight_i4(w, 128)
+    assert torch.equal(packed, ref_packed) and torch.equal(scale.float(), ref_scale)
+    assert torch.equal(O.unpack_i4(packed), codes)
+    deq = O.dequant_weight_i4_fallback(packed, scale.float(), 128).float()
+    assert (deq - w).abs().max() <= scale.max() * 0.5 + 1e-3  # within half a step
+    with pytest.raises(ValueError):
+        quantize_lowbit(w, 4, group_size=100)

@@ -242,6 +242,25 @@ def _check_weight(qt: QTensor, x_dev: torch.device, K: int, what: str) -> None:
         raise TypeError(f"fni8.{what}: weight data/scale must be contiguous (scale fp32)")
 
 
+def _k16_weight(qt: QTensor, K: int) -> tuple[torch.Tensor, int]:
+    """(weight, K) with K a multiple of 16, the row-stride rule of the GEMMs' TMA maps.
+    fni8-serve accepts any K that is a multiple of 4 (convert.py:128); zero input channels
+    add nothing to the int32 sums (nor to a token's absmax), so a weight padded with zero
+    columns, and activations padded with zeros, give the same outputs bit for bit. The
+    padded weight is built on the first call and kept on the QTensor (call once before a
+    CUDA-graph capture, like the GEMM workspace); weights are not modified while serving."""
+    if K % 16 == 0:
+        return qt.data, K
+    Kp = (K + 15) // 16 * 16
+    cached = getattr(qt, "_fni8_k16", None)
+    if cached is not None and cached[0] is qt.data:
+        return cached[1], Kp
+    wp = torch.zeros((qt.data.shape[0], Kp), dtype=torch.int8, device=qt.data.device)
+    wp[:, :K] = qt.data
+    qt._fni8_k16 = (qt.data, wp)
+    return wp, Kp
+
+
 def linear_q(q: torch.Tensor, scale: torch.Tensor, qt: QTensor, bias: torch.Tensor | None = None,
              residual: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16,
              path: int = nat.PATH_AUTO) -> torch.Tensor:
@@ -249,7 +268,10 @@ def linear_q(q: torch.Tensor, scale: torch.Tensor, qt: QTensor, bias: torch.Tens
     _need_cuda(q, "linear_q")
     K = q.shape[-1]
     _check_weight(qt, q.device, K, "linear_q")
+    w, Kp = _k16_weight(qt, K)
     q2 = q.reshape(-1, K).contiguous()
+    if Kp != K:
+        q2 = torch.nn.functional.pad(q2, (0, Kp - K))
     s2 = scale.reshape(-1).to(torch.float32).contiguous()
     M, N = q2.shape[0], qt.data.shape[0]
     odt = _DT[out_dtype]
@@ -257,8 +279,8 @@ def linear_q(q: torch.Tensor, scale: torch.Tensor, qt: QTensor, bias: torch.Tens
     b = bias.to(out_dtype).contiguous() if bias is not None else None
     r = residual.reshape(M, N).to(out_dtype).contiguous() if residual is not None else None
     ws, wsb = _ws(q.device)
-    nat.call("fni8_gemm_w8a8_ex", _vp(q2), _vp(s2), _vp(qt.data), _vp(qt.scale), _vp(b), _vp(r), _vp(out), odt, M, N,
-             K, path, ws, wsb, _stream(q.device))
+    nat.call("fni8_gemm_w8a8_ex", _vp(q2), _vp(s2), _vp(w), _vp(qt.scale), _vp(b), _vp(r), _vp(out), odt, M, N,
+             Kp, path, ws, wsb, _stream(q.device))
     return out.reshape(*q.shape[:-1], N)
 
 
@@ -306,14 +328,17 @@ def linear(x: torch.Tensor, qt: QTensor, bias: torch.Tensor | None = None, path:
     sc = _sidecar(x) if path == nat.PATH_AUTO else None
     if sc is not None:
         return linear_q(sc[0], sc[1], qt, bias=bias, out_dtype=x.dtype).reshape(*x.shape[:-1], N)
+    w, Kp = _k16_weight(qt, K)
     x2 = x.reshape(-1, K).contiguous()
+    if Kp != K:
+        x2 = torch.nn.functional.pad(x2, (0, Kp - K))
     M = x2.shape[0]
     out = torch.empty((M, N), dtype=x.dtype, device=x.device)
-    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    q = torch.empty((M, Kp), dtype=torch.int8, device=x.device)
     s = torch.empty((M,), dtype=torch.float32, device=x.device)
     b = bias.to(x.dtype).contiguous() if bias is not None else None
     ws, wsb = _ws(x.device)
-    nat.call("fni8_linear_w8a8_ex", _vp(x2), dt, _vp(qt.data), _vp(qt.scale), _vp(b), _vp(out), M, N, K, _vp(q),
+    nat.call("fni8_linear_w8a8_ex", _vp(x2), dt, _vp(w), _vp(qt.scale), _vp(b), _vp(out), M, N, Kp, _vp(q),
              _vp(s), path, ws, wsb, _stream(x.device))
     return out.reshape(*x.shape[:-1], N)
 

@@ -23,7 +23,8 @@
  *    y = (float(acc) * a_scale[m]) * w_scale[n] (+ bias[n]) (+ residual[m, n]),
  *    rounded once to the output dtype.
  *  - K must be a multiple of 16 for the GEMMs (TMA row-stride rule); the quantisers
- *    accept any K.
+ *    accept any K. A caller with other K pads K with zeros in both operands (exact:
+ *    zero channels change neither the int32 sums nor a token's absmax).
  *  - Calls are asynchronous on `stream`, allocate nothing and never synchronise, so
  *    they can be captured into a CUDA graph. Calls that share a workspace must not
  *    overlap on the GPU.

@@ -283,6 +283,23 @@ def test_linear_bit_exact_vs_oracle(M, K, N):
     assert torch.equal(got.reshape(M, N), O.linear_w8a8(x, wq, ws, exact=False))
 
 
+@pytest.mark.parametrize("M,K,N", [(1, 100, 128), (37, 40, 200), (300, 1028, 256), (5, 4, 100)])
+def test_linear_any_k_multiple_of_4(M, K, N):
+    """fni8-serve takes any K that is a multiple of 4 (convert.py:128); the GEMMs need 16.
+    fni8.linear and linear_q pad K with zeros (weight once, activations per call): the
+    outputs equal the oracle on the unpadded shapes bit for bit."""
+    import fni8
+
+    x = act_input(M, K, 7 * M + K)
+    wq, ws = weight(N, K, N + 1)
+    qt = fni8.QTensor(wq.to(DEV), ws.to(DEV), scheme="per_row_i8")
+    ref = O.linear_w8a8(x, wq, ws, exact=False)
+    for _ in range(2):  # the second call reuses the padded weight
+        assert torch.equal(fni8.linear(x.to(DEV), qt).cpu(), ref)
+    q, s = fni8.quantize_rows(x.to(DEV))
+    assert torch.equal(fni8.linear_q(q, s, qt).cpu(), ref)
+
+
 def test_linear_matches_reference_golden(golden):
     """The reference's own acceptance bound for its int8 path (tests/test_smoke.py:67-80)
     against LinearW8A8's fp16 fallback output, plus bit-exactness against the oracle."""
@@ -323,9 +340,9 @@ def test_zero_rows_and_errors():
 
     qt = fni8.QTensor(torch.zeros(32, 64, dtype=torch.int8, device=DEV), torch.ones(32, device=DEV))
     assert fni8.linear(torch.zeros(0, 64, dtype=torch.float16, device=DEV), qt).shape == (0, 32)
-    with pytest.raises(Fni8Error, match="multiple of 16"):
-        bad = fni8.QTensor(torch.zeros(32, 40, dtype=torch.int8, device=DEV), torch.ones(32, device=DEV))
-        fni8.linear(torch.zeros(4, 40, dtype=torch.float16, device=DEV), bad)
+    with pytest.raises(Fni8Error, match="multiple of 16"):  # the raw GEMM keeps the TMA rule
+        fni8.gemm_i32(torch.zeros(4, 40, dtype=torch.int8, device=DEV),
+                      torch.zeros(32, 40, dtype=torch.int8, device=DEV))
     packed = torch.zeros(32, 64, dtype=torch.uint8, device=DEV)  # 4-bit weights for K = 128
     with pytest.raises(NotImplementedError):  # NF4 has no integer GEMM (fni8-serve uses its fp16 path)
         fni8.linear(torch.zeros(4, 128, dtype=torch.float16, device=DEV),

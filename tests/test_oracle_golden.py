@@ -134,3 +134,22 @@ def test_w4a8_oracle_against_reference_i4_path(golden):
     ref = torch.from_numpy(g["y_ref"]).float()
     cos = torch.nn.functional.cosine_similarity(y.float().flatten(), ref.flatten(), dim=0).item()
     assert cos >= 0.99, cos
+
+
+@pytest.mark.parametrize("K", [4, 40, 100, 1028])
+def test_zero_padding_k_is_exact(K):
+    """fni8.linear pads K (any multiple of 4, fni8serve/convert.py:128) with zeros up to the
+    GEMMs' multiple of 16. Zero channels leave each token's absmax, every int32 sum and so
+    the dequantised output unchanged; the padded weight is built once per QTensor."""
+    import fni8
+    from fni8.ops import _k16_weight
+
+    g = torch.Generator().manual_seed(K)
+    x = torch.randn(9, K, generator=g).to(torch.float16)
+    wq, ws = O.quantize_weight_rowwise(0.02 * torch.randn(24, K, generator=g))
+    qt = fni8.QTensor(wq, ws, scheme="per_row_i8")
+    wp, Kp = _k16_weight(qt, K)
+    assert Kp % 16 == 0 and Kp - K < 16 and torch.equal(wp[:, :K], wq) and not wp[:, K:].any()
+    assert _k16_weight(qt, K)[0] is wp
+    xp = F.pad(x, (0, Kp - K))
+    assert torch.equal(O.linear_w8a8(xp, wp, ws), O.linear_w8a8(x, wq, ws))

@@ -156,13 +156,25 @@ static int64_t splitk_auto_max_m() {
   return m;
 }
 
+// Above 64 tokens a weight matrix with at least this many 256-row tiles goes to the tile
+// kernel, whose 256-column tiles let each MMA consume twice the weight bytes of a split-K
+// MMA. Default: one tile per SM (an LM head, N = 151936, measured on B200);
+// FNI8_WIDE_MIN_TILES overrides it for measurements.
+static int64_t wide_min_tiles() {
+  static int64_t v = [] {
+    const char* e = getenv("FNI8_WIDE_MIN_TILES");
+    const long x = e ? atol(e) : 0;
+    return (int64_t)(x > 0 ? x : num_sms(current_device()));
+  }();
+  return v;
+}
+
+static bool wide_weights(int64_t M, int64_t N) { return M > 64 && (N + 255) / 256 >= wide_min_tiles(); }
+
 static int pick_path(int path, int64_t M, size_t ws_bytes, int64_t N, int64_t K) {
   if (path == FNI8_PATH_TILE || path == FNI8_PATH_STREAM || path == FNI8_PATH_SPLITK) return path;
   if (M <= stream_auto_max_m() && ws_bytes >= stream_workspace_bytes(M, N, K)) return FNI8_PATH_STREAM;
-  // Above 64 tokens a weight matrix with at least one 256-row tile per SM (an LM head:
-  // N = 151936) streams faster through the tile kernel, whose MMAs consume twice the
-  // weight bytes per instruction (measured on B200).
-  const bool wide = M > 64 && (N + 255) / 256 >= num_sms(current_device());
+  const bool wide = wide_weights(M, N);
   // Above 128 tokens split-K wins only where it splits K over clusters that are all
   // resident at once (measured at M = 256: QKV, O and down projections; the unsplit
   // gate_up, 192 weight tiles, streams faster through the tile kernel).
@@ -183,7 +195,15 @@ static int check_path(int path, int64_t M) {
   return FNI8_OK;
 }
 
+// Column width of a single-CTA tile: 256 where there are two 256-wide tiles per SM, else
+// 128 (FNI8_TILE_BN=128/256 forces one, for measurements).
 static int pick_bn(int64_t M, int64_t N) {
+  static const int forced = [] {
+    const char* e = getenv("FNI8_TILE_BN");
+    const int x = e ? atoi(e) : 0;
+    return (x == 128 || x == 256) ? x : 0;
+  }();
+  if (forced) return forced;
   const int64_t tiles256 = ((M + 127) / 128) * ((N + 255) / 256);
   return tiles256 >= 2 * num_sms(current_device()) ? 256 : 128;
 }

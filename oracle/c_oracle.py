@@ -41,6 +41,9 @@ def load():
         lib.fni8o_dequant.argtypes = [vp, vp, vp, vp, vp, i32, i64, i64, vp]
         lib.fni8o_linear_w8a8.argtypes = [vp, i32, i64, i64, vp, vp, i64, vp, vp, vp, vp, vp]
         lib.fni8o_linear_w8a8.restype = i32
+        lib.fni8o_unpack_i4.argtypes = [vp, i64, i64, vp]
+        lib.fni8o_dequant_weight_i4.argtypes = [vp, vp, i64, i64, i64, vp, vp]
+        lib.fni8o_linear_w4a8.argtypes = [vp, i32, i64, i64, vp, vp, i64, i64, vp, vp, vp, vp, vp]
         _lib = lib
     return _lib
 
@@ -124,4 +127,38 @@ def linear_w8a8(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, bias: torch
     acc, out = np.empty((M, N), np.int32), np.empty((M, N), np.int16)
     if load().fni8o_linear_w8a8(_p(b), dt, M, K, _p(wn), _p(wsn), N, _p(bn), _p(q), _p(s), _p(acc), _p(out)):
         raise OverflowError("int32 accumulator range exceeded")
+    return _from_bits(out, dt).reshape(*x.shape[:-1], N)
+
+
+def unpack_i4(packed: torch.Tensor) -> torch.Tensor:
+    p = np.ascontiguousarray(packed.numpy())
+    N, K = p.shape[0], 2 * p.shape[1]
+    codes = np.empty((N, K), np.int8)
+    load().fni8o_unpack_i4(_p(p), N, K, _p(codes))
+    return torch.from_numpy(codes)
+
+
+def dequant_weight_i4_fallback(packed: torch.Tensor, scale: torch.Tensor, group_size: int) -> torch.Tensor:
+    p = np.ascontiguousarray(packed.numpy())
+    sc = np.ascontiguousarray(scale.float().numpy())
+    N, K = p.shape[0], 2 * p.shape[1]
+    codes, out = np.empty((N, K), np.int8), np.empty((N, K), np.int16)
+    load().fni8o_dequant_weight_i4(_p(p), _p(sc), N, K, group_size, _p(codes), _p(out))
+    return _from_bits(out, F16)
+
+
+def linear_w4a8(x: torch.Tensor, packed: torch.Tensor, scale: torch.Tensor, group_size: int,
+                bias: torch.Tensor | None = None) -> torch.Tensor:
+    K = x.shape[-1]
+    b, dt = _half_bits(x.reshape(-1, K))
+    M = b.shape[0]
+    p = np.ascontiguousarray(packed.numpy())
+    sc = np.ascontiguousarray(scale.float().numpy())
+    N = p.shape[0]
+    if 2 * p.shape[1] != K or K % group_size:
+        raise ValueError("packed weight does not match K / group_size")
+    bn = _half_bits(bias.to(x.dtype))[0] if bias is not None else None
+    q, s = np.empty((M, K), np.int8), np.empty(M, np.float32)
+    codes, out = np.empty((N, K), np.int8), np.empty((M, N), np.int16)
+    load().fni8o_linear_w4a8(_p(b), dt, M, K, _p(p), _p(sc), N, group_size, _p(bn), _p(q), _p(s), _p(codes), _p(out))
     return _from_bits(out, dt).reshape(*x.shape[:-1], N)

@@ -14,7 +14,10 @@
  *    q = clamp(round_half_even(x * (127 / absmax)), -127, 127), a zero row gives s = 0, q = 0;
  *  - the int8 x int8 -> int32 contraction, accumulated in int64 and range-checked;
  *  - the dequant epilogue y = (float(acc) * a_scale[m]) * w_scale[n] (+ bias[n])
- *    (+ residual[m, n]) in fp32, rounded once to fp16 or bf16 (round to nearest even).
+ *    (+ residual[m, n]) in fp32, rounded once to fp16 or bf16 (round to nearest even);
+ *  - per_group_i4 / int4 weights: the nibble unpack and two's-complement decode, the fp16
+ *    fallback weight, and the W4A8 linear (exact int32 sum per scale group, groups added
+ *    in order in fp32, then the token scale and bias).
  *
  * Every floating-point step is one IEEE fp32 operation in the order written (the Makefile
  * builds with -ffp-contract=off, so nothing is fused); fp16/bf16 <-> fp32 conversions are
@@ -154,4 +157,49 @@ int fni8o_linear_w8a8(const uint16_t* x, int dtype, int64_t M, int64_t K, const 
   const int ovf = fni8o_gemm_i32(q_ws, wq, M, N, K, acc_ws);
   fni8o_dequant(acc_ws, s_ws, ws, bias, NULL, dtype, M, N, out);
   return ovf;
+}
+
+/* ---------------------------------------------------------------- W4A8 (per_group_i4, int4)
+ * Packed bytes [N, K/2]: element 2j in the low nibble of byte j, element 2j+1 in the high
+ * nibble, two's complement (fni8serve/convert.py:69-80, fni8serve/layers/linear.py:33-40). */
+void fni8o_unpack_i4(const uint8_t* packed, int64_t N, int64_t K, int8_t* codes) {
+  for (int64_t i = 0; i < N * (K / 2); ++i) {
+    const int lo = packed[i] & 0xf, hi = packed[i] >> 4;
+    codes[2 * i] = (int8_t)(lo >= 8 ? lo - 16 : lo);
+    codes[2 * i + 1] = (int8_t)(hi >= 8 ? hi - 16 : hi);
+  }
+}
+
+/* LinearW8A8's fp16 fallback weight: code * scale[n, k / group] in fp32, rounded once
+   (fni8serve/layers/linear.py:41-45) */
+void fni8o_dequant_weight_i4(const uint8_t* packed, const float* scale, int64_t N, int64_t K, int64_t group,
+                             int8_t* codes_ws, uint16_t* out) {
+  fni8o_unpack_i4(packed, N, K, codes_ws);
+  for (int64_t n = 0; n < N; ++n)
+    for (int64_t k = 0; k < K; ++k)
+      out[n * K + k] = f32_to_f16((float)codes_ws[n * K + k] * scale[n * (K / group) + k / group]);
+}
+
+/* fni8.linear for per_group_i4: per-token int8 rows; per group g an exact int32 sum acc_g;
+   y = sum over g in order of float(acc_g) * scale[n, g] (each product and each sum rounded
+   in fp32); out = y * a_scale[m] (+ bias[n]), rounded once to dtype */
+void fni8o_linear_w4a8(const uint16_t* x, int dtype, int64_t M, int64_t K, const uint8_t* packed, const float* scale,
+                       int64_t N, int64_t group, const uint16_t* bias, int8_t* q_ws, float* s_ws, int8_t* codes_ws,
+                       uint16_t* out) {
+  const int64_t G = K / group;
+  fni8o_quantize_rows(x, dtype, M, K, q_ws, s_ws);
+  fni8o_unpack_i4(packed, N, K, codes_ws);
+  for (int64_t m = 0; m < M; ++m)
+    for (int64_t n = 0; n < N; ++n) {
+      float y = 0.0f;
+      for (int64_t g = 0; g < G; ++g) {
+        int32_t acc = 0; /* |acc| <= 127 * 8 * group: far inside int32 */
+        for (int64_t k = g * group; k < (g + 1) * group; ++k) acc += (int32_t)q_ws[m * K + k] * codes_ws[n * K + k];
+        const float term = (float)acc * scale[n * G + g];
+        y = y + term;
+      }
+      y = y * s_ws[m];
+      if (bias) y = y + load(bias, n, dtype);
+      out[m * N + n] = store(y, dtype);
+    }
 }

@@ -106,3 +106,28 @@ def test_gemm_extremes_and_overflow():
     assert torch.equal(acc, O.int_mm_exact(a, w))
     with pytest.raises(OverflowError):
         C.gemm_i32(torch.full((1, 2 * K), 127, dtype=torch.int8), torch.full((1, 2 * K), 127, dtype=torch.int8))
+
+
+def test_w4a8_on_reference_fixture(golden):
+    """per_group_i4 / int4: the C unpack and fp16 fallback weight equal the reference's own
+    reconstruction (fni8serve/layers/linear.py:33-45, tests/golden/linear_i4.npz) bit for
+    bit, and the C and torch W4A8 linears agree bit for bit (same group order)."""
+    g = golden("linear_i4")
+    packed, scale, gs = t(g["packed"]), t(g["scale"]), int(g["group_size"])
+    assert torch.equal(C.unpack_i4(packed), O.unpack_i4(packed))
+    assert torch.equal(C.dequant_weight_i4_fallback(packed, scale, gs), t(g["w_ref"]))
+    x, bias = t(g["x"]), t(g["bias"])
+    for b in (None, bias):
+        assert torch.equal(C.linear_w4a8(x, packed, scale, gs, bias=b), O.linear_w4a8(x, packed, scale, gs, bias=b))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_w4a8_matches_torch_oracle(dtype):
+    N, K, gs = 48, 512, 128
+    x = activations(9, K, 17, dtype)
+    packed, scale = O.quantize_weight_i4(0.05 * torch.randn(N, K, generator=gen(18)), gs)
+    codes = torch.randint(-8, 8, (N, K), generator=gen(19), dtype=torch.int8)  # every code, both nibbles
+    for p in (packed, O.pack_i4(codes)):
+        assert torch.equal(C.unpack_i4(p), O.unpack_i4(p))
+        assert torch.equal(C.linear_w4a8(x, p, scale, gs), O.linear_w4a8(x, p, scale, gs))
+    assert torch.equal(C.unpack_i4(O.pack_i4(codes)), codes)

@@ -37,7 +37,7 @@ int current_device() {
 }
 
 int num_sms(int device) {
-  static int cache[kMaxDevices] = {};
+  static std::atomic<int> cache[kMaxDevices] = {};
   if (device < 0 || device >= kMaxDevices) return 148;
   if (cache[device] == 0) {
     int n = 0;

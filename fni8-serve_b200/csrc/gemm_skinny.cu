@@ -487,7 +487,7 @@ template <typename T, int NT>
 static int launch_skinny(const CUtensorMap& tw, const void* x, const float* w_scale, const void* bias, void* out,
                          int M, int N, int K, const SkinnyPlan& p, cudaStream_t st) {
   auto kern = skinny::skinny_linear_kernel<T, NT>;
-  static bool configured[kMaxDevices] = {};
+  static std::atomic<bool> configured[kMaxDevices] = {};
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) return fail(FNI8_ERR_CUDA, "no current CUDA device");
   if (!configured[dev]) {

@@ -26,6 +26,8 @@
 //    are published; its weight loads then queue behind this kernel's.
 // Shared memory stays under half an SM up to NT = 128, so two CTAs (or this kernel and
 // the next) share an SM. Every mbarrier wait is bounded (fni8_common.cuh).
+#include <mutex>
+
 #include "fni8_common.cuh"
 #include "gemm_internal.h"
 
@@ -469,7 +471,7 @@ struct SplitPlan {
 
 template <int NT>
 static cudaError_t configure_splitk(int dev) {
-  static bool configured[kMaxDevices] = {};
+  static std::atomic<bool> configured[kMaxDevices] = {};
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (configured[dev]) return cudaSuccess;
   auto kern = splitk::w8a8_splitk_kernel<NT>;
@@ -491,7 +493,7 @@ static __global__ void __launch_bounds__(1024, 1) occupancy_standin() {}
 // S). Registers are not modelled (the callers' kernels fit two CTAs per SM by registers).
 // -1 when the runtime cannot tell (no device).
 int max_active_clusters(int threads, int smem, int S) {
-  static bool configured[kMaxDevices] = {};
+  static std::atomic<bool> configured[kMaxDevices] = {};
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) return -1;
   if (!configured[dev]) {
@@ -526,6 +528,8 @@ static int max_clusters(int nt, int smem, int S) {
   struct Entry { int dev, smem, S, n; };
   static Entry cache[64];
   static int used = 0;
+  static std::mutex mu;  // GEMMs may be planned from several host threads
+  std::lock_guard<std::mutex> lock(mu);
   const int dev = current_device();
   for (int i = 0; i < used; ++i)
     if (cache[i].dev == dev && cache[i].smem == smem && cache[i].S == S) return cache[i].n;

@@ -405,7 +405,7 @@ static int launch_stream_cfg(const CUtensorMap& tw, const CUtensorMap& tx, const
                              int grid, int32_t* ws, cudaStream_t st) {
   using C = strm::Cfg<NT, BUDGET_KB>;
   auto kern = strm::w8a8_stream_kernel<NT, BUDGET_KB>;
-  static bool configured[kMaxDevices] = {};
+  static std::atomic<bool> configured[kMaxDevices] = {};
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) return fail(FNI8_ERR_CUDA, "no current CUDA device");
   if (!configured[dev]) {

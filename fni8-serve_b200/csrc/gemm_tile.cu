@@ -590,7 +590,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, 
            const Groups& grp, int M, int N, int K, int grid, bool vec_ok, cudaStream_t st) {
   using C = Cfg<BN, PAIR>;
   auto kern = w8a8_tile_kernel<BN, GROUPED, PAIR>;
-  static bool configured[fni8h::kMaxDevices] = {};  // the attribute is set per device
+  static std::atomic<bool> configured[fni8h::kMaxDevices] = {};  // the attribute is set per device
   const int dev = fni8h::current_device();
   if (dev < 0 || dev >= fni8h::kMaxDevices) return fni8h::fail(FNI8_ERR_CUDA, "no current CUDA device");
   if (!configured[dev]) {

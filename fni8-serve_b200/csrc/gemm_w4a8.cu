@@ -445,7 +445,7 @@ template <int NT>
 static int launch_w4(const CUtensorMap& tp, const CUtensorMap& tx, const w4::Epi& epi, int M, int N, int K,
                      const W4Plan& p, uint4* ws, cudaStream_t st) {
   auto kern = w4::w4a8_splitk_kernel<NT>;
-  static bool configured[kMaxDevices] = {};
+  static std::atomic<bool> configured[kMaxDevices] = {};
   const int dev = current_device();
   if (dev < 0 || dev >= kMaxDevices) return fail(FNI8_ERR_CUDA, "no current CUDA device");
   if (!configured[dev]) {

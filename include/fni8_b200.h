@@ -28,6 +28,9 @@
  *  - Calls are asynchronous on `stream`, allocate nothing and never synchronise, so
  *    they can be captured into a CUDA graph. Calls that share a workspace must not
  *    overlap on the GPU.
+ *  - Any host thread may call any entry point, concurrently with others: the one-time
+ *    setup (kernel attributes, cluster-occupancy plans, the tensor-map encoder) is
+ *    guarded, and the error message is per thread.
  */
 #ifndef FNI8_B200_H
 #define FNI8_B200_H

@@ -300,6 +300,52 @@ def test_linear_any_k_multiple_of_4(M, K, N):
     assert torch.equal(fni8.linear_q(q, s, qt).cpu(), ref)
 
 
+def test_first_calls_from_several_host_threads():
+    """Four host threads make their first fni8.linear calls at the same moment in a fresh
+    process (one-time kernel attribute setup, split-K cluster plans, the tensor-map encoder
+    and the workspace are all first touched concurrently), all on the default stream; every
+    result equals the oracle."""
+    import subprocess
+    import sys
+
+    root = os.path.dirname(PKG)
+    code = f"""
+import sys, threading, torch
+sys.path.insert(0, {PKG!r}); sys.path.insert(0, {root!r})
+import fni8
+from oracle import w8a8_oracle as O
+shapes = [(1, 4096, 6144), (24, 1024, 4096), (100, 2048, 3072), (300, 1024, 2048)]
+g = torch.Generator().manual_seed(5)
+cases = []
+for M, K, N in shapes:
+    x = torch.randn(M, K, generator=g).half()
+    wq, ws = O.quantize_weight_rowwise(0.02 * torch.randn(N, K, generator=g))
+    cases.append((x, wq, ws, O.linear_w8a8(x, wq, ws, exact=False)))
+dev = [(x.cuda(), fni8.QTensor(wq.cuda(), ws.cuda())) for x, wq, ws, _ in cases]
+torch.cuda.synchronize()
+start = threading.Barrier(len(cases))
+out, err = [None] * len(cases), []
+def run(i):
+    try:
+        start.wait()
+        out[i] = [fni8.linear(dev[i][0], dev[i][1]) for _ in range(3)]
+    except BaseException as e:
+        err.append(repr(e))
+ts = [threading.Thread(target=run, args=(i,)) for i in range(len(cases))]
+[t.start() for t in ts]
+[t.join() for t in ts]
+torch.cuda.synchronize()
+assert not err, err
+for i, (_, _, _, ref) in enumerate(cases):
+    for y in out[i]:
+        assert torch.equal(y.cpu(), ref), i
+assert fni8.device_status() == 0
+print("ok")
+"""
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
+
+
 def test_linear_matches_reference_golden(golden):
     """The reference's own acceptance bound for its int8 path (tests/test_smoke.py:67-80)
     against LinearW8A8's fp16 fallback output, plus bit-exactness against the oracle."""

@@ -18,6 +18,8 @@ Every output below is computed by fni8-serve's own modules on CPU:
     layers/linear.py LinearW8A8 (fp16 fallback) -> linear.npz
     layers/linear.py LinearW8A8 with per_group_i4 / int4 weights (its weight
         reconstruction and fp16 fallback)      -> linear_i4.npz
+    layers/linear.py LinearW8A8 with per_group_i4 / NF4 weights (table lookup and
+        fp16 fallback)                         -> linear_nf4.npz
     models/weights.py to_qtensor/merge_qtensor -> weights.npz
     models/moe.py SparseMoE (softmax and sigmoid+group-limited routing) -> moe_*.npz
     tests/test_layers.py::_i8 and tests/test_smoke.py::_i8 (the reference tests' own
@@ -153,6 +155,25 @@ def gen_linear_i4(L) -> dict:
             "in_features": np.int64(lin.in_features), "w_ref": _np(L.linear._dequant_weight(qt)), "y_ref": _np(lin(x))}
 
 
+def gen_linear_nf4(L) -> dict:
+    """LinearW8A8 on CPU with NF4 weights (per_group_i4, codebook "nf4"): the reference's
+    table lookup by 4-bit code, low nibble first (linear.py:33-39), times the group scale,
+    and its fp16 fallback forward. The table is this package's fni8.quant.lowbit
+    NF4_CODEBOOK (the reference imports it from `fni8`, linear.py:22-25); it is stored too,
+    so a change to the table shows up as a fixture mismatch."""
+    g = torch.Generator().manual_seed(505)
+    M, K, N, gs = 8, 256, 96, 64
+    codes = torch.randint(0, 16, (N, K), generator=g)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).to(torch.uint8)
+    scale = 0.01 + 0.05 * torch.rand(N, K // gs, generator=g)
+    qt = L.fni8.QTensor(packed, scale, scheme="per_group_i4", group_size=gs, codebook="nf4")
+    x = torch.randn(M, K, generator=g).to(torch.float16)
+    lin = L.linear.LinearW8A8(qt, None)
+    cb = torch.tensor(L.linear.NF4_CODEBOOK, dtype=torch.float32)
+    return {"x": _np(x), "packed": _np(packed), "scale": _np(scale), "group_size": np.int64(gs), "codebook": _np(cb),
+            "in_features": np.int64(lin.in_features), "w_ref": _np(L.linear._dequant_weight(qt)), "y_ref": _np(lin(x))}
+
+
 def gen_weights(L) -> dict:
     g = torch.Generator().manual_seed(404)
     sd = {f"p.{n}_proj.weight": (0.05 * torch.randn(*s, generator=g)).to(torch.float16)
@@ -229,6 +250,7 @@ def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--reference", default=os.environ.get("FNI8_REFERENCE"),
                     help="fni8-serve checkout (default: $FNI8_REFERENCE)")
+    ap.add_argument("--only", nargs="*", help="fixture names to (re)write (default: all)")
     a = ap.parse_args()
     if a.reference is None:
         print("pass --reference <fni8-serve checkout> or set FNI8_REFERENCE", file=sys.stderr)
@@ -239,10 +261,16 @@ def main() -> int:
     torch.set_num_threads(4)
     L = _setup(a.reference)
     jobs = {"rmsnorm": lambda: gen_rmsnorm(L), "act": lambda: gen_act(L), "linear": lambda: gen_linear(L),
-            "linear_i4": lambda: gen_linear_i4(L),
+            "linear_i4": lambda: gen_linear_i4(L), "linear_nf4": lambda: gen_linear_nf4(L),
             "weights": lambda: gen_weights(L), "i8_fixture": lambda: gen_i8_fixture(a.reference, L),
             "moe_softmax": lambda: gen_moe(L, "softmax"), "moe_sigmoid": lambda: gen_moe(L, "sigmoid")}
+    unknown = set(a.only or ()) - set(jobs)
+    if unknown:
+        print(f"unknown fixtures {sorted(unknown)}; known: {sorted(jobs)}", file=sys.stderr)
+        return 2
     for name, fn in jobs.items():
+        if a.only and name not in a.only:
+            continue
         path = os.path.join(HERE, f"{name}.npz")
         np.savez_compressed(path, **fn())
         print(f"wrote {path} ({os.path.getsize(path)} bytes)")

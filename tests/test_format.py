@@ -177,3 +177,28 @@ def test_quantize_lowbit_feeds_the_converters_int4_packing():
     assert (deq - w).abs().max() <= scale.max() * 0.5 + 1e-3  # within half a step
     with pytest.raises(ValueError):
         quantize_lowbit(w, 4, group_size=100)
+
+
+def test_nf4_codebook_is_normal_float():
+    """fni8.quant.lowbit.NF4_CODEBOOK, the table fni8-serve indexes by code for NF4 weights
+    (fni8serve/layers/linear.py:22-25,37-39) and NF4 LoRA adapters (training/qlora.py:31,54):
+    16 ascending levels in [-1, 1] with an exact zero, 8 above and 7 below it, each the
+    quantile of N(0, 1) at evenly spaced probabilities (checked with scipy's normal CDF,
+    an implementation independent of the one the module uses)."""
+    from scipy.stats import norm
+
+    from fni8.quant.lowbit import NF4_CODEBOOK as cb
+
+    assert len(cb) == 16 and cb == sorted(cb) and cb[0] == -1.0 and cb[-1] == 1.0 and cb[7] == 0.0
+    offset = 0.5 * ((1 - 1 / 30) + (1 - 1 / 32))
+    top = norm.ppf(offset)
+    pos = [norm.cdf(v * top) for v in cb[8:]]      # 8 probabilities above 1/2
+    neg = [norm.cdf(-v * top) for v in cb[:7]]     # 7 mirrored probabilities above 1/2
+    for probs, count in ((pos, 8), (neg, 7)):
+        step = (offset - 0.5) / count
+        expect = sorted(0.5 + step * (i + 1) for i in range(count))
+        assert max(abs(a - b) for a, b in zip(sorted(probs), expect)) < 1e-12
+    # the reference's lookup: a float32 table indexed by 4-bit codes
+    t = torch.tensor(cb, dtype=torch.float32)
+    codes = torch.arange(16)
+    assert torch.equal(t[codes], t) and t.abs().max() == 1.0

@@ -153,3 +153,20 @@ def test_zero_padding_k_is_exact(K):
     assert _k16_weight(qt, K)[0] is wp
     xp = F.pad(x, (0, Kp - K))
     assert torch.equal(O.linear_w8a8(xp, wp, ws), O.linear_w8a8(x, wq, ws))
+
+
+def test_nf4_fallback_weight_matches_reference(golden):
+    """per_group_i4 / NF4: the reference's table lookup (low nibble first) and group scaling
+    (fni8serve/layers/linear.py:33-45), computed by its own LinearW8A8 with this package's
+    NF4_CODEBOOK, equal the oracle's restatement bit for bit; the fp16 fallback forward is
+    F.linear on that weight; the stored table is the one the package exports today."""
+    from fni8.quant.lowbit import NF4_CODEBOOK
+
+    g = golden("linear_nf4")
+    cb = t(g["codebook"])
+    assert torch.equal(cb, torch.tensor(NF4_CODEBOOK, dtype=torch.float32))
+    packed, scale, gs = t(g["packed"]), t(g["scale"]), int(g["group_size"])
+    assert int(g["in_features"]) == 2 * packed.shape[1]
+    w16 = O.dequant_weight_nf4_fallback(packed, scale, gs, cb)
+    assert torch.equal(w16, t(g["w_ref"]))
+    assert torch.equal(F.linear(t(g["x"]), w16), t(g["y_ref"]))

@@ -21,6 +21,8 @@ Every output below is computed by fni8-serve's own modules on CPU:
     layers/linear.py LinearW8A8 with per_group_i4 / NF4 weights (table lookup and
         fp16 fallback)                         -> linear_nf4.npz
     models/weights.py to_qtensor/merge_qtensor -> weights.npz
+    convert.py convert_hf_to_fni8 + loader.py on a tiny Qwen3 checkpoint, through
+        this package's .fni8 format             -> convert.npz
     models/moe.py SparseMoE (softmax and sigmoid+group-limited routing) -> moe_*.npz
     tests/test_layers.py::_i8 and tests/test_smoke.py::_i8 (the reference tests' own
         weight-quant fixtures)                  -> i8_fixture.npz
@@ -174,6 +176,56 @@ def gen_linear_nf4(L) -> dict:
             "in_features": np.int64(lin.in_features), "w_ref": _np(L.linear._dequant_weight(qt)), "y_ref": _np(lin(x))}
 
 
+def gen_convert(L) -> dict:
+    """fni8-serve's own converter and loader on a tiny synthetic Qwen3 checkpoint, run over
+    this package's `.fni8` format: convert_hf_to_fni8 (convert.py:254-362: safetensors in,
+    its quantisation rules and 4-bit packing, FQWriter out) at 8 and 4 bits, then
+    load_fni8_state_dict / checkpoint_info (loader.py:19-69). Stores the source weights,
+    each container's bytes, and what the reference's loader reported."""
+    import json
+    import tempfile
+
+    from safetensors.torch import save_file
+
+    conv = importlib.import_module("fni8serve.convert")
+    loader = importlib.import_module("fni8serve.loader")
+    H, I, V, nh, nkv, hd, gs = 64, 128, 128, 4, 2, 16, 32
+    cfg = {"architectures": ["Qwen3ForCausalLM"], "model_type": "qwen3", "hidden_size": H, "intermediate_size": I,
+           "num_hidden_layers": 1, "num_attention_heads": nh, "num_key_value_heads": nkv, "head_dim": hd,
+           "vocab_size": V, "rms_norm_eps": 1e-6, "rope_theta": 10000.0, "max_position_embeddings": 512,
+           "tie_word_embeddings": False, "torch_dtype": "bfloat16"}
+    g = torch.Generator().manual_seed(606)
+    sd = {"model.embed_tokens.weight": torch.randn(V, H, generator=g), "model.norm.weight": torch.ones(H),
+          "lm_head.weight": 0.02 * torch.randn(V, H, generator=g)}
+    p = "model.layers.0."
+    for n, shape in (("self_attn.q_proj", (nh * hd, H)), ("self_attn.k_proj", (nkv * hd, H)),
+                     ("self_attn.v_proj", (nkv * hd, H)), ("self_attn.o_proj", (H, nh * hd)),
+                     ("mlp.gate_proj", (I, H)), ("mlp.up_proj", (I, H)), ("mlp.down_proj", (H, I))):
+        sd[p + n + ".weight"] = 0.02 * torch.randn(*shape, generator=g)
+    for n, size in (("self_attn.q_norm", hd), ("self_attn.k_norm", hd), ("input_layernorm", H),
+                    ("post_attention_layernorm", H)):
+        sd[p + n + ".weight"] = 1 + 0.1 * torch.randn(size, generator=g)
+    sd = {k: v.to(torch.bfloat16).contiguous() for k, v in sd.items()}
+    out = {"names": np.array(sorted(sd)), "group_size": np.int64(gs)}
+    for k in sorted(sd):
+        out["src/" + k] = _np(sd[k].view(torch.int16))  # bf16 bits
+    with tempfile.TemporaryDirectory() as d:
+        with open(os.path.join(d, "config.json"), "w") as f:
+            json.dump(cfg, f)
+        save_file(sd, os.path.join(d, "model.safetensors"))
+        for bits in (8, 4):
+            path = os.path.join(d, f"m{bits}.fni8")
+            conv.convert_hf_to_fni8(d, path, weight_bits=bits, group_size=gs)
+            info = loader.checkpoint_info(path)
+            st = loader.load_fni8_state_dict(path, device="cpu")
+            with open(path, "rb") as f:
+                out[f"file{bits}"] = np.frombuffer(f.read(), dtype=np.uint8)
+            out[f"info{bits}"] = np.array(json.dumps(info, sort_keys=True))
+            out[f"schemes{bits}"] = np.array(json.dumps({k: getattr(v, "scheme", "tensor") for k, v in st.items()},
+                                                        sort_keys=True))
+    return out
+
+
 def gen_weights(L) -> dict:
     g = torch.Generator().manual_seed(404)
     sd = {f"p.{n}_proj.weight": (0.05 * torch.randn(*s, generator=g)).to(torch.float16)
@@ -262,7 +314,7 @@ def main() -> int:
     L = _setup(a.reference)
     jobs = {"rmsnorm": lambda: gen_rmsnorm(L), "act": lambda: gen_act(L), "linear": lambda: gen_linear(L),
             "linear_i4": lambda: gen_linear_i4(L), "linear_nf4": lambda: gen_linear_nf4(L),
-            "weights": lambda: gen_weights(L), "i8_fixture": lambda: gen_i8_fixture(a.reference, L),
+            "convert": lambda: gen_convert(L), "weights": lambda: gen_weights(L), "i8_fixture": lambda: gen_i8_fixture(a.reference, L),
             "moe_softmax": lambda: gen_moe(L, "softmax"), "moe_sigmoid": lambda: gen_moe(L, "sigmoid")}
     unknown = set(a.only or ()) - set(jobs)
     if unknown:

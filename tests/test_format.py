@@ -202,3 +202,44 @@ def test_nf4_codebook_is_normal_float():
     t = torch.tensor(cb, dtype=torch.float32)
     codes = torch.arange(16)
     assert torch.equal(t[codes], t) and t.abs().max() == 1.0
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_reference_converter_output_reads_back(golden, tmp_path, bits):
+    """Containers written by fni8-serve's own converter (convert_hf_to_fni8 over this
+    package's FQWriter, tests/golden/convert.npz) read back here exactly as the reference's
+    loader saw them (same names, schemes, header and meta), and hold what the oracle
+    computes from the source weights: per-row int8 codes and scales, int4 codes packed two
+    per byte low nibble first (the converter's packing, convert.py:69-80), fp16 raw tensors."""
+    import json
+
+    import numpy as np
+
+    from fni8 import FQReader
+    from oracle import w8a8_oracle as O
+
+    g = golden("convert")
+    path = tmp_path / f"m{bits}.fni8"
+    path.write_bytes(g[f"file{bits}"].tobytes())
+    info = json.loads(str(g[f"info{bits}"]))
+    schemes = json.loads(str(g[f"schemes{bits}"]))
+    gs = int(g["group_size"])
+    src = {n: torch.from_numpy(np.ascontiguousarray(g["src/" + n])).view(torch.bfloat16) for n in g["names"]}
+    with FQReader(str(path)) as r:
+        assert sorted(r.names) == sorted(src) == sorted(schemes) and len(r.names) == info["num_tensors"]
+        assert (r.header["arch"], r.header["quant"], r.header["version"]) == (info["arch"], info["quant"],
+                                                                                 info["version"])
+        assert r.header.get("__meta__") == info["meta"] and r.shards == {}
+        got = r.load_many(r.names, "cpu")
+    for name, qt in got.items():
+        assert (qt.scheme if qt.scheme != "raw" else "tensor") == schemes[name], name
+        w = src[name].float()
+        if qt.scheme == "per_row_i8":
+            q, s = O.quantize_weight_rowwise(w)
+            assert torch.equal(qt.data, q) and torch.equal(qt.scale, s), name
+        elif qt.scheme == "per_group_i4":
+            packed, s = O.quantize_weight_i4(w, gs)
+            assert qt.codebook == "int4" and qt.group_size == gs
+            assert torch.equal(qt.data, packed) and torch.equal(qt.scale, s), name
+        else:
+            assert torch.equal(qt.data, src[name].to(torch.float16)), name

@@ -24,6 +24,7 @@ Every output below is computed by fni8-serve's own modules on CPU:
     convert.py convert_hf_to_fni8 + loader.py on a tiny Qwen3 checkpoint, through
         this package's .fni8 format             -> convert.npz
     models/moe.py SparseMoE (softmax and sigmoid+group-limited routing) -> moe_*.npz
+    models/moe.py SparseMoE with a gated shared expert and routed scaling -> moe_shared.npz
     tests/test_layers.py::_i8 and tests/test_smoke.py::_i8 (the reference tests' own
         weight-quant fixtures)                  -> i8_fixture.npz
 Inputs are seeded; every fixture stores its inputs too, so the tests need nothing else.
@@ -39,6 +40,7 @@ import types
 
 import numpy as np
 import torch
+import torch.nn.functional as F
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
@@ -174,6 +176,36 @@ def gen_linear_nf4(L) -> dict:
     cb = torch.tensor(L.linear.NF4_CODEBOOK, dtype=torch.float32)
     return {"x": _np(x), "packed": _np(packed), "scale": _np(scale), "group_size": np.int64(gs), "codebook": _np(cb),
             "in_features": np.int64(lin.in_features), "w_ref": _np(L.linear._dequant_weight(qt)), "y_ref": _np(lin(x))}
+
+
+def gen_moe_shared(L) -> dict:
+    """SparseMoE with a gated shared expert and a routed scaling factor (moe.py:95,107-112),
+    softmax routing, on CPU: the block's output, and its shared expert's (gated) output."""
+    g = torch.Generator().manual_seed(608)
+    E, k, H, I, Is = 8, 2, 128, 64, 96
+    B, S = 2, 12
+    sd = {}
+    for e in list(range(E)) + ["s"]:
+        n = Is if e == "s" else I
+        sd[f"e{e}.gate_proj.weight"] = (0.05 * torch.randn(n, H, generator=g)).to(torch.float16)
+        sd[f"e{e}.up_proj.weight"] = (0.05 * torch.randn(n, H, generator=g)).to(torch.float16)
+        sd[f"e{e}.down_proj.weight"] = (0.05 * torch.randn(H, n, generator=g)).to(torch.float16)
+    experts = [(L.weights.gate_up_weight(sd, f"e{e}"), L.weights.to_qtensor(sd[f"e{e}.down_proj.weight"]))
+               for e in range(E)]
+    shared = (L.weights.gate_up_weight(sd, "es"), L.weights.to_qtensor(sd["es.down_proj.weight"]))
+    gate = (0.05 * torch.randn(E, H, generator=g)).to(torch.float16)
+    sgate = (0.05 * torch.randn(1, H, generator=g)).to(torch.float16)
+    moe = L.moe.SparseMoE(gate=gate, experts=experts, top_k=k, norm_topk_prob=True, shared_expert=shared,
+                          shared_expert_gate=sgate, routed_scaling_factor=2.5)
+    x = torch.randn(B, S, H, generator=g).to(torch.float16)
+    y = moe(x)
+    xf = x.reshape(-1, H)
+    ys = moe.shared(x).reshape(-1, H) * torch.sigmoid(F.linear(xf.float(), sgate.float())).to(x.dtype)
+    return {"x": _np(x), "gate": _np(gate), "sgate": _np(sgate), "y": _np(y), "y_shared": _np(ys),
+            "w_gu": np.stack([_np(gu.data) for gu, _ in experts]), "s_gu": np.stack([_np(gu.scale) for gu, _ in experts]),
+            "w_dn": np.stack([_np(dn.data) for _, dn in experts]), "s_dn": np.stack([_np(dn.scale) for _, dn in experts]),
+            "sh_gu_q": _np(shared[0].data), "sh_gu_s": _np(shared[0].scale), "sh_dn_q": _np(shared[1].data),
+            "sh_dn_s": _np(shared[1].scale), "E": np.array(E), "k": np.array(k), "scaling": np.float32(2.5)}
 
 
 def gen_convert(L) -> dict:
@@ -315,7 +347,8 @@ def main() -> int:
     jobs = {"rmsnorm": lambda: gen_rmsnorm(L), "act": lambda: gen_act(L), "linear": lambda: gen_linear(L),
             "linear_i4": lambda: gen_linear_i4(L), "linear_nf4": lambda: gen_linear_nf4(L),
             "convert": lambda: gen_convert(L), "weights": lambda: gen_weights(L), "i8_fixture": lambda: gen_i8_fixture(a.reference, L),
-            "moe_softmax": lambda: gen_moe(L, "softmax"), "moe_sigmoid": lambda: gen_moe(L, "sigmoid")}
+            "moe_softmax": lambda: gen_moe(L, "softmax"), "moe_sigmoid": lambda: gen_moe(L, "sigmoid"),
+            "moe_shared": lambda: gen_moe_shared(L)}
     unknown = set(a.only or ()) - set(jobs)
     if unknown:
         print(f"unknown fixtures {sorted(unknown)}; known: {sorted(jobs)}", file=sys.stderr)

@@ -170,3 +170,22 @@ def test_nf4_fallback_weight_matches_reference(golden):
     w16 = O.dequant_weight_nf4_fallback(packed, scale, gs, cb)
     assert torch.equal(w16, t(g["w_ref"]))
     assert torch.equal(F.linear(t(g["x"]), w16), t(g["y_ref"]))
+
+
+def test_moe_shared_expert_and_scaling_vs_reference(golden):
+    """SparseMoE with a gated shared expert and routed_scaling_factor (moe.py:95,107-112),
+    computed by the reference on CPU: the oracle's shared expert and the whole block (its
+    routing with the scaling factor, routed experts, shared expert) stay within the
+    reference tests' bound (cos >= 0.99 against the reference's fp16 fallback)."""
+    g = golden("moe_shared")
+    x, gate, sgate = t(g["x"]), t(g["gate"]), t(g["sgate"])
+    B, S, H = x.shape
+    k = int(g["k"])
+    xf = x.reshape(-1, H)
+    topi, topw = O.moe_route(F.linear(xf.float(), gate.float()), k, scaling=float(g["scaling"]))
+    ys = O.moe_shared_expert(xf, t(g["sh_gu_q"]), t(g["sh_gu_s"]), t(g["sh_dn_q"]), t(g["sh_dn_s"]), sgate)
+    y = O.moe_experts_w8a8(xf, topi, topw.float(), t(g["w_gu"]), t(g["s_gu"]), t(g["w_dn"]), t(g["s_dn"])) + ys
+    for got, ref in ((ys, t(g["y_shared"])), (y, t(g["y"]).reshape(-1, H))):
+        cos = F.cosine_similarity(got.flatten().float(), ref.flatten().float(), dim=0).item()
+        assert cos >= 0.99, cos
+    assert y.dtype == x.dtype

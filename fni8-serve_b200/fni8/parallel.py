@@ -136,15 +136,23 @@ class PeerExchange:
         dist.all_gather_object(handles, handle.raw, group=group)
         self._opened = []
         bases = []
-        for r, h in enumerate(handles):
-            if r == self.rank:
-                bases.append(self._own)
-                continue
-            p = ctypes.c_void_p()
-            hb = ctypes.create_string_buffer(h, 64)
-            nat.call("fni8_ipc_open", ctypes.cast(hb, ctypes.c_void_p), ctypes.byref(p))
-            self._opened.append(p.value)
-            bases.append(p.value)
+        try:
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bases.append(self._own)
+                    continue
+                p = ctypes.c_void_p()
+                hb = ctypes.create_string_buffer(h, 64)
+                nat.call("fni8_ipc_open", ctypes.cast(hb, ctypes.c_void_p), ctypes.byref(p))
+                self._opened.append(p.value)
+                bases.append(p.value)
+        except BaseException:
+            # unmap what this rank mapped and free its own buffer before reporting the error
+            for p in self._opened:
+                nat.lib().fni8_ipc_close(ctypes.c_void_p(p))
+            nat.lib().fni8_ipc_free(ctypes.c_void_p(self._own))
+            self._opened, self._own = [], None
+            raise
         arr = ctypes.c_void_p * self.world
         self._arrays = {name: arr(*[b + self.off[name] for b in bases]) for name, _ in parts}
         self.peer = {name: ctypes.cast(a, ctypes.c_void_p) for name, a in self._arrays.items()}

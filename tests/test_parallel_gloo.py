@@ -136,12 +136,59 @@ def _cp_worker(rank, world, port, errq):
         raise
 
 
-@pytest.mark.parametrize("worker", [_ep_worker, _cp_worker], ids=["expert_parallel", "column_parallel"])
-def test_two_gloo_ranks(worker):
+def _ipc_fail_worker(rank, world, port, errq):
+    """PeerExchange set-up where mapping a peer's buffer fails: the rank unmaps the peer it
+    already mapped, frees its own buffer and raises (native calls faked on the host)."""
+    try:
+        import ctypes
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from fni8 import _native as nat
+        from fni8.parallel import PeerExchange
+
+        own, log, opens = 0x10000 * (rank + 1), [], [0]
+
+        def fake_call(name, *args):
+            if name == "fni8_ipc_alloc":
+                args[1]._obj.value = own
+                ctypes.memmove(args[2].value, b"handle-of-%d" % rank, 11)
+            elif name == "fni8_ipc_open":
+                opens[0] += 1
+                if opens[0] == 2:
+                    raise nat.Fni8Error(nat.ERR_CUDA, "fni8_ipc_open: peer mapping refused")
+                args[1]._obj.value = 0x900000 + opens[0]
+            else:
+                raise AssertionError(f"unexpected native call {name}")
+
+        class FakeLib:
+            def fni8_ipc_close(self, p):
+                log.append(("close", p.value))
+                return 0
+
+            def fni8_ipc_free(self, p):
+                log.append(("free", p.value))
+                return 0
+
+        nat.call, nat.lib = fake_call, (lambda: FakeLib())
+        try:
+            PeerExchange(4, 2, 16, torch.float16, torch.device("cpu"))
+            raise AssertionError("PeerExchange did not raise")
+        except nat.Fni8Error:
+            pass
+        assert log == [("close", 0x900001), ("free", own)], log
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        errq.put(f"rank {rank}: {e!r}")
+        raise
+
+
+def _spawn(worker, world):
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
     port = _free_port()
-    procs = [ctx.Process(target=worker, args=(r, 2, port, errq)) for r in range(2)]
+    procs = [ctx.Process(target=worker, args=(r, world, port, errq)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -154,6 +201,15 @@ def test_two_gloo_ranks(worker):
             p.kill()
             errs.append("rank timed out")
     assert not errs and all(p.exitcode == 0 for p in procs), errs
+
+
+def test_peer_exchange_cleans_up_a_failed_mapping():
+    _spawn(_ipc_fail_worker, 3)
+
+
+@pytest.mark.parametrize("worker", [_ep_worker, _cp_worker], ids=["expert_parallel", "column_parallel"])
+def test_two_gloo_ranks(worker):
+    _spawn(worker, 2)
 
 
 def test_exchange_helpers_single_rank():

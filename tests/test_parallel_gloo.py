@@ -1,10 +1,12 @@
-"""Multi-process logic of the multi-GPU forms, on CPU gloo ranks (world_size 2).
+"""Multi-process logic of the multi-GPU forms, on CPU gloo ranks (world_size 2, and 3 for
+the peer-exchange failure path).
 
 The expert-parallel layer (fni8/parallel.py) owns the exchange: per-expert counts,
 split sizes, int8 row dispatch, (source rank, local expert) segments and the combine
 return trip. Here its compute steps are the CPU oracle's, so two gloo ranks must
 reproduce the single-process oracle MoE bit for bit; the column-parallel linear must
-reassemble the unsharded output exactly. No GPU is involved.
+reassemble the unsharded output exactly; a peer-memory exchange whose set-up fails must
+release what it mapped and allocated. No GPU is involved.
 """
 import os
 import socket

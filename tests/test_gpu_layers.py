@@ -247,6 +247,28 @@ def test_sparse_moe_dropin_matches_reference_golden(golden, scoring):
     assert y.shape == ref.shape and cos >= 0.99, cos
 
 
+def test_sparse_moe_shared_expert_matches_reference_golden(golden):
+    """The drop-in SparseMoE with a gated shared expert and routed_scaling_factor
+    (fni8serve/models/moe.py:95,107-112) against the reference block's output, and the
+    oracle's routed + shared restatement (tests/golden/moe_shared.npz)."""
+    import fni8
+    import fni8.moe as M
+
+    g = golden("moe_shared")
+    E, k = int(g["E"]), int(g["k"])
+    T = lambda a: torch.from_numpy(a)  # noqa: E731
+    experts = [(fni8.QTensor(T(g["w_gu"][e]), T(g["s_gu"][e])), fni8.QTensor(T(g["w_dn"][e]), T(g["s_dn"][e])))
+               for e in range(E)]
+    shared = (fni8.QTensor(T(g["sh_gu_q"]), T(g["sh_gu_s"])), fni8.QTensor(T(g["sh_dn_q"]), T(g["sh_dn_s"])))
+    moe = M.SparseMoE(gate=T(g["gate"]), experts=experts, top_k=k, shared_expert=shared,
+                      shared_expert_gate=T(g["sgate"]), routed_scaling_factor=float(g["scaling"])).to(DEV)
+    x = T(g["x"]).to(DEV)
+    y = moe(x).cpu()
+    ref = T(g["y"])
+    cos = F.cosine_similarity(y.flatten().float(), ref.flatten().float(), dim=0).item()
+    assert y.shape == ref.shape and cos >= 0.99, cos
+
+
 def test_fni8_container_loads_to_the_gpu(tmp_path):
     """A .fni8 checkpoint (fni8.format) loads straight into the layout the kernels read:
     the linear on the loaded weight equals the linear on the original, bit for bit."""

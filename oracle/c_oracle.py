@@ -44,6 +44,9 @@ def load():
         lib.fni8o_unpack_i4.argtypes = [vp, i64, i64, vp]
         lib.fni8o_dequant_weight_i4.argtypes = [vp, vp, i64, i64, i64, vp, vp]
         lib.fni8o_linear_w4a8.argtypes = [vp, i32, i64, i64, vp, vp, i64, i64, vp, vp, vp, vp, vp]
+        lib.fni8o_moe_plan.argtypes = [vp, i64, ctypes.c_int32, vp, vp, vp, vp, vp]
+        lib.fni8o_moe_plan.restype = i64
+        lib.fni8o_moe_combine.argtypes = [vp, i32, vp, vp, i64, i64, i64, vp]
         _lib = lib
     return _lib
 
@@ -162,3 +165,25 @@ def linear_w4a8(x: torch.Tensor, packed: torch.Tensor, scale: torch.Tensor, grou
     codes, out = np.empty((N, K), np.int8), np.empty((M, N), np.int16)
     load().fni8o_linear_w4a8(_p(b), dt, M, K, _p(p), _p(sc), N, group_size, _p(bn), _p(q), _p(s), _p(codes), _p(out))
     return _from_bits(out, dt).reshape(*x.shape[:-1], N)
+
+
+def moe_plan(topi: torch.Tensor, E: int):
+    """(counts [E], offsets [E+1], row_of_slot [T*k], slot_of_row [rows]) as int64 tensors."""
+    ti = np.ascontiguousarray(topi.reshape(-1).to(torch.int32).numpy())
+    n = ti.size
+    counts, offsets = np.empty(E, np.int32), np.empty(E + 1, np.int32)
+    ros, sor, cur = np.empty(n, np.int32), np.empty(max(n, 1), np.int32), np.empty(E, np.int32)
+    rows = load().fni8o_moe_plan(_p(ti), n, E, _p(counts), _p(offsets), _p(ros), _p(sor), _p(cur))
+    return (torch.from_numpy(counts).long(), torch.from_numpy(offsets).long(), torch.from_numpy(ros).long(),
+            torch.from_numpy(sor[:rows].copy()).long())
+
+
+def moe_combine(y: torch.Tensor, row_of_slot: torch.Tensor, topw: torch.Tensor) -> torch.Tensor:
+    b, dt = _half_bits(y)
+    T, k = topw.shape
+    H = b.shape[1]
+    ros = np.ascontiguousarray(row_of_slot.reshape(-1).to(torch.int32).numpy())
+    tw = np.ascontiguousarray(topw.float().numpy())
+    out = np.empty((T, H), np.int16)
+    load().fni8o_moe_combine(_p(b), dt, _p(ros), _p(tw), T, k, H, _p(out))
+    return _from_bits(out, dt)

@@ -17,7 +17,10 @@
  *    (+ residual[m, n]) in fp32, rounded once to fp16 or bf16 (round to nearest even);
  *  - per_group_i4 / int4 weights: the nibble unpack and two's-complement decode, the fp16
  *    fallback weight, and the W4A8 linear (exact int32 sum per scale group, groups added
- *    in order in fp32, then the token scale and bias).
+ *    in order in fp32, then the token scale and bias);
+ *  - the MoE block's index and combine steps (fni8serve/models/moe.py:97-105): stable
+ *    grouping of (token, slot) pairs by expert, and the weighted sum over a token's slots
+ *    in slot order in fp32, rounded once.
  *
  * Every floating-point step is one IEEE fp32 operation in the order written (the Makefile
  * builds with -ffp-contract=off, so nothing is fused); fp16/bf16 <-> fp32 conversions are
@@ -201,5 +204,49 @@ void fni8o_linear_w4a8(const uint16_t* x, int dtype, int64_t M, int64_t K, const
       y = y * s_ws[m];
       if (bias) y = y + load(bias, n, dtype);
       out[m * N + n] = store(y, dtype);
+    }
+}
+
+/* ---------------------------------------------------------------- MoE (fni8serve/models/moe.py:97-105)
+ * Stable grouping of the T*k (token, slot) pairs by expert: counts[E], offsets[E+1]
+ * (exclusive prefix sums), slot_of_row[rows] (the slots of expert 0 in slot order, then
+ * expert 1's, ...) and row_of_slot[T*k] (its inverse; -1 for an expert id outside [0, E),
+ * which is not grouped). Returns the number of grouped rows. */
+int64_t fni8o_moe_plan(const int32_t* topi, int64_t n, int32_t E, int32_t* counts, int32_t* offsets,
+                       int32_t* row_of_slot, int32_t* slot_of_row, int32_t* cursor_ws) {
+  for (int32_t e = 0; e < E; ++e) counts[e] = 0;
+  for (int64_t i = 0; i < n; ++i)
+    if (topi[i] >= 0 && topi[i] < E) counts[topi[i]] += 1;
+  offsets[0] = 0;
+  for (int32_t e = 0; e < E; ++e) offsets[e + 1] = offsets[e] + counts[e];
+  for (int32_t e = 0; e < E; ++e) cursor_ws[e] = offsets[e];
+  for (int64_t i = 0; i < n; ++i) {
+    const int32_t e = topi[i];
+    if (e < 0 || e >= E) {
+      row_of_slot[i] = -1;
+      continue;
+    }
+    const int32_t row = cursor_ws[e]++;
+    row_of_slot[i] = row;
+    slot_of_row[row] = (int32_t)i;
+  }
+  return offsets[E];
+}
+
+/* out[t] = sum over j = 0..k-1 in order of topw[t, j] * y[row_of_slot[t*k + j]] in fp32
+ * (each product and each sum rounded), skipping slots with no row, rounded once to dtype.
+ * y: [rows, H] fp16/bf16; topw fp32 [T, k]. */
+void fni8o_moe_combine(const uint16_t* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,
+                       int64_t k, int64_t H, uint16_t* out) {
+  for (int64_t t = 0; t < T; ++t)
+    for (int64_t h = 0; h < H; ++h) {
+      float acc = 0.0f;
+      for (int64_t j = 0; j < k; ++j) {
+        const int32_t r = row_of_slot[t * k + j];
+        if (r < 0) continue;
+        const float term = topw[t * k + j] * load(y, (int64_t)r * H + h, dtype);
+        acc = acc + term;
+      }
+      out[t * H + h] = store(acc, dtype);
     }
 }

@@ -21,8 +21,8 @@ Every output below is computed by fni8-serve's own modules on CPU:
     layers/linear.py LinearW8A8 with per_group_i4 / NF4 weights (table lookup and
         fp16 fallback)                         -> linear_nf4.npz
     models/weights.py to_qtensor/merge_qtensor -> weights.npz
-    convert.py convert_hf_to_fni8 + loader.py on a tiny Qwen3 checkpoint, through
-        this package's .fni8 format             -> convert.npz
+    convert.py convert_hf_to_fni8 + loader.py on a tiny Qwen3 checkpoint, and
+        loader.py save_training_checkpoint, through this package's .fni8 format -> convert.npz
     models/moe.py SparseMoE (softmax and sigmoid+group-limited routing) -> moe_*.npz
     models/moe.py SparseMoE with a gated shared expert and routed scaling -> moe_shared.npz
     tests/test_layers.py::_i8 and tests/test_smoke.py::_i8 (the reference tests' own
@@ -255,6 +255,23 @@ def gen_convert(L) -> dict:
             out[f"info{bits}"] = np.array(json.dumps(info, sort_keys=True))
             out[f"schemes{bits}"] = np.array(json.dumps({k: getattr(v, "scheme", "tensor") for k, v in st.items()},
                                                         sort_keys=True))
+        # the training checkpoint writer (loader.py:75-103): raw fp32 weights, AdamW state
+        # and meta through save_fni8
+        tr = types.ModuleType("fni8serve.training")
+        tr.__path__ = [os.path.join(os.path.dirname(conv.__file__), "training")]
+        sys.modules.setdefault("fni8serve.training", tr)
+        torch.manual_seed(607)
+        net = torch.nn.Sequential(torch.nn.Linear(16, 32), torch.nn.Linear(32, 8))
+        opt = torch.optim.AdamW(net.parameters(), lr=1e-3)
+        net(torch.randn(4, 16)).sum().backward()
+        opt.step()
+        path = os.path.join(d, "train.fni8")
+        loader.save_training_checkpoint(path, net.state_dict(), opt, meta={"step": 7})
+        with open(path, "rb") as f:
+            out["train_file"] = np.frombuffer(f.read(), dtype=np.uint8)
+        out["train_info"] = np.array(json.dumps(loader.checkpoint_info(path), sort_keys=True))
+        for k, v in net.state_dict().items():
+            out["train_sd/" + k] = _np(v)
     return out
 
 

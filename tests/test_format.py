@@ -243,3 +243,29 @@ def test_reference_converter_output_reads_back(golden, tmp_path, bits):
             assert torch.equal(qt.data, packed) and torch.equal(qt.scale, s), name
         else:
             assert torch.equal(qt.data, src[name].to(torch.float16)), name
+
+
+def test_reference_training_checkpoint_reads_back(golden, tmp_path):
+    """fni8-serve's training checkpoint writer (save_training_checkpoint, loader.py:75-103:
+    raw fp32 weights, optimizer buffers under optimizer.state.*, training meta) over this
+    format: the container it wrote reads back with every weight exact and its meta intact."""
+    import json
+
+    import numpy as np
+
+    from fni8 import FQReader
+
+    g = golden("convert")
+    path = tmp_path / "train.fni8"
+    path.write_bytes(g["train_file"].tobytes())
+    info = json.loads(str(g["train_info"]))
+    sd = {k[len("train_sd/"):]: torch.from_numpy(np.ascontiguousarray(g[k])) for k in g
+          if k.startswith("train_sd/")}
+    with FQReader(str(path)) as r:
+        meta = r.header.get("__meta__")
+        assert meta == info["meta"] and meta["training"] is True and meta["step"] == 7
+        assert len(r.names) == info["num_tensors"] and set(sd) <= set(r.names)
+        assert any(n.startswith("optimizer.state.") for n in r.names)
+        got = r.load_many(r.names, "cpu")
+    for name, ref in sd.items():
+        assert got[name].scheme == "raw" and torch.equal(got[name].data, ref), name

@@ -212,8 +212,9 @@ def gen_convert(L) -> dict:
     """fni8-serve's own converter and loader on a tiny synthetic Qwen3 checkpoint, run over
     this package's `.fni8` format: convert_hf_to_fni8 (convert.py:254-362: safetensors in,
     its quantisation rules and 4-bit packing, FQWriter out) at 8 and 4 bits, then
-    load_fni8_state_dict / checkpoint_info (loader.py:19-69). Stores the source weights,
-    each container's bytes, and what the reference's loader reported."""
+    load_fni8_state_dict / checkpoint_info (loader.py:19-69), and a training checkpoint
+    from save_training_checkpoint (loader.py:75-103). Stores the source weights, each
+    container's bytes, and what the reference's loader reported."""
     import json
     import tempfile
 

@@ -248,16 +248,17 @@ def _k16_weight(qt: QTensor, K: int) -> tuple[torch.Tensor, int]:
     add nothing to the int32 sums (nor to a token's absmax), so a weight padded with zero
     columns, and activations padded with zeros, give the same outputs bit for bit. The
     padded weight is built on the first call and kept on the QTensor (call once before a
-    CUDA-graph capture, like the GEMM workspace); weights are not modified while serving."""
+    CUDA-graph capture, like the GEMM workspace); it is rebuilt if the weight tensor is
+    replaced or modified in place."""
     if K % 16 == 0:
         return qt.data, K
     Kp = (K + 15) // 16 * 16
     cached = getattr(qt, "_fni8_k16", None)
-    if cached is not None and cached[0] is qt.data:
-        return cached[1], Kp
+    if cached is not None and cached[0] is qt.data and cached[1] == qt.data._version:
+        return cached[2], Kp
     wp = torch.zeros((qt.data.shape[0], Kp), dtype=torch.int8, device=qt.data.device)
     wp[:, :K] = qt.data
-    qt._fni8_k16 = (qt.data, wp)
+    qt._fni8_k16 = (qt.data, qt.data._version, wp)
     return wp, Kp
 
 

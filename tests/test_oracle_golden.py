@@ -153,6 +153,11 @@ def test_zero_padding_k_is_exact(K):
     assert _k16_weight(qt, K)[0] is wp
     xp = F.pad(x, (0, Kp - K))
     assert torch.equal(O.linear_w8a8(xp, wp, ws), O.linear_w8a8(x, wq, ws))
+    qt.data[0, 0] = -qt.data[0, 0] - 1  # an in-place weight update rebuilds the padded copy
+    wp2, _ = _k16_weight(qt, K)
+    assert wp2 is not wp and torch.equal(wp2[:, :K], qt.data)
+    qt.data = qt.data.clone()  # so does a replaced weight tensor
+    assert _k16_weight(qt, K)[0] is not wp2
 
 
 def test_nf4_fallback_weight_matches_reference(golden):

@@ -256,7 +256,11 @@ extern "C" int fni8_device_status(int* code_out) {
   *code_out = 0;
   for (int v : codes)
     if (*code_out == 0) *code_out = v;
-  return *code_out == 0 ? FNI8_OK : fail(FNI8_ERR_DEVICE_TIMEOUT, "device watchdog code 0x%x", *code_out);
+  if (*code_out == 0) return FNI8_OK;
+  // a kernel that left its loop on a timed-out wait may have left partial sums in the
+  // shared scratch of the allocation-free GEMM: zero it before the next call uses it
+  if (int s = noalloc_scratch_reset()) return s;
+  return fail(FNI8_ERR_DEVICE_TIMEOUT, "device watchdog code 0x%x", *code_out);
 }
 
 extern "C" size_t fni8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K) {

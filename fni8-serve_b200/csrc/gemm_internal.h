@@ -31,6 +31,8 @@ int stream_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const fl
                 size_t ws_bytes, cudaStream_t st);
 int stream_status_read_and_clear(int* code);
 constexpr int64_t kStreamMaxM = 256;
+// Re-zero the allocation-free GEMM's built-in scratch on the current device (synchronous).
+int noalloc_scratch_reset();
 
 // Fused quantise + GEMM for decode (gemm_skinny.cu): fp16/bf16 x[M, K] in, out[M, N].
 constexpr int64_t kSkinnyMaxM = 32;

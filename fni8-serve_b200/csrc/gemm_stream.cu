@@ -483,7 +483,8 @@ int stream_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const fl
 // whole HBM for its KV cache and weights, or a host program reaching this library through
 // a thin FFI with no device allocator of its own — get that scratch from a fixed array
 // compiled into the library instead. Every GPU that loads the library holds the array
-// until the process exits.
+// until the process exits. CUDA loads modules lazily by default, so the array is only
+// materialised on a device when this file's module is first used there.
 // ------------------------------------------------------------------------------------
 #include <mutex>
 
@@ -492,28 +493,70 @@ namespace strm {
 constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB per device
 constexpr int64_t kNoAllocMaxM = 32;                        // rows of activations per call
 static __device__ __align__(256) int32_t g_noalloc_scratch[kNoAllocScratchBytes / sizeof(int32_t)];
+
+// Failure-detection self-test (fni8_watchdog_selftest): one warp, whose lane 0 waits on a
+// flag that nothing in the library ever sets. The wait is bounded like every other wait in
+// the library (globaltimer, at most kWaitBudgetNs), so the kernel always ends; when it
+// gives up it records kCodeSelftest in this file's status word. With `dirty` set the warp
+// first leaves non-zero partial sums and counts in the allocation-free scratch, the state a
+// stream-K reduction abandoned by a timed-out wait would leave behind.
+enum : int { kCodeSelftest = 0x2F0 };
+static __device__ int g_selftest_flag;
+
+__global__ void __launch_bounds__(32) watchdog_selftest_kernel(uint64_t budget_ns, int dirty) {
+  if (dirty) {
+    constexpr int n = static_cast<int>(kNoAllocScratchBytes / sizeof(int32_t));
+    for (int i = threadIdx.x; i < n; i += 32) g_noalloc_scratch[i] = 0x5A5A0000 | (i & 0xFFFF);
+    __threadfence();
+  }
+  if (threadIdx.x != 0) return;
+  if (budget_ns > kWaitBudgetNs) budget_ns = kWaitBudgetNs;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (*reinterpret_cast<volatile int*>(&g_selftest_flag) != 0) return;
+    if ((i & 63u) == 0u && globaltimer_ns() - t0 > budget_ns) {
+      atomicCAS(&g_status, 0, kCodeSelftest);
+      return;
+    }
+  }
+}
 }  // namespace strm
 }  // namespace fni8b
 
 namespace fni8h {
 
 static std::mutex g_noalloc_mu;
-static void* g_noalloc_addr[kMaxDevices];
+static std::atomic<void*> g_noalloc_addr[kMaxDevices];
 
 // Device address of the scratch array on the current device. The first call on a device
 // looks the address up (in host code the array's name is only a stand-in for it) and
-// zeroes the array on `st`; later calls reuse both.
+// zeroes the array on `st`; later calls read the cached address without taking the lock.
 static int noalloc_scratch(int dev, cudaStream_t st, void** out) {
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, strm::g_noalloc_scratch);
-    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(no-alloc scratch)");
-    e = cudaMemsetAsync(p, 0, strm::kNoAllocScratchBytes, st);
-    if (e != cudaSuccess) return cuda_status(e, "clear no-alloc scratch");
-    g_noalloc_addr[dev] = p;
+  void* p = g_noalloc_addr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    p = g_noalloc_addr[dev].load(std::memory_order_relaxed);
+    if (p == nullptr) {
+      cudaError_t e = cudaGetSymbolAddress(&p, strm::g_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(no-alloc scratch)");
+      e = cudaMemsetAsync(p, 0, strm::kNoAllocScratchBytes, st);
+      if (e != cudaSuccess) return cuda_status(e, "clear no-alloc scratch");
+      g_noalloc_addr[dev].store(p, std::memory_order_release);
+    }
   }
-  *out = g_noalloc_addr[dev];
+  *out = p;
+  return FNI8_OK;
+}
+
+// Zero the allocation-free scratch of the current device again (synchronous). Called by
+// fni8_device_status when a bounded wait has given up: a stream-K kernel that left its
+// loop may have added partial sums or counts that no finishing CTA cleared.
+int noalloc_scratch_reset() {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, strm::g_noalloc_scratch);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(no-alloc scratch)");
+  e = cudaMemset(p, 0, strm::kNoAllocScratchBytes);
+  if (e != cudaSuccess) return cuda_status(e, "re-zero no-alloc scratch");
   return FNI8_OK;
 }
 
@@ -546,4 +589,15 @@ extern "C" int fni8_gemm_w8a8_noalloc(const int8_t* a, const float* a_scale, con
   if (int s = noalloc_scratch(dev, st, &scratch)) return s;
   return stream_gemm(a, a_scale, w, w_scale, bias, residual, out, out_dtype == FNI8_F16 ? 0 : 1, M, N, K, scratch,
                      strm::kNoAllocScratchBytes, st);
+}
+
+extern "C" int fni8_watchdog_selftest(int64_t wait_us, int dirty_scratch, void* stream) {
+  using namespace fni8h;
+  if (wait_us < 1 || wait_us > 1000000)
+    return fail(FNI8_ERR_INVALID, "wait_us=%lld: expected 1 .. 1000000", (long long)wait_us);
+  strm::watchdog_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint64_t>(wait_us) * 1000ull, dirty_scratch != 0 ? 1 : 0);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e, "launch watchdog self-test");
+  return FNI8_OK;
 }

@@ -31,6 +31,7 @@ SIGNATURES: dict[str, tuple] = {
     "fni8_status_string": (ctypes.c_char_p, [_i]),
     "fni8_last_error_message": (ctypes.c_char_p, []),
     "fni8_device_status": (_i, [ctypes.POINTER(_i)]),
+    "fni8_watchdog_selftest": (_i, [_i64, _i, _p]),
     "fni8_quantize_rows_i8": (_i, [_p, _i, _i64, _i64, _p, _p, _p]),
     "fni8_rmsnorm": (_i, [_p, _p, _p, _i, _i64, _i64, _f, _i, _p, _p, _p]),
     "fni8_rmsnorm_quant_i8": (_i, [_p, _p, _p, _i, _i64, _i64, _f, _i, _p, _p, _p, _p, _p]),

@@ -359,9 +359,27 @@ def gemm_i32(a: torch.Tensor, w: torch.Tensor, path: int = nat.PATH_AUTO) -> tor
 
 
 def device_status() -> int:
-    """Synchronise and return (and clear) the device watchdog code; 0 means healthy."""
+    """Synchronise and return (and clear) the device watchdog code of the current device;
+    0 means healthy. A non-zero code means a kernel left its loop on a timed-out wait and
+    its outputs are void; the abandoned kernel may have left partial sums in the GEMM
+    workspace, so this device's WORKSPACE is zeroed again before the next GEMM reads it
+    (the library re-zeroes its own allocation-free scratch)."""
     code = ctypes.c_int(0)
     st = nat.lib().fni8_device_status(ctypes.byref(code))
     if st not in (nat.OK, nat.ERR_DEVICE_TIMEOUT):
         nat.check(st, "fni8_device_status")
+    if code.value != 0:
+        buf = WORKSPACE._bufs.get(torch.cuda.current_device())
+        if buf is not None:
+            buf.zero_()
+            torch.cuda.synchronize()
     return code.value
+
+
+def watchdog_selftest(wait_us: int = 20000, dirty_scratch: bool = False) -> None:
+    """Launch the failure-detection self-test on the current stream: a kernel whose bounded
+    wait on a flag that nothing sets gives up after `wait_us` and records a watchdog code
+    (read it with device_status()); with dirty_scratch it first leaves non-zero partial
+    sums in the allocation-free GEMM's scratch, as an abandoned reduction would."""
+    nat.call("fni8_watchdog_selftest", int(wait_us), int(bool(dirty_scratch)),
+             _stream(torch.device("cuda", torch.cuda.current_device())))

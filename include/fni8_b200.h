@@ -77,8 +77,23 @@ FNI8_API int fni8_abi_version(void);
 FNI8_API const char* fni8_status_string(int status);
 FNI8_API const char* fni8_last_error_message(void);
 /* Reads and clears the device-side watchdog words of the current device. *code_out
- * receives 0 when no bounded wait has timed out since the last call. Synchronises. */
+ * receives 0 when no bounded wait has timed out since the last call. Synchronises.
+ * A non-zero code (returned with FNI8_ERR_DEVICE_TIMEOUT) means a kernel left its loop
+ * early and its results are void; the call then re-zeroes the built-in scratch of
+ * fni8_gemm_w8a8_noalloc on the current device. A caller-provided GEMM workspace may
+ * hold partial sums of the abandoned kernel: zero it again (fni8_workspace_init)
+ * before its next use. */
 FNI8_API int fni8_device_status(int* code_out);
+/* Test hook for the failure-detection path (no counterpart in the reference, whose
+ * kernels have no bounded waits): launches one warp on `stream` that waits on a device
+ * flag nothing ever sets. The wait gives up after wait_us microseconds (1 .. 1000000),
+ * records watchdog code 0x2F0 for fni8_device_status and the kernel ends; with
+ * dirty_scratch == 0 no GPU state beyond the status word changes. Otherwise the warp first fills the
+ * built-in scratch of fni8_gemm_w8a8_noalloc with non-zero words, as a stream-K
+ * reduction abandoned by a timed-out wait would leave it, so a test can check that
+ * fni8_device_status restores it. Any in-flight call of fni8_gemm_w8a8_noalloc on the
+ * device races with it. */
+FNI8_API int fni8_watchdog_selftest(int64_t wait_us, int dirty_scratch, void* stream);
 
 /* ------------------------------------------------------------------ quantisers */
 /* Per-token absmax int8 quantisation of x[M, K]: the activation stage inside
@@ -147,9 +162,13 @@ FNI8_API int fni8_gemm_w8a8_ex(const int8_t* a, const float* a_scale, const int8
  * process exits. Takes M <= 32 rows (larger M, or an N/K split that would need more than
  * 4 MiB, returns FNI8_ERR_UNSUPPORTED) and calls no allocator. The first call on a device
  * looks up the array's address and zeroes it on `stream`; make that first call before
- * any stream capture. All calls on a device share the array: calls that overlap on the
- * GPU (other streams, other threads) race and must be serialised by the caller. The
- * kernels leave the array zeroed after every completed call. */
+ * any stream capture. CUDA loads a library's modules lazily by default, so the array's
+ * 4 MiB are taken on a device at that first call (or the first use of any stream-K
+ * kernel there): make it before the engine reserves all of HBM, or run with
+ * CUDA_MODULE_LOADING=EAGER. All calls on a device share the array: calls that overlap on
+ * the GPU (other streams, other threads) race and must be serialised by the caller. The
+ * kernels leave the array zeroed after every completed call; after a watchdog timeout
+ * fni8_device_status zeroes it again. */
 FNI8_API int fni8_gemm_w8a8_noalloc(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
                                     const void* bias, const void* residual, void* out, int out_dtype, int64_t M,
                                     int64_t N, int64_t K, void* stream);

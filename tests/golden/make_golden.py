@@ -25,6 +25,8 @@ Every output below is computed by fni8-serve's own modules on CPU:
         loader.py save_training_checkpoint, through this package's .fni8 format -> convert.npz
     models/moe.py SparseMoE (softmax and sigmoid+group-limited routing) -> moe_*.npz
     models/moe.py SparseMoE with a gated shared expert and routed scaling -> moe_shared.npz
+    models/moe.py SparseMoE's combine: every expert's contribution and the output the
+        expert loop accumulates with index_add_ (moe.py:97-105) -> moe_combine.npz
     tests/test_layers.py::_i8 and tests/test_smoke.py::_i8 (the reference tests' own
         weight-quant fixtures)                  -> i8_fixture.npz
 Inputs are seeded; every fixture stores its inputs too, so the tests need nothing else.
@@ -348,6 +350,55 @@ def gen_moe(L, scoring: str) -> dict:
     return out
 
 
+def gen_moe_combine(L) -> dict:
+    """The reference's expert loop with each expert's output recorded (a forward hook on
+    every GatedMLP): y_slot[t, j] is the contribution of the expert in slot j of token t,
+    y the block output the loop accumulated in fp16 with index_add_ in expert order
+    (fni8serve/models/moe.py:97-105). Four slots per token, so each output element is a
+    sum of four rounded products."""
+    g = torch.Generator().manual_seed(608)
+    E, k, H, I = 8, 4, 64, 32
+    B, S = 4, 32
+    sd = {}
+    for e in range(E):
+        sd[f"e{e}.gate_proj.weight"] = (0.2 * torch.randn(I, H, generator=g)).to(torch.float16)
+        sd[f"e{e}.up_proj.weight"] = (0.2 * torch.randn(I, H, generator=g)).to(torch.float16)
+        sd[f"e{e}.down_proj.weight"] = (0.2 * torch.randn(H, I, generator=g)).to(torch.float16)
+    experts = [(L.weights.gate_up_weight(sd, f"e{e}"), L.weights.to_qtensor(sd[f"e{e}.down_proj.weight"]))
+               for e in range(E)]
+    gate = (0.3 * torch.randn(E, H, generator=g)).to(torch.float16)
+    moe = L.moe.SparseMoE(gate=gate, experts=experts, top_k=k, norm_topk_prob=True)
+    x = torch.randn(B, S, H, generator=g).to(torch.float16)
+    T = B * S
+    captured = {}
+    real_topk = torch.topk
+
+    def spy(inp, kk, *a, **kws):
+        r = real_topk(inp, kk, *a, **kws)
+        if kk == k and inp.shape[-1] == E:
+            captured["topi"] = r[1].clone()
+        return r
+
+    outs = {}
+    hooks = [m.register_forward_hook(lambda mod, inp, out, e=e: outs.__setitem__(e, out.detach().clone()))
+             for e, m in enumerate(moe.experts)]
+    torch.topk = spy
+    try:
+        y = moe(x)
+    finally:
+        torch.topk = real_topk
+        for h in hooks:
+            h.remove()
+    topi = captured["topi"]
+    y_slot = torch.zeros(T, k, H, dtype=torch.float16)
+    for e, o in outs.items():
+        tok, slot = (topi == e).nonzero(as_tuple=True)  # the loop's own row order
+        y_slot[tok, slot] = o.reshape(-1, H)
+    logits = F.linear(x.reshape(-1, H).float(), gate.float())
+    return {"x": _np(x), "gate": _np(gate), "logits": _np(logits), "topi": _np(topi), "y_slot": _np(y_slot),
+            "y": _np(y), "E": np.array(E), "k": np.array(k)}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--reference", default=os.environ.get("FNI8_REFERENCE"),
@@ -366,7 +417,7 @@ def main() -> int:
             "linear_i4": lambda: gen_linear_i4(L), "linear_nf4": lambda: gen_linear_nf4(L),
             "convert": lambda: gen_convert(L), "weights": lambda: gen_weights(L), "i8_fixture": lambda: gen_i8_fixture(a.reference, L),
             "moe_softmax": lambda: gen_moe(L, "softmax"), "moe_sigmoid": lambda: gen_moe(L, "sigmoid"),
-            "moe_shared": lambda: gen_moe_shared(L)}
+            "moe_shared": lambda: gen_moe_shared(L), "moe_combine": lambda: gen_moe_combine(L)}
     unknown = set(a.only or ()) - set(jobs)
     if unknown:
         print(f"unknown fixtures {sorted(unknown)}; known: {sorted(jobs)}", file=sys.stderr)

@@ -108,6 +108,9 @@ def test_argument_validation_without_launch(lib):
     assert lib.fni8_ipc_alloc(0, ctypes.byref(ctypes.c_void_p()), p) == n.ERR_INVALID
     assert lib.fni8_ipc_open(None, ctypes.byref(ctypes.c_void_p())) == n.ERR_INVALID
     assert lib.fni8_act_and_mul_quant_i8_rows(p, n.F16, 0, 4, 32, None, p, p, None) == n.ERR_INVALID
+    # watchdog self-test: the wait budget must lie in 1 us .. 1 s
+    assert lib.fni8_watchdog_selftest(0, 0, None) == n.ERR_INVALID
+    assert lib.fni8_watchdog_selftest(2_000_000, 1, None) == n.ERR_INVALID
     # zero-size work is a successful no-op (no launch)
     assert lib.fni8_ep_dispatch_i8(None, None, None, None, 16, 2, 0, 4, 512, None, pp, pp, pp, 0, 0, None) == n.OK
     assert lib.fni8_ep_return(None, n.F16, None, 0, None, 512, 2, pp, 0, None) == n.OK

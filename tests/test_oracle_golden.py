@@ -194,3 +194,26 @@ def test_moe_shared_expert_and_scaling_vs_reference(golden):
         cos = F.cosine_similarity(got.flatten().float(), ref.flatten().float(), dim=0).item()
         assert cos >= 0.99, cos
     assert y.dtype == x.dtype
+
+
+def test_moe_combine_restatement_vs_reference(golden):
+    """The reference's expert-loop combine (fni8serve/models/moe.py:97-105: fp16
+    `contrib * topw` added with index_add_ in expert order), run by the reference on CPU
+    with every expert's contribution recorded: the oracle's restatement reproduces the
+    block output bit for bit from those contributions, and this library's fp32 combine
+    (one rounding) stays inside moe_combine_bound of it on every element."""
+    g = golden("moe_combine")
+    k = int(g["k"])
+    topi, topw = O.moe_route(t(g["logits"]), k)
+    assert torch.equal(topi, t(g["topi"]))  # the routing the reference chose
+    y_slot = t(g["y_slot"])
+    ref = t(g["y"]).reshape(-1, y_slot.shape[-1])
+    assert torch.equal(O.moe_combine_reference(y_slot, topi, topw), ref)
+    ours = O.moe_combine_fp32(y_slot, topw)
+    assert bool(((ours.float() - ref.float()).abs() <= O.moe_combine_bound(y_slot, topw)).all())
+    # a planted change in the restatement (fp32 product, no rounding to fp16) is caught
+    planted = torch.zeros_like(ref)
+    for e in range(int(g["E"])):
+        tok, slot = (topi == e).nonzero(as_tuple=True)
+        planted[tok] = (planted[tok].float() + y_slot[tok, slot].float() * topw[tok, slot].float()[:, None]).half()
+    assert not torch.equal(planted, ref)

@@ -1,18 +1,26 @@
 """Benchmark of the B200 W8A8 path on BASELINE.json's configurations.
 
-    python bench.py [--config 1] [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--config C] [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Prints ONE JSON line (rank 0). The default workload is BASELINE config 1, the Qwen3-8B
-decode-step linear set: for each decode batch M in {1, 8, 32, 128, 256} the four
-fni8.linear calls QKV (4096->6144), O (4096->4096), gate_up (4096->24576) and
-down (12288->4096), each = per-token int8 quantisation + int8 GEMM + dequant epilogue.
-A step is that whole set (20 linears). Metric: algorithmic HBM bytes per second
-(weights + scales + activations in + outputs out). Every linear has its own weights
-(965 MB per step), so every weight read comes from HBM, not the 126 MB L2.
+Prints ONE JSON line (rank 0). BASELINE.json's metric has three parts — prefill TOPS,
+decode GB/s, and MoE tokens/s on 1-8 GPUs — and the default run (no --config) reports
+all three in one line:
 
-Other configs (parity-test workloads, also benchable): 0 single linear, 2 prefill
-(fused RMSNorm+quant -> 4 GEMMs at M=8192, TOPS), 3 MoE expert layer (tokens/s,
-expert-parallel under torchrun), 4 column-parallel K=8192 N=28672 sweep.
+  * top level: BASELINE config 3, the Qwen3-30B-A3B-shaped MoE expert layer (E=128,
+    top-8, H=2048, I=768) at 4096 tokens per GPU, expert-parallel over the ranks under
+    torchrun (weak scaling: each rank routes its own 4096 tokens and owns E/N experts;
+    rows cross NVLink as peer-memory stores). Metric: whole-job tokens/s. This is the
+    part of the path that shards, so the 1->8 GPU runs measure it.
+  * at N=1 also the keyed sub-blocks "decode" (for each decode batch
+    M in {1, 8, 32, 128, 256} the four Qwen3-8B fni8.linear calls QKV 4096->6144,
+    O 4096->4096, gate_up 4096->24576, down 12288->4096; 20 linears, 965 MB of distinct
+    weights per step; HBM GB/s) and "prefill" (fused RMSNorm+quant ->
+    QKV, O, gate_up -> SiLU*up+quant -> down at M=8192; TOP/s), each with its own
+    roofline, cpu_baseline and e2e. The dense paths run replicas only, so they are not
+    repeated at N>1.
+
+--config 0..4 runs one configuration alone (0 single linear, 1 decode, 2 prefill,
+3 MoE, 4 column-parallel K=8192 N=28672 sweep).
 
 --impl reference times the reference's own CPU path for the same workload on the
 host cores: the oracle port (torch._int_mm + fp32 dequant, oracle/w8a8_oracle.py),
@@ -871,12 +879,13 @@ def cpu_workload(config):
     raise ValueError(config)
 
 
-def reference_arm(args, world, rank):
+def reference_arm(args, world, rank, config=None):
     """The reference's CPU int8 path on the host cores (oracle port), same config/metric."""
     if rank != 0:
         return None
+    config = args.config if config is None else config
     torch.set_num_threads(os.cpu_count() or 1)
-    step, work, scale, sample = cpu_workload(args.config)
+    step, work, scale, sample = cpu_workload(config)
     for _ in range(max(1, min(args.warmup, 2))):
         step()
     t0 = time.perf_counter()
@@ -884,17 +893,60 @@ def reference_arm(args, world, rank):
         step()
     dt = (time.perf_counter() - t0) / args.steps
     v = work / dt / scale
-    metric, unit = METRICS[args.config]
+    metric, unit = METRICS[config]
     return {"metric": metric, "value": round(v, 4), "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
-            "config": {"workload": f"BASELINE config {args.config}", "parallelism": "host cores"},
+            "config": {"workload": f"BASELINE config {config}", "parallelism": "host cores"},
             "cpu_baseline": {"value": round(v, 4), "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(v, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-def cpu_baseline_sample(config, seconds=10.0):
+SUB_BLOCKS = {"decode": 1, "prefill": 2}
+_RUN_KEYS = ("n_gpus", "steps", "warmup", "vs_baseline", "data", "impl")
+
+
+def _sub_block(line):
+    """A config's line as a keyed sub-block of the default line (run-wide keys dropped)."""
+    return {k: v for k, v in line.items() if k not in _RUN_KEYS}
+
+
+def headline(args, world, rank, dev):
+    """The default line: the MoE layer (config 3, expert-parallel at N>1) at the top level;
+    at N=1 the decode (config 1) and prefill (config 2) lines as keyed sub-blocks."""
+    line, _ = run_config3(args, world, rank, dev)
+    line["config"]["sub_blocks"] = (
+        {k: f"BASELINE config {c}" for k, c in SUB_BLOCKS.items()} if world == 1 else
+        "none at N>1 (the dense configs run replicas only; BENCH at N=1 carries them)")
+    if world == 1:
+        if rank == 0 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_sample(3)
+        torch.cuda.empty_cache()
+        for key, c in SUB_BLOCKS.items():
+            sub, keep = (run_config1 if c == 1 else run_config2)(args, world, rank, dev)
+            del keep
+            torch.cuda.empty_cache()
+            if not args.no_cpu_baseline:
+                sub["cpu_baseline"] = cpu_baseline_sample(c)
+            line[key] = _sub_block(sub)
+    return line
+
+
+def reference_headline(args, world, rank):
+    """The reference arm of the default line: the same three workloads on the host cores."""
+    line = reference_arm(args, world, rank, config=3)
+    if line is None:
+        return None
+    line["config"]["sub_blocks"] = ({k: f"BASELINE config {c}" for k, c in SUB_BLOCKS.items()} if world == 1
+                                    else "none at N>1")
+    if world == 1:
+        for key, c in SUB_BLOCKS.items():
+            line[key] = _sub_block(reference_arm(args, world, rank, config=c))
+    return line
+
+
+def cpu_baseline_sample(config, seconds=8.0):
     """Bounded CPU sample of the same workload for the cpu_baseline key of our line."""
     torch.set_num_threads(os.cpu_count() or 1)
     step, work, scale, sample = cpu_workload(config)
@@ -925,7 +977,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
+    ap.add_argument("--config", type=int, default=None, choices=[0, 1, 2, 3, 4],
+                    help="one configuration alone (default: MoE line with decode/prefill sub-blocks)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -934,7 +987,7 @@ def main():
     out = json_channel()
 
     if args.impl == "reference":
-        line = reference_arm(args, world, rank)
+        line = reference_arm(args, world, rank) if args.config is not None else reference_headline(args, world, rank)
         if line is not None:
             print(json.dumps(line), file=out, flush=True)
         return 0
@@ -943,12 +996,13 @@ def main():
     dev = torch.device("cuda", local)
     init_dist(world, local)
     runners = {0: run_config0, 1: run_config1, 2: run_config2, 3: run_config3, 4: run_config4}
-    if args.config not in runners:
-        raise SystemExit(f"config {args.config}: not wired into bench.py yet")
-    line, _ = runners[args.config](args, world, rank, dev)
-    if rank == 0:
-        if world == 1 and not args.no_cpu_baseline:
+    if args.config is None:
+        line = headline(args, world, rank, dev)
+    else:
+        line, _ = runners[args.config](args, world, rank, dev)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample(args.config)
+    if rank == 0:
         print(json.dumps(line), file=out, flush=True)
     if world > 1:
         torch.distributed.barrier()

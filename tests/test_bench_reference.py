@@ -48,3 +48,21 @@ def test_reference_arm_under_torchrun_prints_once():
     assert len(lines) == 1, out.stdout
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
+
+
+def test_reference_arm_default_line_carries_the_three_metrics():
+    """The default run (no --config) is BASELINE.json's metric in one line: MoE tokens/s at
+    the top level, decode GB/s and prefill TOP/s as keyed sub-blocks at N=1, each a timed
+    run of the host path with its own cpu_baseline."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "1"], capture_output=True, text=True, timeout=900, env=env, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1, out.stdout
+    d = json.loads(lines[0])
+    assert KEYS <= set(d) and d["unit"] == "tokens/s" and d["value"] > 0
+    for key, unit in (("decode", "GB/s"), ("prefill", "TOP/s")):
+        sub = d[key]
+        assert sub["unit"] == unit and sub["value"] > 0 and sub["cpu_baseline"]["value"] == sub["value"]
+        assert sub["e2e"]["h2d_bytes_per_step"] == 0

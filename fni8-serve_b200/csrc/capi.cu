@@ -298,6 +298,19 @@ extern "C" int fni8_gemm_w8a8(const int8_t* a, const float* a_scale, const int8_
                            workspace, workspace_bytes, stream);
 }
 
+extern "C" int fni8_gemm_w8a8_act(const int8_t* a, const float* a_scale, const int8_t* w_gu, const float* s_gu, int act,
+                                  void* out, int out_dtype, int64_t M, int64_t I, int64_t K, void* stream) {
+  if (int s = check_gemm(a, w_gu, out, M, 2 * I, K)) return s;
+  if (I <= 0) return fail(FNI8_ERR_INVALID, "bad I=%lld", (long long)I);
+  if (out_dtype != FNI8_F16 && out_dtype != FNI8_BF16)
+    return fail(FNI8_ERR_INVALID, "out_dtype %d: expected F16 or BF16", out_dtype);
+  if (M > 0 && (a_scale == nullptr || s_gu == nullptr)) return fail(FNI8_ERR_INVALID, "null scale");
+  if (M == 0) return FNI8_OK;
+  // 256-row tiles on CTA pairs from 256 tokens on (prefill), as the plain tile GEMM
+  return tile_gemm_act(a, a_scale, M, w_gu, s_gu, 1, I, K, nullptr, nullptr, nullptr, 0, act, out,
+                       out_dtype == FNI8_F16 ? 0 : 1, tile_pair_enabled() && M >= 256, static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int fni8_gemm_w8a8_i32(const int8_t* a, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
                                   int path, void* workspace, size_t workspace_bytes, void* stream) {
   if (int s = check_gemm(a, w, acc, M, N, K)) return s;

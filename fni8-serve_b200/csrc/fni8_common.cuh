@@ -403,6 +403,51 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
+// Round to the storage type and back (the value the unfused chain would re-read).
+template <typename T>
+__device__ __forceinline__ float round_trip(float v) {
+  return to_f32<T>(from_f32<T>(v));
+}
+
+// g / d for d >= 1 (or +inf) in straight-line code: the hardware reciprocal estimate of d,
+// one Newton-Raphson step r' = r + r (1 - d r) (the classical reciprocal iteration, which
+// doubles the correct bits), the quotient q0 = g r', and Markstein's correction step
+// q = q0 + r' (g - q0 d) with fused multiply-adds (P. Markstein, "IA-64 and Elementary
+// Functions", 2000), which leaves q the correctly rounded quotient except in rare
+// double-rounding cases. d = +inf gives g * 0 (the IEEE quotient of a finite g). Unlike an
+// IEEE division it has no slow-path branch, so an unrolled epilogue can interleave many
+// elements.
+__device__ __forceinline__ float div_by_ge1(float g, float d) {
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(d));
+  r = __fmaf_rn(__fmaf_rn(-d, r, 1.0f), r, r);
+  const float q0 = __fmul_rn(g, r);
+  const float q = __fmaf_rn(__fmaf_rn(-q0, d, g), r, q0);
+  return isinf(d) ? __fmul_rn(g, 0.0f) : q;
+}
+
+// act(g) of act_and_mul (fni8serve/layers/activation.py:21-45) in fp32: SiLU g / (1 + e^-g),
+// or the tanh-approximated GELU 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))); CUDA's
+// expf / tanhf, no contraction outside the quotient. Shared by the row kernels and the GEMM
+// epilogue that applies it, so both round identically.
+template <int ACT>
+__device__ __forceinline__ float act_fn(float g) {
+  if constexpr (ACT == FNI8_ACT_SILU) {
+    return div_by_ge1(g, __fadd_rn(1.0f, expf(-g)));
+  } else {
+    const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+    float inner = __fmul_rn(k0, __fadd_rn(g, __fmul_rn(k1, __fmul_rn(g, __fmul_rn(g, g)))));
+    return __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, tanhf(inner)));
+  }
+}
+
+// One element of act_and_mul on the rounded gate and up values: act(g) rounded to T, times
+// u, rounded to T (the reference's F.silu(gate) * up on fp16 tensors).
+template <typename T, int ACT>
+__device__ __forceinline__ T act_mul_one(float g, float u) {
+  return from_f32<T>(__fmul_rn(round_trip<T>(act_fn<ACT>(g)), u));
+}
+
 }  // namespace fni8b
 
 // ---------------------------------------------------------------------------------

@@ -19,6 +19,12 @@ int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const in
                       const int32_t* seg_cnt, int64_t S, void* out, int out_mode, int bn, bool pair,
                       cudaStream_t st, const int32_t* row_tag = nullptr,
                       void* const* peer_out = nullptr, int n_peers = 0, int64_t peer_rows = 0);
+// Tile GEMM over a merged gate_up weight (gate rows [0, I), up rows [I, 2I)) whose
+// epilogue applies act_and_mul: out[M, I] in fp16/bf16 (out_mode 0/1), I % 128 == 0.
+// Dense when seg_expert is null; grouped over S segments of a [E, 2I, K] stack otherwise.
+int tile_gemm_act(const int8_t* a, const float* a_scale, int64_t M, const int8_t* w, const float* w_scale, int64_t E,
+                  int64_t I, int64_t K, const int32_t* seg_expert, const int32_t* seg_off, const int32_t* seg_cnt,
+                  int64_t S, int act, void* out, int out_mode, bool pair, cudaStream_t st);
 // Whether dense (prefill-size) and grouped tile GEMMs run on CTA pairs.
 bool tile_pair_enabled();
 bool grouped_pair_enabled();

@@ -74,6 +74,12 @@ struct Epi {
   void* peer_out[kMaxScatterPeers];
   int n_peers;
   int64_t peer_rows;
+  // ACTMUL kernels (gate_up with act_and_mul in the epilogue): the weight holds the gate
+  // rows [0, act_i) and the up rows [act_i, 2 act_i); tile n covers gate rows
+  // [128 n, 128 n + 128) in accumulator columns 0-127 and the matching up rows in columns
+  // 128-255; out is [rows, act_i]. act: FNI8_ACT_SILU or FNI8_ACT_GELU_TANH.
+  int act;
+  int act_i;
 };
 struct Groups {
   const int32_t* expert;
@@ -200,11 +206,44 @@ __device__ __forceinline__ void store_chunk_i32(const Epi& epi, const uint32_t (
   }
 }
 
-template <int BN, bool GROUPED, bool PAIR>
+// act_and_mul of 32 output columns of one row from the gate accumulators rg and the up
+// accumulators ru: each value is dequantised and rounded to T exactly as the plain
+// epilogue stores it, then act(gate) * up is formed as the act_and_mul kernels form it
+// (act_mul_one), so the fused result equals GEMM -> act_and_mul bit for bit. Packed as
+// four 16-byte chunks of 8 outputs.
+template <typename T, int ACT>
+__device__ __forceinline__ void act_chunk(const uint32_t (&rg)[32], const uint32_t (&ru)[32], float a_s,
+                                          const float* sg, const float* su, uint4 (&o)[4]) {
+#pragma unroll
+  for (int j8 = 0; j8 < 4; ++j8) {
+    T* oo = reinterpret_cast<T*>(&o[j8]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = j8 * 8 + j;
+      const float g = round_trip<T>(__fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(rg[c])), a_s), sg[c]));
+      const float u = round_trip<T>(__fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(ru[c])), a_s), su[c]));
+      oo[j] = act_mul_one<T, ACT>(g, u);
+    }
+  }
+}
+
+__device__ __forceinline__ void act_chunk_any(int mode, int act, const uint32_t (&rg)[32], const uint32_t (&ru)[32],
+                                              float a_s, const float* sg, const float* su, uint4 (&o)[4]) {
+  if (mode == kOutF16) {
+    if (act == FNI8_ACT_SILU) act_chunk<__half, FNI8_ACT_SILU>(rg, ru, a_s, sg, su, o);
+    else act_chunk<__half, FNI8_ACT_GELU_TANH>(rg, ru, a_s, sg, su, o);
+  } else {
+    if (act == FNI8_ACT_SILU) act_chunk<__nv_bfloat16, FNI8_ACT_SILU>(rg, ru, a_s, sg, su, o);
+    else act_chunk<__nv_bfloat16, FNI8_ACT_GELU_TANH>(rg, ru, a_s, sg, su, o);
+  }
+}
+
+template <int BN, bool GROUPED, bool PAIR, bool ACTMUL = false>
 __global__ void __launch_bounds__(kThreads, 1)
     w8a8_tile_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmOut, Epi epi, Groups grp, int M, int N, int K, int vec_ok,
                      int tma_store) {
+  static_assert(!ACTMUL || BN == 256, "act_and_mul tiles pair 128 gate with 128 up columns");
   using C = Cfg<BN, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -320,7 +359,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       auto load_b = [&](int s, int kx, int nb, int ex) {
         uint8_t* dst = smem + s * C::STAGE + C::A_BYTES;
-        if constexpr (PAIR) {
+        if constexpr (ACTMUL) {
+          // gate rows [128 nb, +128) then up rows [act_i + 128 nb, +128): two 128-row boxes
+          // that land where one 256-row box would (a pair's even CTA loads the gate half,
+          // the odd CTA the up half)
+          const int g_row = nb * 128, u_row = epi.act_i + nb * 128;
+          if constexpr (PAIR) {
+            const uint32_t bar = mapa_shared(smem_u32(&full[s]), lead);
+            const int r = half == 0 ? g_row : u_row;
+            if constexpr (GROUPED) tma_load_3d_pair(&tmB, bar, dst, kx, r, ex);
+            else tma_load_2d_pair(&tmB, bar, dst, kx, r);
+          } else {
+            if constexpr (GROUPED) {
+              tma_load_3d(&tmB, &full[s], dst, kx, g_row, ex);
+              tma_load_3d(&tmB, &full[s], dst + 128 * BK, kx, u_row, ex);
+            } else {
+              tma_load_2d(&tmB, &full[s], dst, kx, g_row);
+              tma_load_2d(&tmB, &full[s], dst + 128 * BK, kx, u_row);
+            }
+          }
+        } else if constexpr (PAIR) {
           const uint32_t bar = mapa_shared(smem_u32(&full[s]), lead);
           if constexpr (GROUPED) tma_load_3d_pair(&tmB, bar, dst, kx, nb * BN + b_off, ex);
           else tma_load_2d_pair(&tmB, bar, dst, kx, nb * BN + b_off);
@@ -477,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             valid = false;
           }
         } else {
-          orow = static_cast<uint8_t*>(epi.out) + row * static_cast<int64_t>(N) * 2;
+          orow = static_cast<uint8_t*>(epi.out) + row * static_cast<int64_t>(ACTMUL ? epi.act_i : N) * 2;
         }
       }
       const int nb0 = tc.n_blk * BN;
@@ -486,7 +544,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       float wreg = 0.0f, breg = 0.0f;
       float a_s = 0.0f;
       if (epi.mode != kOutI32) {
-        const int col = nb0 + et;
+        // ACTMUL: staged scales 0-127 are the gate rows', 128-255 the matching up rows'
+        const int col = !ACTMUL ? nb0 + et
+                                : (et < 128 ? tc.n_blk * 128 + et : epi.act_i + tc.n_blk * 128 + (et - 128));
         if (et < BN && col < N) {
           wreg = __ldg(wsc + col);
           if (epi.bias != nullptr)
@@ -513,6 +573,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       // residual add takes the per-thread path
       const bool slab_tma = tma_store && epi.residual == nullptr && epi.row_tag == nullptr &&
                             (!GROUPED || rows_here - q * 32 >= 32) && q * 32 < rows_here;
+      if constexpr (ACTMUL) {
+        // this warp's 64 of the tile's 128 product columns: gate accumulators at c, up at
+        // 128 + c; outputs at column 128 n + c of the [rows, act_i] product
+        const int p_beg = (ew >> 2) * 64;
+#pragma unroll 1
+        for (int c = p_beg; c < p_beg + 64; c += 32) {
+          uint32_t rg[32], ru[32];
+          tmem_ld32(tbase + static_cast<uint32_t>(c), rg);
+          tmem_ld32(tbase + static_cast<uint32_t>(128 + c), ru);
+          tmem_ld_wait();
+          const int n0 = tc.n_blk * 128 + c;
+          uint4 o[4];
+          act_chunk_any(epi.mode, epi.act, rg, ru, a_s, s_ws + c, s_ws + 128 + c, o);
+          if (slab_tma) {
+            uint8_t* buf = stg + ew * C::STG_BUF;
+            if (lane == 0) bulk_wait_group_read<0>();
+            __syncwarp();
+#pragma unroll
+            for (int j8 = 0; j8 < 4; ++j8)
+              *reinterpret_cast<uint4*>(buf + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = o[j8];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmOut, buf, n0, row0 + q * 32);
+              bulk_commit_group();
+            }
+          } else if (valid) {  // rows 16-byte aligned (checked on the host)
+#pragma unroll
+            for (int j8 = 0; j8 < 4; ++j8) *reinterpret_cast<uint4*>(orow + (n0 + 8 * j8) * 2) = o[j8];
+          }
+        }
+      } else
 #pragma unroll 1
       for (int c = c_beg; c < c_beg + BN / 2; c += 32) {
         uint32_t r[32];
@@ -585,11 +677,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, bool GROUPED, bool PAIR>
+template <int BN, bool GROUPED, bool PAIR, bool ACTMUL = false>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, bool tma_store, const Epi& epi,
            const Groups& grp, int M, int N, int K, int grid, bool vec_ok, cudaStream_t st) {
   using C = Cfg<BN, PAIR>;
-  auto kern = w8a8_tile_kernel<BN, GROUPED, PAIR>;
+  auto kern = w8a8_tile_kernel<BN, GROUPED, PAIR, ACTMUL>;
   static std::atomic<bool> configured[fni8h::kMaxDevices] = {};  // the attribute is set per device
   const int dev = fni8h::current_device();
   if (dev < 0 || dev >= fni8h::kMaxDevices) return fni8h::fail(FNI8_ERR_CUDA, "no current CUDA device");
@@ -765,6 +857,48 @@ int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const in
   if (bn == 256)
     return tile::launch<256, true, false>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
   return tile::launch<128, true, false>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);
+}
+
+int tile_gemm_act(const int8_t* a, const float* a_scale, int64_t M, const int8_t* w, const float* w_scale, int64_t E,
+                  int64_t I, int64_t K, const int32_t* seg_expert, const int32_t* seg_off, const int32_t* seg_cnt,
+                  int64_t S, int act, void* out, int out_mode, bool pair, cudaStream_t st) {
+  if (M <= 0 || I <= 0) return FNI8_OK;
+  if (I % 128 != 0) return fail(FNI8_ERR_UNSUPPORTED, "act_and_mul GEMM takes I a multiple of 128 (got %lld)", (long long)I);
+  if (act != FNI8_ACT_SILU && act != FNI8_ACT_GELU_TANH) return fail(FNI8_ERR_INVALID, "unknown activation %d", act);
+  if (out_mode != tile::kOutF16 && out_mode != tile::kOutBF16) return fail(FNI8_ERR_INVALID, "act GEMM out: F16 or BF16");
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) return fail(FNI8_ERR_ALIGN, "act GEMM output must be 16-byte aligned");
+  const bool grouped = seg_expert != nullptr;
+  if (grouped && S > tile::kMaxSeg)
+    return fail(FNI8_ERR_UNSUPPORTED, "at most %d segments (got %lld)", tile::kMaxSeg, (long long)S);
+  const int64_t N = 2 * I;  // weight rows: gate [0, I), up [I, 2I)
+  CUtensorMap ta, tb;
+  if (int s = encode_tmap_2d_i8(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, 128, 128)) return s;
+  if (grouped) {
+    if (int s = encode_tmap_3d_i8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)E, (uint64_t)K, (uint64_t)(N * K), 128, 128))
+      return s;
+  } else if (int s = encode_tmap_2d_i8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, 128, 128)) {
+    return s;
+  }
+  tile::Epi epi{a_scale, w_scale, nullptr, nullptr, out, out_mode, 0, tile_trigger()};
+  epi.act = act;
+  epi.act_i = static_cast<int>(I);
+  tile::Groups grp{seg_expert, seg_off, seg_cnt, grouped ? (int)S : 0};
+  const int sms = num_sms(current_device());
+  int grid = pair ? (sms & ~1) : sms;
+  if (!grouped) {  // one CTA per tile (two under PAIR), at most one per SM
+    const int64_t tiles = ((M + (pair ? 255 : 127)) / (pair ? 256 : 128)) * (I / 128);
+    const int64_t ctas = pair ? 2 * tiles : tiles;
+    grid = (int)(ctas < grid ? ctas : grid);
+  }
+  CUtensorMap to;
+  const bool tma_store = out_tma_map(&to, out, out_mode, M, I);
+  const int Mi = (int)M, Ni = (int)N, Ki = (int)K;
+  if (grouped) {
+    if (pair) return tile::launch<256, true, true, true>(ta, tb, to, tma_store, epi, grp, Mi, Ni, Ki, grid, true, st);
+    return tile::launch<256, true, false, true>(ta, tb, to, tma_store, epi, grp, Mi, Ni, Ki, grid, true, st);
+  }
+  if (pair) return tile::launch<256, false, true, true>(ta, tb, to, tma_store, epi, grp, Mi, Ni, Ki, grid, true, st);
+  return tile::launch<256, false, false, true>(ta, tb, to, tma_store, epi, grp, Mi, Ni, Ki, grid, true, st);
 }
 
 }  // namespace fni8h

@@ -117,8 +117,8 @@ __global__ void route_kernel(const float* __restrict__ logits, int T, int E, int
       if (e < E && !(keep & (1u << (e / epg)))) sel[i] = NEG;
     }
   }
-  float wsel[kMaxK];
-  int isel[kMaxK];
+  float my_w = 0.0f;
+  int my_i = 0;
   float wsum = 0.0f;
   for (int j = 0; j < k; ++j) {
     float v = NEG;
@@ -142,22 +142,20 @@ __global__ void route_kernel(const float* __restrict__ logits, int T, int E, int
       }
     }
     w = __shfl_sync(0xffffffffu, w, idx & 31);
-    if (j < kMaxK) {
-      wsel[j] = w;
-      isel[j] = idx;
+    if (lane == j) {  // slot j stays in lane j (k <= 32)
+      my_w = w;
+      my_i = idx;
     }
-    wsum = __fadd_rn(wsum, w);
+    wsum = __fadd_rn(wsum, w);  // in slot order, as the reference's sum over k
   }
-  if (lane == 0) {
+  if (lane < k) {
     const float denom = fmaxf(wsum, 1e-9f);
-    for (int j = 0; j < k; ++j) {
-      float w = norm_topk ? __fdiv_rn(wsel[j], denom) : wsel[j];
-      w = __fmul_rn(w, scaling);
-      if (wdtype == FNI8_F16) w = __half2float(__float2half_rn(w));
-      else if (wdtype == FNI8_BF16) w = __bfloat162float(__float2bfloat16_rn(w));
-      topi[static_cast<int64_t>(t) * k + j] = isel[j];
-      topw[static_cast<int64_t>(t) * k + j] = w;
-    }
+    float w = norm_topk ? __fdiv_rn(my_w, denom) : my_w;
+    w = __fmul_rn(w, scaling);
+    if (wdtype == FNI8_F16) w = __half2float(__float2half_rn(w));
+    else if (wdtype == FNI8_BF16) w = __bfloat162float(__float2bfloat16_rn(w));
+    topi[static_cast<int64_t>(t) * k + lane] = my_i;
+    topw[static_cast<int64_t>(t) * k + lane] = w;
   }
 }
 
@@ -185,11 +183,13 @@ __global__ void plan_hist(const int32_t* __restrict__ topi, int64_t n, int E, in
 // them is rewritten (a load issued after a store it might alias waits for that store).
 constexpr int kScanThreads = 256;
 __global__ void __launch_bounds__(kScanThreads) plan_scan(int32_t* __restrict__ hist, int n_chunks, int E,
-                                                          int32_t* __restrict__ counts, int32_t* __restrict__ offsets) {
+                                                          int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
+                                                          int32_t* __restrict__ iota) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ int tot[kMaxE];
   __shared__ int base[kMaxE];
+  __shared__ int warp_tot[kScanThreads / 32];
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int run = 0;
     for (int c0 = 0; c0 < n_chunks; c0 += 32) {
@@ -209,14 +209,36 @@ __global__ void __launch_bounds__(kScanThreads) plan_scan(int32_t* __restrict__ 
     counts[e] = run;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int e = 0; e < E; ++e) {
-      base[e] = run;
-      offsets[e] = run;
-      run += tot[e];
+  // exclusive scan of the expert totals, kScanThreads experts at a time (warp shuffles)
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int carry = 0;
+    for (int e0 = 0; e0 < E; e0 += kScanThreads) {
+      const int e = e0 + threadIdx.x;
+      const int v = e < E ? tot[e] : 0;
+      int x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (lane == 31) warp_tot[warp] = x;
+      __syncthreads();
+      int before = 0, all = 0;
+#pragma unroll
+      for (int w = 0; w < kScanThreads / 32; ++w) {
+        before += w < warp ? warp_tot[w] : 0;
+        all += warp_tot[w];
+      }
+      if (e < E) {
+        base[e] = carry + before + x - v;
+        offsets[e] = carry + before + x - v;
+        if (iota != nullptr) iota[e] = e;
+      }
+      carry += all;
+      __syncthreads();  // warp_tot is rewritten by the next round
     }
-    offsets[E] = run;
+    if (threadIdx.x == 0) offsets[E] = carry;
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -360,9 +382,11 @@ extern "C" size_t fni8_moe_plan_workspace_bytes(int64_t n_slots, int64_t E) {
   return align256(static_cast<size_t>(chunks > 0 ? chunks : 1) * E * 4);
 }
 
-extern "C" int fni8_moe_plan(const int32_t* topi, int64_t n_slots, int64_t E, int32_t* counts, int32_t* offsets,
-                             int32_t* row_of_slot, int32_t* slot_of_row, void* workspace, size_t workspace_bytes,
-                             void* stream) {
+// fni8_moe_plan, optionally also writing iota[e] = e (the segment -> expert table of a
+// grouped launch over all experts) from its scan kernel.
+static int moe_plan(const int32_t* topi, int64_t n_slots, int64_t E, int32_t* counts, int32_t* offsets,
+                    int32_t* row_of_slot, int32_t* slot_of_row, void* workspace, size_t workspace_bytes,
+                    int32_t* iota, void* stream) {
   if (n_slots < 0 || n_slots >= (1LL << 31) || E <= 0 || E > moe::kMaxE)
     return fail(FNI8_ERR_INVALID, "plan: bad sizes");
   if (counts == nullptr || offsets == nullptr) return fail(FNI8_ERR_INVALID, "plan: null counts/offsets");
@@ -375,7 +399,7 @@ extern "C" int fni8_moe_plan(const int32_t* topi, int64_t n_slots, int64_t E, in
   const int chunks = (int)((n_slots + moe::kChunk - 1) / moe::kChunk);
   int32_t* hist = static_cast<int32_t*>(workspace);
   if (chunks > 0) launch_pdl(moe::plan_hist, dim3(chunks), dim3(moe::kChunk), 0, st, topi, n_slots, (int)E, hist);
-  launch_pdl(moe::plan_scan, dim3(1), dim3(moe::kScanThreads), 0, st, hist, chunks, (int)E, counts, offsets);
+  launch_pdl(moe::plan_scan, dim3(1), dim3(moe::kScanThreads), 0, st, hist, chunks, (int)E, counts, offsets, iota);
   if (chunks > 0) {
     const size_t smem = 32 * E * sizeof(int);
     if (smem > 48 * 1024) {
@@ -387,6 +411,13 @@ extern "C" int fni8_moe_plan(const int32_t* topi, int64_t n_slots, int64_t E, in
   }
   FNI8_CHECK_LAUNCH("moe_plan");
   return FNI8_OK;
+}
+
+extern "C" int fni8_moe_plan(const int32_t* topi, int64_t n_slots, int64_t E, int32_t* counts, int32_t* offsets,
+                             int32_t* row_of_slot, int32_t* slot_of_row, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  return moe_plan(topi, n_slots, E, counts, offsets, row_of_slot, slot_of_row, workspace, workspace_bytes, nullptr,
+                  stream);
 }
 
 extern "C" int fni8_moe_gather_rows_i8(const int8_t* q, const float* scale, const int32_t* slot_of_row, int64_t R,
@@ -422,6 +453,22 @@ extern "C" int fni8_grouped_gemm_w8a8(const int8_t* a, const float* a_scale, int
   return tile_gemm_grouped(a, a_scale, R, w, w_scale, E, N, K, seg_expert, seg_off, seg_cnt, S, out, mode, bn,
                            grouped_pair_enabled(),
                            static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int fni8_grouped_gemm_w8a8_act(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w_gu,
+                                          const float* s_gu, int64_t E, int64_t I, int64_t K, const int32_t* seg_expert,
+                                          const int32_t* seg_off, const int32_t* seg_cnt, int64_t S, int act, void* out,
+                                          int out_dtype, void* stream) {
+  if (R < 0 || E <= 0 || I <= 0 || K <= 0 || S < 0) return fail(FNI8_ERR_INVALID, "grouped act: bad sizes");
+  if (K % 16 != 0) return fail(FNI8_ERR_UNSUPPORTED, "grouped act: K must be a multiple of 16");
+  if (R >= (1LL << 31) || 2 * I >= (1LL << 31) || K >= (1LL << 31))
+    return fail(FNI8_ERR_UNSUPPORTED, "grouped act: too large");
+  if (out_dtype != FNI8_F16 && out_dtype != FNI8_BF16) return fail(FNI8_ERR_INVALID, "grouped act: out_dtype");
+  if (R == 0 || S == 0) return FNI8_OK;
+  if (!a || !a_scale || !w_gu || !s_gu || !out || !seg_expert || !seg_off || !seg_cnt)
+    return fail(FNI8_ERR_INVALID, "grouped act: null pointer");
+  return tile_gemm_act(a, a_scale, R, w_gu, s_gu, E, I, K, seg_expert, seg_off, seg_cnt, S, act, out,
+                       out_dtype == FNI8_F16 ? 0 : 1, grouped_pair_enabled(), static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int fni8_grouped_gemm_w8a8_scatter(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w,
@@ -471,7 +518,7 @@ extern "C" int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_
 
 // Workspace layout of fni8_moe_experts_w8a8 (each piece 256-byte aligned).
 struct MoeLayout {
-  size_t xq, xs, plan, counts, offsets, iota, ros, sor, aq, as, h, hq, hs, y, total;
+  size_t plan, counts, offsets, iota, ros, sor, aq, as, h, hq, hs, y, total;
 };
 static MoeLayout moe_layout(int64_t T, int64_t H, int64_t k, int64_t E, int64_t I) {
   MoeLayout L;
@@ -482,8 +529,6 @@ static MoeLayout moe_layout(int64_t T, int64_t H, int64_t k, int64_t E, int64_t 
     off += align256(bytes);
     return o;
   };
-  L.xq = take(static_cast<size_t>(T) * H);
-  L.xs = take(static_cast<size_t>(T) * 4);
   L.plan = take(fni8_moe_plan_workspace_bytes(static_cast<int64_t>(R), E));
   L.counts = take(static_cast<size_t>(E) * 4);
   L.offsets = take(static_cast<size_t>(E + 1) * 4);
@@ -520,8 +565,6 @@ extern "C" int fni8_moe_experts_w8a8(const void* x, int dtype, int64_t T, int64_
     return fail(FNI8_ERR_WORKSPACE, "moe needs %zu workspace bytes (got %zu)", L.total, workspace_bytes);
   if (reinterpret_cast<uintptr_t>(workspace) & 255u) return fail(FNI8_ERR_ALIGN, "moe: workspace must be 256-byte aligned");
   uint8_t* b = static_cast<uint8_t*>(workspace);
-  int8_t* xq = reinterpret_cast<int8_t*>(b + L.xq);
-  float* xs = reinterpret_cast<float*>(b + L.xs);
   int32_t* counts = reinterpret_cast<int32_t*>(b + L.counts);
   int32_t* offsets = reinterpret_cast<int32_t*>(b + L.offsets);
   int32_t* iota = reinterpret_cast<int32_t*>(b + L.iota);
@@ -535,23 +578,21 @@ extern "C" int fni8_moe_experts_w8a8(const void* x, int dtype, int64_t T, int64_
   void* y = b + L.y;
   const int64_t R = T * top_k;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (int s = fni8_quantize_rows_i8(x, dtype, T, H, xq, xs, stream)) return s;
-  if (int s = fni8_moe_plan(topi, R, E, counts, offsets, ros, sor, b + L.plan, L.counts - L.plan, stream)) return s;
-  launch_pdl(moe::iota_kernel, dim3(1), dim3(256), 0, st, iota, (int)E);
-  FNI8_CHECK_LAUNCH("iota");
-  // Rows whose expert id is out of range are dropped by the plan; the grouped GEMMs
-  // only cover offsets[E] rows, so every gathered row is a routed one. R is an upper
-  // bound for the row count, which is only known on the device.
-  {
-    const int64_t blocks = (R + 7) / 8;
-    launch_pdl(moe::gather_rows, dim3((int)(blocks < 148 * 16 ? blocks : 148 * 16)), dim3(256), 0, st,
-               static_cast<const int8_t*>(xq), static_cast<const float*>(xs), static_cast<const int32_t*>(sor), R,
-               static_cast<const int32_t*>(offsets + E), (int)H, (int)top_k, aq, as);
-    FNI8_CHECK_LAUNCH("moe gather");
+  // plan first (with the segment table), then each token is quantised once and its int8
+  // row written straight to the grouped rows of its slots (no [T, H] int8 copy, no gather)
+  if (int s = moe_plan(topi, R, E, counts, offsets, ros, sor, b + L.plan, L.counts - L.plan, iota, stream)) return s;
+  if (int s = fni8_moe_quantize_scatter_i8(x, dtype, T, H, ros, top_k, aq, as, stream)) return s;
+  if (I % 128 == 0) {
+    // gate_up with act_and_mul in its epilogue: the [R, I] product, then its int8 rows
+    if (int s = fni8_grouped_gemm_w8a8_act(aq, as, R, w_gu, s_gu, E, I, H, iota, offsets, counts, E, act, h, dtype,
+                                           stream))
+      return s;
+    if (int s = fni8_quantize_rows_i8(h, dtype, R, I, hq, hs, stream)) return s;
+  } else {
+    if (int s = fni8_grouped_gemm_w8a8(aq, as, R, w_gu, s_gu, E, 2 * I, H, iota, offsets, counts, E, h, dtype, stream))
+      return s;
+    if (int s = fni8_act_and_mul_quant_i8(h, dtype, act, R, I, hq, hs, stream)) return s;
   }
-  if (int s = fni8_grouped_gemm_w8a8(aq, as, R, w_gu, s_gu, E, 2 * I, H, iota, offsets, counts, E, h, dtype, stream))
-    return s;
-  if (int s = fni8_act_and_mul_quant_i8(h, dtype, act, R, I, hq, hs, stream)) return s;
   if (int s = fni8_grouped_gemm_w8a8(hq, hs, R, w_dn, s_dn, E, H, I, iota, offsets, counts, E, y, dtype, stream))
     return s;
   return fni8_moe_combine(y, dtype, ros, topw, T, top_k, H, out, stream);

@@ -63,12 +63,6 @@ struct Vec8<__nv_bfloat16> {
   }
 };
 
-// Round to the storage type and back (the value the unfused chain would re-read).
-template <typename T>
-__device__ __forceinline__ float round_trip(float v) {
-  return to_f32<T>(from_f32<T>(v));
-}
-
 __device__ __forceinline__ float block_reduce_max(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -111,18 +105,6 @@ __device__ __forceinline__ uint2 quant8(const float (&f)[8], float inv) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) hi |= (static_cast<uint32_t>(static_cast<uint8_t>(quant_one(f[4 + i], inv)))) << (8 * i);
   return make_uint2(lo, hi);
-}
-
-template <int ACT>
-__device__ __forceinline__ float act_fn(float g) {
-  if constexpr (ACT == FNI8_ACT_SILU) {
-    return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-  } else {
-    // tanh-approximated GELU: 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3)))
-    const float k0 = 0.7978845608028654f, k1 = 0.044715f;
-    float inner = __fmul_rn(k0, __fadd_rn(g, __fmul_rn(k1, __fmul_rn(g, __fmul_rn(g, g)))));
-    return __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, tanhf(inner)));
-  }
 }
 
 // ---------------------------------------------------------------- vector kernels
@@ -608,10 +590,95 @@ int check_rows(const void* x, int dtype, int64_t M, int64_t K) {
   return FNI8_OK;
 }
 
+// Per-token quantisation whose int8 row goes straight to the expert-grouped rows of the
+// token's routed slots: row row_of_slot[t * k + j] of q_out (and its scale) for every slot j
+// that the plan placed (r >= 0). One CTA per token; the codes are those of quant_rows_vec.
+template <typename T, int MAXC>
+__global__ void __launch_bounds__(kRowThreads) quant_scatter_vec(const T* __restrict__ x, int64_t M, int K, int k,
+                                                                  const int32_t* __restrict__ row_of_slot,
+                                                                  int8_t* __restrict__ q_out,
+                                                                  float* __restrict__ s_out) {
+  __shared__ float red[kRowThreads / 32];
+  const int nch = K >> 3;
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
+    uint4 raw[MAXC];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = threadIdx.x + i * kRowThreads;
+      if (c < nch) {
+        raw[i] = __ldg(xr + c);
+        float f[8];
+        Vec8<T>::unpack(raw[i], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(f[j]));
+      }
+    }
+    amax = block_reduce_max(amax, red);
+    const float s = quant_scale(amax), inv = quant_inv(amax);
+    uint2 qv[MAXC];
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = threadIdx.x + i * kRowThreads;
+      if (c < nch) {
+        float f[8];
+        Vec8<T>::unpack(raw[i], f);
+        qv[i] = quant8(f, inv);
+      }
+    }
+    for (int j = 0; j < k; ++j) {
+      const int32_t r = __ldg(row_of_slot + row * k + j);
+      if (r < 0) continue;
+      uint2* qr = reinterpret_cast<uint2*>(q_out + static_cast<int64_t>(r) * K);
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int c = threadIdx.x + i * kRowThreads;
+        if (c < nch) qr[c] = qv[i];
+      }
+      if (threadIdx.x == 0) s_out[r] = s;
+    }
+  }
+}
+
+template <typename T>
+int quant_scatter_dispatch(const void* x, int64_t M, int64_t K, int64_t k, const int32_t* row_of_slot, int8_t* q,
+                           float* s, cudaStream_t st) {
+  const int64_t nch = K / 8;
+  const dim3 g(row_grid(M)), b(kRowThreads);
+  const T* xt = static_cast<const T*>(x);
+#define FNI8_QS(C) fni8h::launch_pdl(quant_scatter_vec<T, C>, g, b, 0, st, xt, M, (int)K, (int)k, row_of_slot, q, s)
+  if (nch <= kRowThreads) FNI8_QS(1);
+  else if (nch <= 2 * kRowThreads) FNI8_QS(2);
+  else if (nch <= 4 * kRowThreads) FNI8_QS(4);
+  else if (nch <= 8 * kRowThreads) FNI8_QS(8);
+  else FNI8_QS(16);
+#undef FNI8_QS
+  FNI8_CHECK_LAUNCH("quantize_scatter");
+  return FNI8_OK;
+}
+
 }  // namespace
 }  // namespace fni8b
 
 using namespace fni8b;
+
+extern "C" int fni8_moe_quantize_scatter_i8(const void* x, int dtype, int64_t T, int64_t K, const int32_t* row_of_slot,
+                                            int64_t top_k, int8_t* q_out, float* scale_out, void* stream) {
+  if (int st = check_rows(x, dtype, T, K)) return st;
+  if (top_k <= 0 || top_k > 64) return fni8h::fail(FNI8_ERR_INVALID, "quantize_scatter: bad top_k %lld", (long long)top_k);
+  if (T == 0) return FNI8_OK;
+  if (row_of_slot == nullptr || q_out == nullptr || scale_out == nullptr)
+    return fni8h::fail(FNI8_ERR_INVALID, "quantize_scatter: null pointer");
+  if (K % 8 != 0 || K / 8 > 16 * kRowThreads || !aligned16(x) || !aligned16(q_out))
+    return fni8h::fail(FNI8_ERR_UNSUPPORTED, "quantize_scatter: K a multiple of 8 (<= 16384), 16-byte aligned rows");
+  if (K % 16 != 0) return fni8h::fail(FNI8_ERR_UNSUPPORTED, "quantize_scatter: K a multiple of 16");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return dtype == FNI8_F16 ? quant_scatter_dispatch<__half>(x, T, K, top_k, row_of_slot, q_out, scale_out, s)
+                           : quant_scatter_dispatch<__nv_bfloat16>(x, T, K, top_k, row_of_slot, q_out, scale_out, s);
+}
 
 extern "C" int fni8_quantize_rows_i8(const void* x, int dtype, int64_t M, int64_t K, int8_t* q, float* scale,
                                      void* stream) {

@@ -17,16 +17,16 @@ FQWriter, save_fni8; fni8serve/loader.py:16, convert.py:320) reads and writes th
 Importing the package does not load the native library; the first op does, and it
 raises if the library has not been built (there is no fallback path).
 """
-from . import format, quant  # noqa: F401
+from . import format, mlp, quant  # noqa: F401
 from ._native import Fni8Error
 from .format import FQReader, FQWriter, save_fni8
-from .ops import (act_and_mul, act_and_mul_quant, device_status, gemm_i32, linear, linear_q, quantize_rows,
-                  rmsnorm, rmsnorm_quant)
+from .ops import (act_and_mul, act_and_mul_quant, device_status, gemm_i32, linear, linear_act_q, linear_q,
+                  quantize_rows, rmsnorm, rmsnorm_quant)
 from .qtensor import QTensor
 
 __all__ = [
     "QTensor", "linear", "rmsnorm", "act_and_mul", "quant",
-    "rmsnorm_quant", "act_and_mul_quant", "linear_q", "quantize_rows", "gemm_i32", "device_status",
+    "rmsnorm_quant", "act_and_mul_quant", "linear_q", "linear_act_q", "quantize_rows", "gemm_i32", "device_status",
     "Fni8Error", "FQReader", "FQWriter", "save_fni8", "format",
 ]
 __version__ = "0.1.0"

@@ -95,6 +95,42 @@ def grouped_gemm(a: torch.Tensor, a_scale: torch.Tensor, w: torch.Tensor, w_scal
     return out
 
 
+def quantize_scatter(x: torch.Tensor, row_of_slot: torch.Tensor, top_k: int, rows: int):
+    """Per-token int8 quantisation of x[T, H] written straight to the expert-grouped rows of
+    the plan: returns (q [rows, H] int8, scale [rows] fp32) with row row_of_slot[t*k + j]
+    holding token t's codes (the quantise + gather of the expert loop in one pass)."""
+    _need_cuda(x, "moe.quantize_scatter")
+    x2 = x.contiguous()
+    T, H = x2.shape
+    q = torch.empty((rows, H), dtype=torch.int8, device=x.device)
+    s = torch.empty((rows,), dtype=torch.float32, device=x.device)
+    nat.call("fni8_moe_quantize_scatter_i8", _vp(x2), _DT[x.dtype], T, H, _vp(row_of_slot.int().contiguous()), top_k,
+             _vp(q), _vp(s), _stream(x.device))
+    return q, s
+
+
+def grouped_gemm_act(a: torch.Tensor, a_scale: torch.Tensor, w_gu: torch.Tensor, s_gu: torch.Tensor,
+                     seg_expert: torch.Tensor, seg_off: torch.Tensor, seg_cnt: torch.Tensor, act: str = "silu",
+                     out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """The grouped gate_up projection with act_and_mul in its epilogue: out[R, I] where rows
+    [off[s], off[s]+cnt[s]) hold act(gate) * up of expert seg_expert[s] of w_gu [E, 2I, K].
+    Equal bit for bit to act_and_mul(grouped_gemm(...)). Rows outside every segment are
+    left unwritten."""
+    _need_cuda(a, "moe.grouped_gemm_act")
+    R, K = a.shape
+    E, two_i, K2 = w_gu.shape
+    if K2 != K:
+        raise ValueError("grouped_gemm_act: K mismatch")
+    I = two_i // 2
+    out = torch.empty((R, I), dtype=out_dtype, device=a.device)
+    S = seg_expert.numel()
+    nat.call("fni8_grouped_gemm_w8a8_act", _vp(a.contiguous()), _vp(a_scale.float().contiguous()), R,
+             _vp(w_gu.contiguous()), _vp(s_gu.float().contiguous()), E, I, K, _vp(seg_expert.int().contiguous()),
+             _vp(seg_off.int().contiguous()), _vp(seg_cnt.int().contiguous()), S, _ACT[act], _vp(out), _DT[out_dtype],
+             _stream(a.device))
+    return out
+
+
 def combine(y: torch.Tensor, row_of_slot: torch.Tensor, topw: torch.Tensor) -> torch.Tensor:
     """out[t] = sum_j topw[t, j] * y[row_of_slot[t*k + j]] (fp32 accumulation, one rounding)."""
     _need_cuda(y, "moe.combine")

@@ -285,6 +285,30 @@ def linear_q(q: torch.Tensor, scale: torch.Tensor, qt: QTensor, bias: torch.Tens
     return out.reshape(*q.shape[:-1], N)
 
 
+def linear_act_q(q: torch.Tensor, scale: torch.Tensor, gate_up: QTensor, act: str = "silu",
+                 out_dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """act_and_mul(gate_up(x)) on pre-quantised activations q[..., K] with per-token scale:
+    the merged gate_up weight [2I, K] (gate rows first, fni8serve/models/weights.py:49-50)
+    runs on the tile GEMM whose epilogue applies act(gate) * up, so only the [..., I]
+    product is written. Equal bit for bit to act_and_mul(linear_q(q, scale, gate_up)).
+    Needs I % 128 == 0 and no bias (fni8.mlp.GatedMLP checks both)."""
+    _need_cuda(q, "linear_act_q")
+    if act not in _ACT:
+        raise ValueError(f"fni8.linear_act_q: unsupported activation {act!r}")
+    K = q.shape[-1]
+    _check_weight(gate_up, q.device, K, "linear_act_q")
+    w, Kp = _k16_weight(gate_up, K)
+    q2 = q.reshape(-1, K).contiguous()
+    if Kp != K:
+        q2 = torch.nn.functional.pad(q2, (0, Kp - K))
+    s2 = scale.reshape(-1).to(torch.float32).contiguous()
+    M, I = q2.shape[0], gate_up.data.shape[0] // 2
+    out = torch.empty((M, I), dtype=out_dtype, device=q.device)
+    nat.call("fni8_gemm_w8a8_act", _vp(q2), _vp(s2), _vp(w), _vp(gate_up.scale), _ACT[act], _vp(out), _DT[out_dtype],
+             M, I, Kp, _stream(q.device))
+    return out.reshape(*q.shape[:-1], I)
+
+
 def _linear_w4a8(x: torch.Tensor, qt: QTensor, bias: torch.Tensor | None) -> torch.Tensor:
     """per_group_i4 / int4 weights (W4A8): packed data [N, K/2] uint8, scale [N, K/g] fp32."""
     if qt.codebook not in (None, "int4"):

@@ -173,6 +173,17 @@ FNI8_API int fni8_gemm_w8a8_noalloc(const int8_t* a, const float* a_scale, const
                                     const void* bias, const void* residual, void* out, int out_dtype, int64_t M,
                                     int64_t N, int64_t K, void* stream);
 
+/* GatedMLP's gate_up projection with act_and_mul applied in the GEMM epilogue
+ * (fni8serve/layers/mlp.py:39-40 with layers/activation.py:21-45): w_gu [2I, K] int8 holds
+ * the gate rows [0, I) and the up rows [I, 2I) in gate_up_weight's merge order
+ * (fni8serve/models/weights.py:49-50), s_gu [2I] their fp32 scales. out[M, I] =
+ * act(gate) * up in out_dtype, equal bit for bit to fni8_gemm_w8a8 into [M, 2I] followed
+ * by fni8_act_and_mul, without the [M, 2I] intermediate. act: FNI8_ACT_SILU or
+ * FNI8_ACT_GELU_TANH. I must be a multiple of 128 (FNI8_ERR_UNSUPPORTED otherwise), out
+ * 16-byte aligned. Tile kernel: meant for prefill-sized M. */
+FNI8_API int fni8_gemm_w8a8_act(const int8_t* a, const float* a_scale, const int8_t* w_gu, const float* s_gu, int act,
+                                void* out, int out_dtype, int64_t M, int64_t I, int64_t K, void* stream);
+
 /* Raw int32 accumulators acc[M, N] = a . w^T (the int8 x int8 -> int32 matmul of the
  * reference's gemm_w8a8; used for the bit-exact check). */
 FNI8_API int fni8_gemm_w8a8_i32(const int8_t* a, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K, int path,
@@ -230,6 +241,15 @@ FNI8_API int fni8_moe_plan(const int32_t* topi, int64_t n_slots, int64_t E, int3
                   int32_t* row_of_slot, int32_t* slot_of_row, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/* Per-token int8 quantisation of x[T, K] (as fni8_quantize_rows_i8) whose rows go straight
+ * to the expert-grouped order of fni8_moe_plan: token t's codes are written to row
+ * row_of_slot[t * top_k + j] of q_out (and its scale to scale_out) for every slot j the plan
+ * placed (entries < 0 are skipped). The quantise-then-gather of the reference's
+ * `xf[tok_idx]` (fni8serve/models/moe.py:103) in one pass over x. K % 16 == 0, K <= 16384,
+ * 16-byte aligned rows. */
+FNI8_API int fni8_moe_quantize_scatter_i8(const void* x, int dtype, int64_t T, int64_t K, const int32_t* row_of_slot,
+                                          int64_t top_k, int8_t* q_out, float* scale_out, void* stream);
+
 /* q_out[r] = q[slot_of_row[r] / top_k], scale_out likewise (int8 row gather). */
 FNI8_API int fni8_moe_gather_rows_i8(const int8_t* q, const float* scale, const int32_t* slot_of_row, int64_t R, int64_t K,
                             int64_t top_k, int8_t* q_out, float* scale_out, void* stream);
@@ -242,6 +262,17 @@ FNI8_API int fni8_moe_gather_rows_i8(const int8_t* q, const float* scale, const 
 FNI8_API int fni8_grouped_gemm_w8a8(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w, const float* w_scale,
                            int64_t E, int64_t N, int64_t K, const int32_t* seg_expert, const int32_t* seg_off,
                            const int32_t* seg_cnt, int64_t S, void* out, int out_dtype, void* stream);
+
+/* The grouped gate_up projection of the expert loop with act_and_mul in its epilogue:
+ * segment s multiplies rows [seg_off[s], seg_off[s] + seg_cnt[s]) of a[R, K] by expert
+ * seg_expert[s] of w_gu [E, 2I, K] (gate rows [0, I), up rows [I, 2I) per expert, fp32
+ * scales s_gu [E, 2I]) and writes act(gate) * up to out[R, I] (the GatedMLP inside each
+ * expert, fni8serve/models/moe.py:103, layers/mlp.py:39-40); equal bit for bit to
+ * fni8_grouped_gemm_w8a8 into [R, 2I] followed by fni8_act_and_mul. I % 128 == 0. */
+FNI8_API int fni8_grouped_gemm_w8a8_act(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w_gu,
+                                        const float* s_gu, int64_t E, int64_t I, int64_t K, const int32_t* seg_expert,
+                                        const int32_t* seg_off, const int32_t* seg_cnt, int64_t S, int act, void* out,
+                                        int out_dtype, void* stream);
 
 /* fni8_grouped_gemm_w8a8 whose output rows go elsewhere: row r (of a segment) is stored as
  * row (row_tag[r] & 0xFFFFFF) of peer_out[row_tag[r] >> 24], a [peer_rows, N] buffer of rank

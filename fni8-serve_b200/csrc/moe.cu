@@ -4,9 +4,12 @@
 //            selection, top-k by warp arg-max rounds, renormalisation, scaling
 //   plan     stable counting sort of the T*k (token, slot) pairs by expert in three
 //            short kernels (per-chunk histograms, one-CTA column scan, per-chunk ranks
-//            with __match_any_sync): row_of_slot / slot_of_row, deterministic order
-//   gather   int8 rows of the once-quantised tokens into expert-grouped order
-//   GEMMs    the grouped tcgen05 tile GEMM (gemm_tile.cu), one segment per expert
+//            with __match_any_sync): row_of_slot / slot_of_row, deterministic order, and
+//            the segment tables of the expert GEMMs
+//   quant    each token quantised once, its int8 row written to the expert-grouped rows
+//            of its slots (quant.cu, fni8_moe_quantize_scatter_i8)
+//   GEMMs    the grouped tcgen05 tile GEMM (gemm_tile.cu): gate_up with SiLU*up in its
+//            epilogue, the product quantised per row, then down; one segment per expert
 //   combine  out[t] = sum_j w[t,j] * y[row_of_slot[t*k+j]] in fp32, one rounding
 //
 // Nothing here waits on another CTA, so there is no watchdog word in this file.
@@ -182,9 +185,10 @@ __global__ void plan_hist(const int32_t* __restrict__ topi, int64_t n, int E, in
 // Each thread owns an expert column; its chunk counts are read 32 at a time before any of
 // them is rewritten (a load issued after a store it might alias waits for that store).
 constexpr int kScanThreads = 256;
+// Optional `tables` [E]: the segment -> expert table (e) of a grouped launch over all experts.
 __global__ void __launch_bounds__(kScanThreads) plan_scan(int32_t* __restrict__ hist, int n_chunks, int E,
                                                           int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
-                                                          int32_t* __restrict__ iota) {
+                                                          int32_t* __restrict__ tables) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ int tot[kMaxE];
@@ -231,9 +235,10 @@ __global__ void __launch_bounds__(kScanThreads) plan_scan(int32_t* __restrict__ 
         all += warp_tot[w];
       }
       if (e < E) {
-        base[e] = carry + before + x - v;
-        offsets[e] = carry + before + x - v;
-        if (iota != nullptr) iota[e] = e;
+        const int off = carry + before + x - v;
+        base[e] = off;
+        offsets[e] = off;
+        if (tables != nullptr) tables[e] = e;  // segment s -> expert s of a grouped launch
       }
       carry += all;
       __syncthreads();  // warp_tot is rewritten by the next round
@@ -281,12 +286,6 @@ __global__ void plan_scatter(const int32_t* __restrict__ topi, int64_t n, int E,
   } else if (i < n) {
     row_of_slot[i] = -1;
   }
-}
-
-__global__ void iota_kernel(int32_t* p, int n) {
-  pdl_launch_dependents();
-  pdl_wait();
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = i;
 }
 
 // ---------------------------------------------------------------- gather / combine
@@ -382,11 +381,11 @@ extern "C" size_t fni8_moe_plan_workspace_bytes(int64_t n_slots, int64_t E) {
   return align256(static_cast<size_t>(chunks > 0 ? chunks : 1) * E * 4);
 }
 
-// fni8_moe_plan, optionally also writing iota[e] = e (the segment -> expert table of a
-// grouped launch over all experts) from its scan kernel.
+// fni8_moe_plan, optionally also writing the segment tables of the expert GEMMs (4 x E
+// ints, laid out as plan_scan documents) from its scan kernel.
 static int moe_plan(const int32_t* topi, int64_t n_slots, int64_t E, int32_t* counts, int32_t* offsets,
                     int32_t* row_of_slot, int32_t* slot_of_row, void* workspace, size_t workspace_bytes,
-                    int32_t* iota, void* stream) {
+                    int32_t* tables, void* stream) {
   if (n_slots < 0 || n_slots >= (1LL << 31) || E <= 0 || E > moe::kMaxE)
     return fail(FNI8_ERR_INVALID, "plan: bad sizes");
   if (counts == nullptr || offsets == nullptr) return fail(FNI8_ERR_INVALID, "plan: null counts/offsets");
@@ -399,7 +398,7 @@ static int moe_plan(const int32_t* topi, int64_t n_slots, int64_t E, int32_t* co
   const int chunks = (int)((n_slots + moe::kChunk - 1) / moe::kChunk);
   int32_t* hist = static_cast<int32_t*>(workspace);
   if (chunks > 0) launch_pdl(moe::plan_hist, dim3(chunks), dim3(moe::kChunk), 0, st, topi, n_slots, (int)E, hist);
-  launch_pdl(moe::plan_scan, dim3(1), dim3(moe::kScanThreads), 0, st, hist, chunks, (int)E, counts, offsets, iota);
+  launch_pdl(moe::plan_scan, dim3(1), dim3(moe::kScanThreads), 0, st, hist, chunks, (int)E, counts, offsets, tables);
   if (chunks > 0) {
     const size_t smem = 32 * E * sizeof(int);
     if (smem > 48 * 1024) {
@@ -518,7 +517,7 @@ extern "C" int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_
 
 // Workspace layout of fni8_moe_experts_w8a8 (each piece 256-byte aligned).
 struct MoeLayout {
-  size_t plan, counts, offsets, iota, ros, sor, aq, as, h, hq, hs, y, total;
+  size_t plan, counts, offsets, tables, ros, sor, aq, as, h, hq, hs, y, total;
 };
 static MoeLayout moe_layout(int64_t T, int64_t H, int64_t k, int64_t E, int64_t I) {
   MoeLayout L;
@@ -532,7 +531,7 @@ static MoeLayout moe_layout(int64_t T, int64_t H, int64_t k, int64_t E, int64_t 
   L.plan = take(fni8_moe_plan_workspace_bytes(static_cast<int64_t>(R), E));
   L.counts = take(static_cast<size_t>(E) * 4);
   L.offsets = take(static_cast<size_t>(E + 1) * 4);
-  L.iota = take(static_cast<size_t>(E) * 4);
+  L.tables = take(static_cast<size_t>(E) * 4);
   L.ros = take(R * 4);
   L.sor = take(R * 4);
   L.aq = take(R * H);
@@ -567,7 +566,7 @@ extern "C" int fni8_moe_experts_w8a8(const void* x, int dtype, int64_t T, int64_
   uint8_t* b = static_cast<uint8_t*>(workspace);
   int32_t* counts = reinterpret_cast<int32_t*>(b + L.counts);
   int32_t* offsets = reinterpret_cast<int32_t*>(b + L.offsets);
-  int32_t* iota = reinterpret_cast<int32_t*>(b + L.iota);
+  int32_t* tables = reinterpret_cast<int32_t*>(b + L.tables);
   int32_t* ros = reinterpret_cast<int32_t*>(b + L.ros);
   int32_t* sor = reinterpret_cast<int32_t*>(b + L.sor);
   int8_t* aq = reinterpret_cast<int8_t*>(b + L.aq);
@@ -578,22 +577,27 @@ extern "C" int fni8_moe_experts_w8a8(const void* x, int dtype, int64_t T, int64_
   void* y = b + L.y;
   const int64_t R = T * top_k;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // plan first (with the segment table), then each token is quantised once and its int8
+  // plan first (with the segment tables), then each token is quantised once and its int8
   // row written straight to the grouped rows of its slots (no [T, H] int8 copy, no gather)
-  if (int s = moe_plan(topi, R, E, counts, offsets, ros, sor, b + L.plan, L.counts - L.plan, iota, stream)) return s;
+  if (int s = moe_plan(topi, R, E, counts, offsets, ros, sor, b + L.plan, L.counts - L.plan, tables, stream))
+    return s;
   if (int s = fni8_moe_quantize_scatter_i8(x, dtype, T, H, ros, top_k, aq, as, stream)) return s;
+  // One segment per expert on single CTAs (measured on B200 at BASELINE config 3: CTA
+  // pairs, for all rows or only for each expert's whole 256-row tiles, were slower).
+  const int32_t* seg_e = tables;
+  const int mode = dtype == FNI8_F16 ? 0 : 1;
   if (I % 128 == 0) {
     // gate_up with act_and_mul in its epilogue: the [R, I] product, then its int8 rows
-    if (int s = fni8_grouped_gemm_w8a8_act(aq, as, R, w_gu, s_gu, E, I, H, iota, offsets, counts, E, act, h, dtype,
-                                           stream))
+    if (int s = tile_gemm_act(aq, as, R, w_gu, s_gu, E, I, H, seg_e, offsets, counts, E, act, h, mode,
+                              grouped_pair_enabled(), st))
       return s;
     if (int s = fni8_quantize_rows_i8(h, dtype, R, I, hq, hs, stream)) return s;
   } else {
-    if (int s = fni8_grouped_gemm_w8a8(aq, as, R, w_gu, s_gu, E, 2 * I, H, iota, offsets, counts, E, h, dtype, stream))
+    if (int s = fni8_grouped_gemm_w8a8(aq, as, R, w_gu, s_gu, E, 2 * I, H, seg_e, offsets, counts, E, h, dtype, stream))
       return s;
     if (int s = fni8_act_and_mul_quant_i8(h, dtype, act, R, I, hq, hs, stream)) return s;
   }
-  if (int s = fni8_grouped_gemm_w8a8(hq, hs, R, w_dn, s_dn, E, H, I, iota, offsets, counts, E, y, dtype, stream))
+  if (int s = fni8_grouped_gemm_w8a8(hq, hs, R, w_dn, s_dn, E, H, I, seg_e, offsets, counts, E, y, dtype, stream))
     return s;
   return fni8_moe_combine(y, dtype, ros, topw, T, top_k, H, out, stream);
 }

@@ -227,6 +227,31 @@ __device__ __forceinline__ void act_chunk(const uint32_t (&rg)[32], const uint32
   }
 }
 
+// The plain epilogue's 32 outputs of one row: (float(acc) * a_s) * ws (+ bias) rounded once
+// to fp16 (mode kOutF16) or bf16, packed as four 16-byte chunks.
+__device__ __forceinline__ void dequant_chunk(int mode, const uint32_t (&r)[32], float a_s, const float* ws,
+                                              const float* bs, bool has_bias, uint4 (&o)[4]) {
+#pragma unroll
+  for (int j8 = 0; j8 < 4; ++j8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = j8 * 8 + j;
+      v[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[c])), a_s), ws[c]);
+      if (has_bias) v[j] = __fadd_rn(v[j], bs[c]);
+    }
+    if (mode == kOutF16) {
+      __half* oo = reinterpret_cast<__half*>(&o[j8]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) oo[j] = __float2half_rn(v[j]);
+    } else {
+      __nv_bfloat16* oo = reinterpret_cast<__nv_bfloat16*>(&o[j8]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) oo[j] = __float2bfloat16_rn(v[j]);
+    }
+  }
+}
+
 __device__ __forceinline__ void act_chunk_any(int mode, int act, const uint32_t (&rg)[32], const uint32_t (&ru)[32],
                                               float a_s, const float* sg, const float* su, uint4 (&o)[4]) {
   if (mode == kOutF16) {
@@ -576,16 +601,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (ACTMUL) {
         // this warp's 64 of the tile's 128 product columns: gate accumulators at c, up at
         // 128 + c; outputs at column 128 n + c of the [rows, act_i] product
+        // Software-pipelined: a chunk's outputs are formed in registers, then the next
+        // chunk's TMEM loads are issued, so they overlap the staging-buffer wait and store.
         const int p_beg = (ew >> 2) * 64;
+        uint32_t rg[32], ru[32];
+        tmem_ld32(tbase + static_cast<uint32_t>(p_beg), rg);
+        tmem_ld32(tbase + static_cast<uint32_t>(128 + p_beg), ru);
+        tmem_ld_wait();
+        tmem_regs_ready(rg);
+        tmem_regs_ready(ru);
 #pragma unroll 1
         for (int c = p_beg; c < p_beg + 64; c += 32) {
-          uint32_t rg[32], ru[32];
-          tmem_ld32(tbase + static_cast<uint32_t>(c), rg);
-          tmem_ld32(tbase + static_cast<uint32_t>(128 + c), ru);
-          tmem_ld_wait();
+          const bool more = c + 32 < p_beg + 64;
           const int n0 = tc.n_blk * 128 + c;
           uint4 o[4];
           act_chunk_any(epi.mode, epi.act, rg, ru, a_s, s_ws + c, s_ws + 128 + c, o);
+          if (more) {
+            tmem_ld32(tbase + static_cast<uint32_t>(c + 32), rg);
+            tmem_ld32(tbase + static_cast<uint32_t>(128 + c + 32), ru);
+          }
           if (slab_tma) {
             uint8_t* buf = stg + ew * C::STG_BUF;
             if (lane == 0) bulk_wait_group_read<0>();
@@ -603,55 +637,56 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j8 = 0; j8 < 4; ++j8) *reinterpret_cast<uint4*>(orow + (n0 + 8 * j8) * 2) = o[j8];
           }
+          if (more) {
+            tmem_ld_wait();
+            tmem_regs_ready(rg);
+            tmem_regs_ready(ru);
+          }
         }
-      } else
-#pragma unroll 1
-      for (int c = c_beg; c < c_beg + BN / 2; c += 32) {
+      } else {
+        // Software-pipelined like the ACTMUL loop: dequantise a chunk into registers, issue
+        // the next chunk's TMEM load, then wait for the staging buffer and store.
+        const int c_end = c_beg + BN / 2;
         uint32_t r[32];
-        tmem_ld32(tbase + static_cast<uint32_t>(c), r);
+        tmem_ld32(tbase + static_cast<uint32_t>(c_beg), r);
         tmem_ld_wait();
-        const int n0 = nb0 + c;
-        if (n0 >= N) continue;
-        if (slab_tma) {
-          uint8_t* buf = stg + ew * C::STG_BUF;
-          if (lane == 0) bulk_wait_group_read<0>();  // the previous store from this buffer has read it
-          __syncwarp();
+        tmem_regs_ready(r);
+#pragma unroll 1
+        for (int c = c_beg; c < c_end; c += 32) {
+          const int n0 = nb0 + c;
+          const bool more = c + 32 < c_end;
+          if (slab_tma && n0 < N) {
+            uint4 o[4];
+            dequant_chunk(epi.mode, r, a_s, s_ws + c, s_bias + c, epi.bias != nullptr, o);
+            if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
+            uint8_t* buf = stg + ew * C::STG_BUF;
+            if (lane == 0) bulk_wait_group_read<0>();  // the previous store from this buffer has read it
+            __syncwarp();
 #pragma unroll
-          for (int j8 = 0; j8 < 4; ++j8) {  // 8 outputs = one 16-byte chunk of this row
-            float v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int col = c + j8 * 8 + j;
-              v[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j8 * 8 + j])), a_s), s_ws[col]);
-              if (epi.bias != nullptr) v[j] = __fadd_rn(v[j], s_bias[col]);
+            for (int j8 = 0; j8 < 4; ++j8)  // 64-byte swizzle of the store map: chunk ^= (row >> 1) & 3
+              *reinterpret_cast<uint4*>(buf + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = o[j8];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmOut, buf, n0, row0 + q * 32);
+              bulk_commit_group();
             }
-            uint4 o;
-            if (epi.mode == kOutF16) {
-              __half* oo = reinterpret_cast<__half*>(&o);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) oo[j] = __float2half_rn(v[j]);
-            } else {
-              __nv_bfloat16* oo = reinterpret_cast<__nv_bfloat16*>(&o);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) oo[j] = __float2bfloat16_rn(v[j]);
+          } else {
+            if (n0 < N && valid) {
+              if (epi.mode == kOutI32) store_chunk_i32(epi, r, row, n0, N, vec_ok != 0);
+              else if (epi.mode == kOutF16)
+                store_chunk<__half>(epi, r, row, reinterpret_cast<__half*>(orow), n0, N, a_s, s_ws + c, s_bias + c,
+                                    vec_ok != 0);
+              else
+                store_chunk<__nv_bfloat16>(epi, r, row, reinterpret_cast<__nv_bfloat16*>(orow), n0, N, a_s,
+                                           s_ws + c, s_bias + c, vec_ok != 0);
             }
-            // 64-byte swizzle of the store map: 16-byte chunk index ^= (row >> 1) & 3
-            *reinterpret_cast<uint4*>(buf + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = o;
+            if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tma_store_2d(&tmOut, buf, n0, row0 + q * 32);
-            bulk_commit_group();
+          if (more) {
+            tmem_ld_wait();
+            tmem_regs_ready(r);
           }
-        } else if (valid) {
-          if (epi.mode == kOutI32) store_chunk_i32(epi, r, row, n0, N, vec_ok != 0);
-          else if (epi.mode == kOutF16)
-            store_chunk<__half>(epi, r, row, reinterpret_cast<__half*>(orow), n0, N, a_s, s_ws + c, s_bias + c,
-                                vec_ok != 0);
-          else
-            store_chunk<__nv_bfloat16>(epi, r, row, reinterpret_cast<__nv_bfloat16*>(orow), n0, N, a_s, s_ws + c,
-                                       s_bias + c, vec_ok != 0);
         }
       }
       tc_fence_before();

@@ -111,11 +111,16 @@ __device__ __forceinline__ uint2 quant8(const float (&f)[8], float inv) {
 // MODE 0: quantise rows of x.
 template <typename T, int MAXC>
 __global__ void __launch_bounds__(kRowThreads) quant_rows_vec(const T* __restrict__ x, int64_t M, int K,
-                                                               int8_t* __restrict__ q, float* __restrict__ scale) {
+                                                               int8_t* __restrict__ q, float* __restrict__ scale,
+                                                               const int32_t* __restrict__ m_dev) {
   __shared__ float red[kRowThreads / 32];
   const int nch = K >> 3;
   pdl_launch_dependents();  // dependents may start now; they wait for our completion
   pdl_wait();
+  if (m_dev != nullptr) {  // rows known only on the device: M is their upper bound
+    const int64_t m = *m_dev;
+    M = m < M ? m : M;
+  }
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + row * K);
     uint4 raw[MAXC];
@@ -487,25 +492,28 @@ int row_grid(int64_t M) {  // one row per CTA up to ~64 CTAs per SM (measured be
 }
 
 template <typename T, int MAXC>
-void launch_quant_vec(const void* x, int64_t M, int K, int8_t* q, float* s, cudaStream_t st) {
+void launch_quant_vec(const void* x, int64_t M, int K, int8_t* q, float* s, cudaStream_t st, const int32_t* m_dev) {
   fni8h::launch_pdl(quant_rows_vec<T, MAXC>, dim3(row_grid(M)), dim3(kRowThreads), 0, st, static_cast<const T*>(x), M,
-                    K, q, s);
+                    K, q, s, m_dev);
 }
 
+// m_dev (optional): the row count lives on the device, M is its upper bound (vector path
+// only: the caller checks alignment first).
 template <typename T>
-int quant_dispatch(const void* x, int64_t M, int64_t K, int8_t* q, float* s, cudaStream_t st) {
+int quant_dispatch(const void* x, int64_t M, int64_t K, int8_t* q, float* s, cudaStream_t st,
+                   const int32_t* m_dev = nullptr) {
   const int64_t nch = K / 8;
   const bool vec = (K % 8 == 0) && aligned16(x) && aligned16(q) && nch <= 16 * kRowThreads;
   if (vec && launch_row_warp<T, 0, 0>(static_cast<const T*>(x), nullptr, nullptr, M, (int)K, 0.f, 0, nullptr, nullptr, q,
-                                      s, st)) {
+                                      s, st, m_dev)) {
     FNI8_CHECK_LAUNCH("quantize_rows_i8");
     return FNI8_OK;
   }
   if (vec) {
-    if (nch <= 2 * kRowThreads) launch_quant_vec<T, 2>(x, M, (int)K, q, s, st);
-    else if (nch <= 4 * kRowThreads) launch_quant_vec<T, 4>(x, M, (int)K, q, s, st);
-    else if (nch <= 8 * kRowThreads) launch_quant_vec<T, 8>(x, M, (int)K, q, s, st);
-    else launch_quant_vec<T, 16>(x, M, (int)K, q, s, st);
+    if (nch <= 2 * kRowThreads) launch_quant_vec<T, 2>(x, M, (int)K, q, s, st, m_dev);
+    else if (nch <= 4 * kRowThreads) launch_quant_vec<T, 4>(x, M, (int)K, q, s, st, m_dev);
+    else if (nch <= 8 * kRowThreads) launch_quant_vec<T, 8>(x, M, (int)K, q, s, st, m_dev);
+    else launch_quant_vec<T, 16>(x, M, (int)K, q, s, st, m_dev);
   } else {
     fni8h::launch_pdl(row_scalar<T, 0, 0>, dim3(row_grid(M)), dim3(kRowThreads), 0, st, static_cast<const T*>(x),
                       static_cast<const T*>(nullptr), static_cast<const T*>(nullptr), M, (int)K, 0.f, 0,
@@ -754,6 +762,19 @@ extern "C" int fni8_act_and_mul(const void* x, int dtype, int act, int64_t M, in
 extern "C" int fni8_act_and_mul_quant_i8(const void* x, int dtype, int act, int64_t M, int64_t I, int8_t* q,
                                          float* scale, void* stream) {
   return act_common(x, dtype, act, M, I, nullptr, q, scale, stream, true);
+}
+
+extern "C" int fni8_quantize_rows_i8_rows(const void* x, int dtype, int64_t M, int64_t K, const int32_t* rows_dev,
+                                          int8_t* q, float* scale, void* stream) {
+  if (int st = check_rows(x, dtype, M, K)) return st;
+  if (M == 0) return FNI8_OK;
+  if (rows_dev == nullptr || q == nullptr || scale == nullptr)
+    return fni8h::fail(FNI8_ERR_INVALID, "null device row count or output");
+  if (K % 8 != 0 || K / 8 > 16 * kRowThreads || !aligned16(x) || !aligned16(q))
+    return fni8h::fail(FNI8_ERR_UNSUPPORTED, "quantize_rows_i8_rows: K a multiple of 8 (<= 16384), 16-byte aligned rows");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return dtype == FNI8_F16 ? quant_dispatch<__half>(x, M, K, q, scale, s, rows_dev)
+                           : quant_dispatch<__nv_bfloat16>(x, M, K, q, scale, s, rows_dev);
 }
 
 extern "C" int fni8_act_and_mul_quant_i8_rows(const void* x, int dtype, int act, int64_t M, int64_t I,

@@ -33,6 +33,7 @@ SIGNATURES: dict[str, tuple] = {
     "fni8_device_status": (_i, [ctypes.POINTER(_i)]),
     "fni8_watchdog_selftest": (_i, [_i64, _i, _p]),
     "fni8_quantize_rows_i8": (_i, [_p, _i, _i64, _i64, _p, _p, _p]),
+    "fni8_quantize_rows_i8_rows": (_i, [_p, _i, _i64, _i64, _p, _p, _p, _p]),
     "fni8_rmsnorm": (_i, [_p, _p, _p, _i, _i64, _i64, _f, _i, _p, _p, _p]),
     "fni8_rmsnorm_quant_i8": (_i, [_p, _p, _p, _i, _i64, _i64, _f, _i, _p, _p, _p, _p, _p]),
     "fni8_act_and_mul": (_i, [_p, _i, _i, _i64, _i64, _p, _p]),

@@ -32,7 +32,7 @@ import torch
 import torch.distributed as dist
 
 from . import _native as nat
-from .moe import ExpertStack, combine, grouped_gemm, plan
+from .moe import ExpertStack, combine, grouped_gemm, grouped_gemm_act, plan
 from .ops import _ACT, _DT, _need_cuda, _stream, _vp, act_and_mul_quant, linear, quantize_rows
 from .qtensor import QTensor
 
@@ -208,6 +208,16 @@ def grouped_gemm_scatter(a, a_scale, w, w_scale, seg_expert, seg_off, seg_cnt, r
              _stream(a.device))
 
 
+def quantize_rows_dev(x: torch.Tensor, rows_dev: torch.Tensor):
+    """fni8 quantize_rows over the first rows_dev[0] rows of x (the rest left as is)."""
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty((M,), dtype=torch.float32, device=x.device)
+    nat.call("fni8_quantize_rows_i8_rows", _vp(x), _DT[x.dtype], M, K, _vp(rows_dev), _vp(q), _vp(s),
+             _stream(x.device))
+    return q, s
+
+
 def act_and_mul_quant_rows(h: torch.Tensor, rows_dev: torch.Tensor, act: str = "silu"):
     """fni8 act_and_mul_quant over the first rows_dev[0] rows of h (the rest left as is)."""
     I = h.shape[-1] // 2
@@ -322,8 +332,13 @@ class ExpertParallelMoE:
         ep_dispatch(xq, xs, sor, offsets, E, self.rank, k, dst_base, X, T * k)
         dist.all_reduce(self._tick, op=dist.ReduceOp.MAX, group=self.group)  # every rank's rows have landed
         L = self.local
-        h = grouped_gemm(X.rq, X.rs, L.w_gu, L.s_gu, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
-        hq, hs = act_and_mul_quant_rows(h, n_recv, self.act)
+        if L.intermediate % 128 == 0:  # gate_up with act_and_mul in its epilogue
+            p = grouped_gemm_act(X.rq, X.rs, L.w_gu, L.s_gu, self._iota, seg_off, seg_cnt, act=self.act,
+                                 out_dtype=x.dtype)
+            hq, hs = quantize_rows_dev(p, n_recv)
+        else:
+            h = grouped_gemm(X.rq, X.rs, L.w_gu, L.s_gu, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
+            hq, hs = act_and_mul_quant_rows(h, n_recv, self.act)
         if self.fuse_return:  # each output row goes straight to its source's slot
             grouped_gemm_scatter(hq, hs, L.w_dn, L.s_dn, self._iota, seg_off, seg_cnt, X.tag, X.peer["back"],
                                  X.world, X.back_rows, out_dtype=x.dtype)

@@ -101,6 +101,12 @@ FNI8_API int fni8_watchdog_selftest(int64_t wait_us, int dirty_scratch, void* st
 FNI8_API int fni8_quantize_rows_i8(const void* x, int dtype, int64_t M, int64_t K, int8_t* q, float* scale,
                           void* stream);
 
+/* fni8_quantize_rows_i8 over the first *rows_dev rows of x[M, K] (M is their upper bound;
+ * the count lives in device memory, e.g. the rows an expert-parallel rank received; rows past
+ * it are left untouched). K a multiple of 8 (<= 16384), 16-byte aligned rows. */
+FNI8_API int fni8_quantize_rows_i8_rows(const void* x, int dtype, int64_t M, int64_t K, const int32_t* rows_dev,
+                                        int8_t* q, float* scale, void* stream);
+
 /* RMSNorm over the last dim: replaces fni8.rmsnorm (fni8serve/layers/norm.py:38-58).
  * y = dtype((x_f32 * (1/sqrt(mean(x_f32^2) + eps))) * g), g = w or (1 + w) when
  * unit_offset. With residual != NULL the input is x + residual (rounded to dtype), which

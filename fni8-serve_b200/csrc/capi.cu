@@ -1,8 +1,8 @@
 // Library plumbing behind include/fni8_b200.h: status strings, thread-local error
 // messages, TMA descriptor encoding (through the runtime's driver entry point, so the
 // library does not link libcuda and loads on machines without a GPU), and the dense
-// GEMM / linear entry points that pick between the tile kernel (gemm_tile.cu) and the
-// skinny stream-K kernel (gemm_stream.cu).
+// GEMM / linear entry points that pick between the tile kernel (gemm_tile.cu), the
+// split-K decode kernel (gemm_splitk.cu) and the stream-K kernel (gemm_stream.cu).
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
@@ -134,39 +134,27 @@ static int check_gemm(const int8_t* a, const int8_t* w, const void* out, int64_t
 }
 
 // Largest M the AUTO choice sends to the stream-K kernel: none by default, the split-K
-// kernel measured faster at every decode size on B200 (FNI8_STREAM_AUTO_MAX_M overrides).
+// kernel measured faster at every decode size on B200 (FNI8_TUNE_STREAM_AUTO_MAX_M).
 static int64_t stream_auto_max_m() {
-  static int64_t m = [] {
-    const char* e = getenv("FNI8_STREAM_AUTO_MAX_M");
-    const long v = e ? atol(e) : 0;
-    return (int64_t)(v < 0 ? 0 : (v > kStreamMaxM ? kStreamMaxM : v));
-  }();
-  return m;
+  constexpr int64_t m = FNI8_TUNE_STREAM_AUTO_MAX_M;
+  return m < 0 ? 0 : (m > kStreamMaxM ? kStreamMaxM : m);
 }
 
 // Largest M the AUTO choice sends to the split-K kernel: measured on B200, it beats the
 // tile kernel up to 256 tokens whenever its grid fits on the GPU in one wave
-// (FNI8_SPLITK_AUTO_MAX_M overrides it for measurements).
+// (FNI8_TUNE_SPLITK_AUTO_MAX_M).
 static int64_t splitk_auto_max_m() {
-  static int64_t m = [] {
-    const char* e = getenv("FNI8_SPLITK_AUTO_MAX_M");
-    const long v = e ? atol(e) : 256;
-    return (int64_t)(v < 0 ? 0 : (v > kSplitkMaxM ? kSplitkMaxM : v));
-  }();
-  return m;
+  constexpr int64_t m = FNI8_TUNE_SPLITK_AUTO_MAX_M;
+  return m < 0 ? 0 : (m > kSplitkMaxM ? kSplitkMaxM : m);
 }
 
 // Above 64 tokens a weight matrix with at least this many 256-row tiles goes to the tile
 // kernel, whose 256-column tiles let each MMA consume twice the weight bytes of a split-K
 // MMA. Default: one tile per SM (an LM head, N = 151936, measured on B200);
-// FNI8_WIDE_MIN_TILES overrides it for measurements.
+// (FNI8_TUNE_WIDE_MIN_TILES).
 static int64_t wide_min_tiles() {
-  static int64_t v = [] {
-    const char* e = getenv("FNI8_WIDE_MIN_TILES");
-    const long x = e ? atol(e) : 0;
-    return (int64_t)(x > 0 ? x : num_sms(current_device()));
-  }();
-  return v;
+  constexpr int64_t x = FNI8_TUNE_WIDE_MIN_TILES;
+  return x > 0 ? x : num_sms(current_device());
 }
 
 static bool wide_weights(int64_t M, int64_t N) { return M > 64 && (N + 255) / 256 >= wide_min_tiles(); }
@@ -196,13 +184,9 @@ static int check_path(int path, int64_t M) {
 }
 
 // Column width of a single-CTA tile: 256 where there are two 256-wide tiles per SM, else
-// 128 (FNI8_TILE_BN=128/256 forces one, for measurements).
+// 128 (FNI8_TUNE_TILE_BN = 128 or 256 forces one).
 static int pick_bn(int64_t M, int64_t N) {
-  static const int forced = [] {
-    const char* e = getenv("FNI8_TILE_BN");
-    const int x = e ? atoi(e) : 0;
-    return (x == 128 || x == 256) ? x : 0;
-  }();
+  constexpr int forced = (FNI8_TUNE_TILE_BN == 128 || FNI8_TUNE_TILE_BN == 256) ? FNI8_TUNE_TILE_BN : 0;
   if (forced) return forced;
   const int64_t tiles256 = ((M + 127) / 128) * ((N + 255) / 256);
   return tiles256 >= 2 * num_sms(current_device()) ? 256 : 128;
@@ -246,13 +230,12 @@ extern "C" int fni8_device_status(int* code_out) {
   if (code_out == nullptr) return fail(FNI8_ERR_INVALID, "null code_out");
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cuda_status(e, "cudaDeviceSynchronize");
-  int codes[6] = {0, 0, 0, 0, 0, 0};
+  int codes[5] = {0, 0, 0, 0, 0};
   if (int s = tile_status_read_and_clear(&codes[0])) return s;
   if (int s = stream_status_read_and_clear(&codes[1])) return s;
-  if (int s = skinny_status_read_and_clear(&codes[2])) return s;
-  if (int s = splitk_status_read_and_clear(&codes[3])) return s;
-  if (int s = w4a8_status_read_and_clear(&codes[4])) return s;
-  if (int s = ep_status_read_and_clear(&codes[5])) return s;
+  if (int s = splitk_status_read_and_clear(&codes[2])) return s;
+  if (int s = w4a8_status_read_and_clear(&codes[3])) return s;
+  if (int s = ep_status_read_and_clear(&codes[4])) return s;
   *code_out = 0;
   for (int v : codes)
     if (*code_out == 0) *code_out = v;
@@ -338,15 +321,8 @@ extern "C" int fni8_linear_w8a8_ex(const void* x, int dtype, const int8_t* w, co
   if (x == nullptr || w == nullptr || w_scale == nullptr || out == nullptr)
     return fail(FNI8_ERR_INVALID, "null linear operand");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // decode sizes: per-token quantisation fused into the GEMM, one launch, no scratch
-  const bool fused_ok = skinny_supported(x, M, N, K);
-  if (path == FNI8_PATH_FUSED) {
-    if (!fused_ok) return fail(FNI8_ERR_UNSUPPORTED, "fused decode linear takes M <= %lld and 16-byte aligned x",
-                               (long long)kSkinnyMaxM);
-    return skinny_linear(x, dtype == FNI8_BF16, w, w_scale, bias, out, M, N, K, st);
-  }
-  if (path == FNI8_PATH_AUTO && fused_ok && M <= skinny_auto_max_m())
-    return skinny_linear(x, dtype == FNI8_BF16, w, w_scale, bias, out, M, N, K, st);
+  if (path == FNI8_PATH_FUSED)
+    return fail(FNI8_ERR_UNSUPPORTED, "FNI8_PATH_FUSED is not built (measured slower than quantiser + split-K)");
   if (q_scratch == nullptr || s_scratch == nullptr) return fail(FNI8_ERR_INVALID, "null linear scratch");
   if (int s = fni8_quantize_rows_i8(x, dtype, M, K, q_scratch, s_scratch, stream)) return s;
   return gemm_any(q_scratch, s_scratch, w, w_scale, bias, nullptr, out, dtype == FNI8_F16 ? 0 : 1, M, N, K, path,

@@ -16,6 +16,7 @@
 #include <atomic>
 
 #include "../../include/fni8_b200.h"
+#include "tuning.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "fni8-serve_b200 kernels target sm_100a only"
@@ -488,14 +489,8 @@ int encode_tmap_3d_i8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t 
 }  // namespace fni8h
 
 namespace fni8h {
-// Programmatic dependent launch is on unless FNI8_PDL=0 (a measurement switch).
-inline int pdl_enabled() {
-  static const int on = [] {
-    const char* e = getenv("FNI8_PDL");
-    return (e != nullptr && e[0] == '0') ? 0 : 1;
-  }();
-  return on;
-}
+// Programmatic dependent launch between the library's kernels (FNI8_TUNE_PDL, on).
+inline int pdl_enabled() { return FNI8_TUNE_PDL != 0 ? 1 : 0; }
 
 // Launch with programmatic dependent launch allowed: the kernel may be scheduled while
 // the previous kernel on the stream drains; it must execute griddepcontrol.wait before

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "tuning.h"
+
 namespace fni8h {
 
 constexpr int kMaxDevices = 64;
@@ -40,13 +42,6 @@ constexpr int64_t kStreamMaxM = 256;
 // Re-zero the allocation-free GEMM's built-in scratch on the current device (synchronous).
 int noalloc_scratch_reset();
 
-// Fused quantise + GEMM for decode (gemm_skinny.cu): fp16/bf16 x[M, K] in, out[M, N].
-constexpr int64_t kSkinnyMaxM = 32;
-bool skinny_supported(const void* x, int64_t M, int64_t N, int64_t K);
-int64_t skinny_auto_max_m();
-int skinny_linear(const void* x, bool bf16, const int8_t* w, const float* w_scale, const void* bias, void* out,
-                  int64_t M, int64_t N, int64_t K, cudaStream_t st);
-int skinny_status_read_and_clear(int* code);
 
 // Cluster split-K swap-AB GEMM for decode (gemm_splitk.cu): int8 activations; partial sums
 // of a split K range cross the zero-maintained GEMM workspace and are zeroed again.

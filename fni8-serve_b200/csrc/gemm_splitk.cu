@@ -459,11 +459,6 @@ int splitk_status_read_and_clear(int* code) {
   return FNI8_OK;
 }
 
-static int env_int(const char* name, int dflt) {
-  const char* e = getenv(name);
-  return e ? atoi(e) : dflt;
-}
-
 struct SplitPlan {
   int nt, S, grid, stages, smem;
   size_t ws_bytes;  // partial-sum slabs of the K split (zero-maintained GEMM workspace)
@@ -545,11 +540,11 @@ static int max_clusters(int nt, int smem, int S) {
 // fit in ~half an SM's shared memory (two CTAs per SM, so the next kernel can become
 // resident), at least 3 when the K range is split (2 otherwise), else the whole SM; the
 // drained ring must also hold the staged output tile of the CTA's columns.
-// FNI8_SPLITK_S, FNI8_SPLITK_TARGET_PCT and FNI8_SPLITK_SMEM_KB override (measurement
-// knobs).
+// FNI8_TUNE_SPLITK_S, FNI8_TUNE_SPLITK_TARGET_PCT and FNI8_TUNE_SPLITK_SMEM_KB override
+// the plan in a measurement build.
 static bool plan_ring(int nt, int S, SplitPlan* p) {
   const int stage = splitk::BNW * splitk::BK + nt * splitk::BK;
-  static const int forced_kb = env_int("FNI8_SPLITK_SMEM_KB", 0);
+  constexpr int forced_kb = FNI8_TUNE_SPLITK_SMEM_KB;
   const int sh = S > 1 ? splitk::split_share(nt, S) : nt;
   const int out_tile = ((sh * splitk::BNW * 2 + 15) & ~15) + (S - 1) * sh * splitk::BNW * 4;
   const int fixed = 1024 + splitk::kBarBytes + splitk::kAsBytes;
@@ -576,8 +571,8 @@ static bool plan_splitk(int64_t M, int64_t N, int64_t K, SplitPlan* p) {
   const int n_tiles = (int)((N + splitk::BNW - 1) / splitk::BNW);
   const int kb = (int)((K + splitk::BK - 1) / splitk::BK);
   const int sms = num_sms(current_device());
-  static const int forced_s = env_int("FNI8_SPLITK_S", 0);
-  static const int target_pct = env_int("FNI8_SPLITK_TARGET_PCT", 100);
+  constexpr int forced_s = FNI8_TUNE_SPLITK_S;
+  constexpr int target_pct = FNI8_TUNE_SPLITK_TARGET_PCT;
   int S = forced_s;
   if (S < 1 || S > 8) {
     const int target = sms * target_pct / 100;
@@ -596,8 +591,7 @@ static bool plan_splitk(int64_t M, int64_t N, int64_t K, SplitPlan* p) {
   p->S = S;
   p->grid = n_tiles * S;
   p->ws_bytes = S > 1 ? static_cast<size_t>(p->grid) * nt * splitk::BNW * 4 : 0;
-  static const int log_plan = env_int("FNI8_PLAN_LOG", 0);
-  if (log_plan)
+  if (FNI8_TUNE_PLAN_LOG)
     fprintf(stderr, "fni8 split-K plan M=%lld N=%lld K=%lld: NT=%d S=%d grid=%d stages=%d smem=%d resident clusters=%d\n",
             (long long)M, (long long)N, (long long)K, nt, S, p->grid, p->stages, p->smem, max_clusters(nt, p->smem, S));
   return true;
@@ -663,11 +657,11 @@ int splitk_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const fl
   if (int s = encode_tmap_2d_i8(&tx, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, 128, (uint32_t)p.nt)) return s;
   const int vec = out_mode != splitk::kOutI32 && residual == nullptr && N % 8 == 0 &&
                   (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
-  // FNI8_SPLITK_L2AHEAD overrides the L2 prefetch depth (measurement knob)
-  static const int l2ahead = env_int("FNI8_SPLITK_L2AHEAD", splitk::kL2Ahead);
-  // FNI8_SPLITK_TRIGGER: when the next kernel is released (0 entry, 1 after the last load,
-  // 2 after the partial sums are published: the default, fastest in measured decode chains)
-  static const int trigger = env_int("FNI8_SPLITK_TRIGGER", 2);
+  // L2 prefetch depth (FNI8_TUNE_SPLITK_L2AHEAD, none) and when the next kernel is released
+  // (FNI8_TUNE_SPLITK_TRIGGER: 0 entry, 1 after the last load, 2 after the partial sums are
+  // published: the default, fastest in measured decode chains)
+  constexpr int l2ahead = FNI8_TUNE_SPLITK_L2AHEAD > splitk::kL2Ahead ? FNI8_TUNE_SPLITK_L2AHEAD : splitk::kL2Ahead;
+  constexpr int trigger = FNI8_TUNE_SPLITK_TRIGGER;
   splitk::Epi epi{a_scale, w_scale, bias, residual, out, out_mode, vec, l2ahead < 0 ? 0 : l2ahead, trigger};
   uint4* w4 = static_cast<uint4*>(ws);
   switch (p.nt) {

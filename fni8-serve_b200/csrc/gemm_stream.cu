@@ -432,13 +432,7 @@ static int launch_stream_cfg(const CUtensorMap& tw, const CUtensorMap& tx, const
   return FNI8_OK;
 }
 
-static int stream_budget_kb() {
-  static int kb = [] {
-    const char* e = getenv("FNI8_STREAM_SMEM_KB");
-    return (e != nullptr && atoi(e) == 200) ? 200 : 100;
-  }();
-  return kb;
-}
+static int stream_budget_kb() { return FNI8_TUNE_STREAM_SMEM_KB == 200 ? 200 : 100; }
 
 template <int NT>
 static int launch_stream(const CUtensorMap& tw, const CUtensorMap& tx, const strm::Epi& epi, int M, int N, int K,

@@ -771,41 +771,16 @@ int tile_status_read_and_clear(int* code) {
 
 // Measured on B200: CTA pairs raise the dense prefill GEMMs by 4-10 %, while the grouped
 // expert GEMM, whose experts mostly hold fewer than 256 rows, loses ~10 % (a pair spends
-// two SMs on a short segment). FNI8_TILE_PAIR / FNI8_GROUPED_PAIR override for measurements.
-bool tile_pair_enabled() {
-  static const bool on = [] {
-    const char* e = getenv("FNI8_TILE_PAIR");
-    return e == nullptr || atoi(e) != 0;
-  }();
-  return on;
-}
+// two SMs on a short segment). FNI8_TUNE_TILE_PAIR / FNI8_TUNE_GROUPED_PAIR.
+bool tile_pair_enabled() { return FNI8_TUNE_TILE_PAIR != 0; }
 
-bool grouped_pair_enabled() {
-  static const bool on = [] {
-    const char* e = getenv("FNI8_GROUPED_PAIR");
-    return e != nullptr && atoi(e) != 0;
-  }();
-  return on;
-}
+bool grouped_pair_enabled() { return FNI8_TUNE_GROUPED_PAIR != 0; }
 
-// L2 prefetch depth and the point where the next kernel is released (measurement knobs
-// FNI8_TILE_L2AHEAD and FNI8_TILE_TRIGGER).
-static int tile_l2ahead() {
-  static const int v = [] {
-    const char* e = getenv("FNI8_TILE_L2AHEAD");
-    const int x = e ? atoi(e) : tile::kL2AheadUnits;
-    return x < 0 ? 0 : x;
-  }();
-  return v;
-}
+// L2 prefetch depth and the point where the next kernel is released (FNI8_TUNE_TILE_L2AHEAD
+// and FNI8_TUNE_TILE_TRIGGER).
+static int tile_l2ahead() { return FNI8_TUNE_TILE_L2AHEAD < 0 ? 0 : FNI8_TUNE_TILE_L2AHEAD; }
 
-static int tile_trigger() {
-  static const int v = [] {
-    const char* e = getenv("FNI8_TILE_TRIGGER");
-    return e ? atoi(e) : 1;
-  }();
-  return v;
-}
+static int tile_trigger() { return FNI8_TUNE_TILE_TRIGGER; }
 
 // Tensor map for the TMA-store epilogue: 16-bit outputs whose rows are 16-byte aligned.
 // Returns false (per-thread stores) otherwise; no error is raised for that.

@@ -68,7 +68,7 @@ enum fni8_gemm_path {
   FNI8_PATH_AUTO = 0,   /* by shape, from B200 measurements */
   FNI8_PATH_TILE = 1,   /* tcgen05 tile kernel, 128-row activation tiles */
   FNI8_PATH_STREAM = 2, /* swap-AB stream-K kernel for M <= 256 (uses the workspace) */
-  FNI8_PATH_FUSED = 3,  /* linear only: quantisation fused into a cluster split-K kernel, M <= 32 */
+  FNI8_PATH_FUSED = 3,  /* reserved: not built (returns FNI8_ERR_UNSUPPORTED) */
   FNI8_PATH_SPLITK = 4  /* swap-AB cluster split-K kernel for M <= 256 (uses the workspace) */
 };
 
@@ -202,8 +202,7 @@ FNI8_API int fni8_gemm_w8a8_i32(const int8_t* a, const int8_t* w, int32_t* acc, 
 FNI8_API int fni8_linear_w8a8(const void* x, int dtype, const int8_t* w, const float* w_scale, const void* bias,
                               void* out, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
                               void* workspace, size_t workspace_bytes, void* stream);
-/* Same with an explicit kernel choice (enum fni8_gemm_path). FNI8_PATH_FUSED runs one
- * kernel that quantises x itself and needs neither scratch nor workspace. */
+/* Same with an explicit kernel choice (enum fni8_gemm_path). */
 FNI8_API int fni8_linear_w8a8_ex(const void* x, int dtype, const int8_t* w, const float* w_scale, const void* bias,
                                  void* out, int64_t M, int64_t N, int64_t K, int8_t* q_scratch, float* s_scratch,
                                  int path, void* workspace, size_t workspace_bytes, void* stream);

@@ -404,22 +404,24 @@ def test_zero_rows_and_errors():
 @pytest.mark.parametrize("M,N,K", [(1, 4096, 4096), (3, 6144, 4096), (16, 4096, 12288), (17, 24576, 4096),
                                    (32, 1000, 2048), (5, 128, 16), (8, 640, 4112), (2, 300, 1024)])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_fused_decode_linear_bit_exact(M, N, K, dtype):
-    """fni8.linear at decode sizes runs one fused kernel (per-token quantisation inside
-    the GEMM, split-K over a thread-block cluster reduced through DSMEM). It must equal
-    the oracle and the unfused quantiser + GEMM path bit for bit, with and without bias."""
+def test_decode_linear_bit_exact(M, N, K, dtype):
+    """fni8.linear at decode sizes (per-token quantiser, then the split-K GEMM) equals the
+    oracle bit for bit, with and without bias, and equals linear_q on the same int8 rows.
+    FNI8_PATH_FUSED is reserved and refused."""
     import fni8
+    from fni8 import Fni8Error
+    from fni8 import _native as nat
 
     x = act_input(M, K, 7 * M + N, dtype)
     wq, ws = weight(N, K, K + 1)
     qt = fni8.QTensor(wq.to(DEV), ws.to(DEV))
     bias = (0.1 * torch.randn(N, generator=gen(9))).to(dtype)
-    from fni8 import _native as nat
-
     for b in (None, bias):
-        got = fni8.linear(x.to(DEV), qt, bias=None if b is None else b.to(DEV), path=nat.PATH_FUSED).cpu()
+        got = fni8.linear(x.to(DEV), qt, bias=None if b is None else b.to(DEV)).cpu()
         assert torch.equal(got, O.linear_w8a8(x, wq, ws, bias=b, exact=False))
         q, s = fni8.quantize_rows(x.to(DEV))
-        unfused = fni8.linear_q(q, s, qt, bias=None if b is None else b.to(DEV), out_dtype=dtype).cpu()
-        assert torch.equal(got, unfused)
+        viaq = fni8.linear_q(q, s, qt, bias=None if b is None else b.to(DEV), out_dtype=dtype).cpu()
+        assert torch.equal(got, viaq)
+    with pytest.raises(Fni8Error, match="not built"):
+        fni8.linear(x.to(DEV), qt, path=nat.PATH_FUSED)
     assert fni8.device_status() == 0

@@ -268,19 +268,33 @@ def time_graph(fn, steps, warmup, world, flush=None):
 
 
 def per_launch_ms(fn, reps=20):
-    """Average device time of one fn() launch sequence, events on the launching stream."""
-    for _ in range(3):
-        fn()
+    """Average device time of one fn() launch sequence: `reps` back-to-back calls captured
+    in one CUDA graph, timed with CUDA events around its replays (the best of three), so
+    no host launch gap falls between the calls. The launches keep their L2 state between
+    calls (the kernel's own weights dominate its traffic at the shapes timed here)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
-    ev = []
-    for _ in range(reps):
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(3):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        fn()
+        graph.replay()
         b.record()
-        ev.append((a, b))
-    torch.cuda.synchronize()
-    return sum(a.elapsed_time(b) for a, b in ev) / reps
+        torch.cuda.synchronize()
+        best = min(best, a.elapsed_time(b) / reps)
+    del graph
+    return best
 
 
 def time_eager(fn, steps, warmup, world, flush=None):
@@ -658,27 +672,28 @@ def run_config3(args, world, rank, dev):
                 ms = time_eager(step, args.steps, args.warmup, world) / args.steps
         timing = ("CUDA graph replay (peer-memory exchange over NVLink)" if ep.transport == "p2p" else
                   "eager (all_to_all split sizes visit the host), CUDA events")
-    # grouped-GEMM share: the two grouped launches alone, on the routed inputs
+    # grouped-GEMM share: the two grouped launches of the single-GPU step alone (gate_up with
+    # SiLU*up in its epilogue, then down), on the routed inputs
     topi, topw = moe.route(logits, k)
-    from fni8.moe import grouped_gemm, plan
-    from fni8.ops import act_and_mul_quant, quantize_rows
+    from fni8.moe import grouped_gemm, grouped_gemm_act, plan, quantize_scatter
+    from fni8.ops import quantize_rows
 
-    xq, xs = quantize_rows(x)
     counts, offsets, ros, sor = plan(topi, E)
-    from fni8.parallel import gather_rows
-
     n = int(offsets[-1].item())
-    aq, as_ = gather_rows(xq, xs, sor, n, k)
+    aq, as_ = quantize_scatter(x, ros, k, n)
     iota = torch.arange(E, dtype=torch.int32, device=dev)
     full = moe_experts_on(dev, 0, E) if world > 1 else stack
-    h = grouped_gemm(aq, as_, full.w_gu, full.s_gu, iota, offsets[:E], counts)
-    hq, hs = act_and_mul_quant(h)
-    t_gu = per_launch_ms(lambda: grouped_gemm(aq, as_, full.w_gu, full.s_gu, iota, offsets[:E], counts), reps=10)
+    hq, hs = quantize_rows(grouped_gemm_act(aq, as_, full.w_gu, full.s_gu, iota, offsets[:E], counts))
+    t_gu = per_launch_ms(lambda: grouped_gemm_act(aq, as_, full.w_gu, full.s_gu, iota, offsets[:E], counts), reps=10)
     t_dn = per_launch_ms(lambda: grouped_gemm(hq, hs, full.w_dn, full.s_dn, iota, offsets[:E], counts), reps=10)
     ach = ops / ((t_gu + t_dn) * 1e-3) / 1e12
     ops_gu = 2 * T * k * 2 * I * H
     ach_gu = ops_gu / (t_gu * 1e-3) / 1e12
     wbytes = E * (2 * I * H + H * I)
+    # algorithmic bytes of the gate_up launch: the 128 experts' weights and scales, the routed
+    # int8 rows and scales read, the [rows, I] fp16 product written
+    bytes_gu = E * (2 * I * H + 2 * I * 4) + n * (H + 4) + n * I * 2
+    gbs_gu = bytes_gu / (t_gu * 1e-3) / 1e9
     line = base_line("MoE expert layer tokens/s (E=128 top-8 H=2048 I=768, W8A8 grouped GEMM, expert parallel)",
                      world * T / (ms * 1e-3), "tokens/s", world, args, ms,
                      {"workload": "BASELINE config 3: Qwen3-30B-A3B-shaped MoE layer", "tokens_per_rank": T,
@@ -687,14 +702,25 @@ def run_config3(args, world, rank, dev):
                       "l2": "inputs larger than L2 (604 MB of expert weights)"})
     line["frac_tensor_vs_nominal"] = round(ach / INT8_DENSE_NOMINAL_TOPS, 3)
     line["frac_weights_vs_hbm"] = round(wbytes / ((t_gu + t_dn) * 1e-3) / 1e9 / peaks()["hbm_gbs"], 3)
-    line["roofline"] = {"bound": "tensor", "achieved": round(ach_gu, 1), "peak": INT8_DENSE_NOMINAL_TOPS,
-                        "unit": "TOP/s", "frac": round(ach_gu / INT8_DENSE_NOMINAL_TOPS, 3),
-                        "traffic": committed_traffic("moe_grouped"),
-                        "kernel": "w8a8_tile_kernel<grouped>, gate_up launch (all 128 experts)",
-                        "both_grouped_launches_tops": round(ach, 1),
-                        "weights_gbs": round(wbytes / ((t_gu + t_dn) * 1e-3) / 1e9, 1),
-                        "note": "309 GOP vs 604 MB of weights: tensor (69 us) and HBM (92 us) bounds are close; "
-                                "L2-to-SM traffic 3.5x DRAM (ncu)"}
+    # Both bounds are close for this layer (309 GOP vs 604 MB of weights); the roofline object
+    # carries the larger of the gate_up launch's two fractions, the other beside it.
+    hbm = peaks()["hbm_gbs"]
+    frac_t, frac_h = ach_gu / INT8_DENSE_NOMINAL_TOPS, gbs_gu / hbm
+    common = {"traffic": committed_traffic("moe_grouped_act"),
+              "kernel": "w8a8_tile_kernel<256,1,0,ACTMUL>: grouped gate_up of all 128 experts with SiLU*up in "
+                        "its epilogue (one launch, device time from a CUDA graph of 10 launches)",
+              "algorithmic_bytes_per_launch": bytes_gu, "gate_up_us": round(t_gu * 1e3, 1),
+              "down_us": round(t_dn * 1e3, 1), "both_grouped_launches_tops": round(ach, 1),
+              "weights_gbs": round(wbytes / ((t_gu + t_dn) * 1e-3) / 1e9, 1)}
+    if frac_h >= frac_t:
+        line["roofline"] = {"bound": "hbm", "achieved": round(gbs_gu, 1), "peak": hbm, "unit": "GB/s",
+                            "frac": round(frac_h, 3), "tensor_tops": round(ach_gu, 1),
+                            "tensor_frac_vs_nominal": round(frac_t, 3), **common}
+    else:
+        line["roofline"] = {"bound": "tensor", "achieved": round(ach_gu, 1), "peak": INT8_DENSE_NOMINAL_TOPS,
+                            "unit": "TOP/s", "frac": round(frac_t, 3), "hbm_gbs": round(gbs_gu, 1),
+                            "hbm_frac": round(frac_h, 3), **common}
+    line["roofline"]["peak_source"] = "hbm: MEASURED_PEAKS.json hbm_gbs; int8: nominal dense 4500 TOP/s"
     # end to end: H2D of the step's tokens and router logits (one pinned buffer), routing +
     # experts (a CUDA graph per input slot on one GPU; eager under expert parallelism, whose
     # all_to_all split sizes visit the host), D2H of the layer output; three streams
@@ -723,7 +749,10 @@ def run_config3(args, world, rank, dev):
                            f"({ep.transport})") + (" captured in a CUDA graph per input slot" if graphed else
                                                    " (eager)") +
                           "; pinned host buffers; H2D, layer and D2H on three streams, steps pipelined"}
-    line["gpu_launches"] = 12 * args.steps
+    # route, plan (3), quantise-scatter, gate_up+SiLU, quantise, down, combine; under expert
+    # parallelism: route, quantise, plan (3), dispatch, gate_up+SiLU, quantise, down, return,
+    # combine
+    line["gpu_launches"] = (9 if world == 1 else 11) * args.steps
     line["clocks"] = clk.summary()
     return line, None
 

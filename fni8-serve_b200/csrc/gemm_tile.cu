@@ -252,6 +252,27 @@ __device__ __forceinline__ void dequant_chunk(int mode, const uint32_t (&r)[32],
   }
 }
 
+// One warp's 32 x 32 chunk of 16-bit outputs (lane = row of the slab, o = its four
+// 16-byte pieces) to rows [row_base, row_base + 32), columns [n0, n0 + 32) of the output
+// through one TMA store: staged in the warp's 2 KB buffer with the 64-byte swizzle of the
+// store map (16-byte piece index ^= (row >> 1) & 3), reused only after the previous store
+// from it has read it. (Measured on B200: copying the staged chunk out with coalesced
+// 16-byte stores instead was slower.)
+__device__ __forceinline__ void store_slab(uint8_t* buf, const uint4 (&o)[4], int lane, const CUtensorMap* tmOut,
+                                           int n0, int row_base) {
+  if (lane == 0) bulk_wait_group_read<0>();
+  __syncwarp();
+#pragma unroll
+  for (int j8 = 0; j8 < 4; ++j8)
+    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = o[j8];
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmOut, buf, n0, row_base);
+    bulk_commit_group();
+  }
+}
+
 __device__ __forceinline__ void act_chunk_any(int mode, int act, const uint32_t (&rg)[32], const uint32_t (&ru)[32],
                                               float a_s, const float* sg, const float* su, uint4 (&o)[4]) {
   if (mode == kOutF16) {
@@ -621,18 +642,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld32(tbase + static_cast<uint32_t>(128 + c + 32), ru);
           }
           if (slab_tma) {
-            uint8_t* buf = stg + ew * C::STG_BUF;
-            if (lane == 0) bulk_wait_group_read<0>();
-            __syncwarp();
-#pragma unroll
-            for (int j8 = 0; j8 < 4; ++j8)
-              *reinterpret_cast<uint4*>(buf + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = o[j8];
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_2d(&tmOut, buf, n0, row0 + q * 32);
-              bulk_commit_group();
-            }
+            store_slab(stg + ew * C::STG_BUF, o, lane, &tmOut, n0, row0 + q * 32);
           } else if (valid) {  // rows 16-byte aligned (checked on the host)
 #pragma unroll
             for (int j8 = 0; j8 < 4; ++j8) *reinterpret_cast<uint4*>(orow + (n0 + 8 * j8) * 2) = o[j8];
@@ -659,18 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint4 o[4];
             dequant_chunk(epi.mode, r, a_s, s_ws + c, s_bias + c, epi.bias != nullptr, o);
             if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
-            uint8_t* buf = stg + ew * C::STG_BUF;
-            if (lane == 0) bulk_wait_group_read<0>();  // the previous store from this buffer has read it
-            __syncwarp();
-#pragma unroll
-            for (int j8 = 0; j8 < 4; ++j8)  // 64-byte swizzle of the store map: chunk ^= (row >> 1) & 3
-              *reinterpret_cast<uint4*>(buf + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = o[j8];
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_2d(&tmOut, buf, n0, row0 + q * 32);
-              bulk_commit_group();
-            }
+            store_slab(stg + ew * C::STG_BUF, o, lane, &tmOut, n0, row0 + q * 32);
           } else {
             if (n0 < N && valid) {
               if (epi.mode == kOutI32) store_chunk_i32(epi, r, row, n0, N, vec_ok != 0);

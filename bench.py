@@ -767,7 +767,8 @@ def run_config4(args, world, rank, dev):
     shard = shard_rows(full, world, rank)
     del full
     xs = [act(M, K, 10 + M, dev) for M in Ms]
-    cp = ColumnParallelLinearW8A8(shard) if world > 1 else None
+    # p2p: each rank's GEMM stores its columns into every rank's output over NVLink
+    cp = ColumnParallelLinearW8A8(shard, max_rows=max(Ms)) if world > 1 else None
     import fni8
 
     def step():
@@ -776,15 +777,27 @@ def run_config4(args, world, rank, dev):
 
     ops = sum(2 * M * N * K for M in Ms)
     with ClockSampler(dev) as clk:
-        if world == 1:
+        if cp is None or cp.transport == "p2p":  # no host synchronisation in the step
             ms = time_graph(step, args.steps, args.warmup, world) / args.steps
         else:
             ms = time_eager(step, args.steps, args.warmup, world) / args.steps
     per = {}
+    n = N // world
     for M, x in zip(Ms, xs):
         t = per_launch_ms(lambda x=x: fni8.linear(x, shard), reps=10)
-        per[f"M{M}_shard"] = {"us": round(t * 1e3, 1), "TOP/s": round(2 * M * (N // world) * K / (t * 1e-3) / 1e12, 1),
-                              "GB/s": round(((N // world) * K + 2 * M * K + 2 * M * (N // world)) / (t * 1e-3) / 1e9, 1)}
+        per[f"M{M}_shard"] = {"us": round(t * 1e3, 1), "TOP/s": round(2 * M * n * K / (t * 1e-3) / 1e12, 1),
+                              "GB/s": round((n * K + 2 * M * K + 2 * M * n) / (t * 1e-3) / 1e9, 1)}
+        if cp is not None:
+            # the whole column-parallel call: quantise, GEMM with the all-gather stores, the
+            # ordering all_reduce. Bound: the slower of the shard's int8 work at the nominal
+            # peak and the (world-1)/world of the output each rank receives over NVLink at the
+            # measured 770 GB/s per direction.
+            tg = per_launch_ms(lambda x=x: cp(x), reps=10)
+            recv = (world - 1) * M * n * 2
+            bound_us = max(2 * M * n * K / (INT8_DENSE_NOMINAL_TOPS * 1e12), recv / 770e9) * 1e6
+            per[f"M{M}_shard"].update({"gathered_us": round(tg * 1e3, 1),
+                                       "nvlink_recv_GBs": round(recv / (tg * 1e-3) / 1e9, 1),
+                                       "bound_us": round(bound_us, 1), "frac_of_bound": round(bound_us / (tg * 1e3), 3)})
     line = base_line("Column-parallel W8A8 TOP/s (K=8192 N=28672, M=16/512/4096, N sharded, all-gather)",
                      ops / (ms * 1e-3) / 1e12, "TOP/s", world, args, ms,
                      {"workload": "BASELINE config 4: column-parallel dense sweep", "K": K, "N": N, "M": Ms,
@@ -803,24 +816,30 @@ def run_config4(args, world, rank, dev):
     hout = torch.empty(sum(M * N for M in Ms), dtype=torch.float16).pin_memory()
 
     def sweep(xd):
-        outs, off = [], 0
-        for M, n in zip(Ms, sizes):
-            xv = xd[off:off + n].view(M, K)
-            outs.append(cp(xv) if cp is not None else fni8.linear(xv, shard))
-            off += n
-        return torch.cat([o.reshape(-1) for o in outs])
+        res = torch.empty(hout.numel(), dtype=torch.float16, device=dev)
+        off, o2 = 0, 0
+        for M, sz in zip(Ms, sizes):
+            xv = xd[off:off + sz].view(M, K)
+            y = cp(xv) if cp is not None else fni8.linear(xv, shard)  # p2p: a view of the layer's buffer
+            res[o2:o2 + y.numel()].copy_(y.reshape(-1))
+            off, o2 = off + sz, o2 + y.numel()
+        return res
 
     slots = [torch.empty_like(hin, device=dev) for _ in range(2)]
-    fn = graph_per_slot(slots, sweep) if world == 1 else sweep
+    fn = graph_per_slot(slots, sweep) if cp is None or cp.transport == "p2p" else sweep
     e2e_ms = time_pipelined([(hin, slots, fn, hout)], args.steps, args.warmup, world) / args.steps
     del fn
     line["e2e"] = {"value": round(ops / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TOP/s", "h2d_bytes_per_step": hin.numel() * 2,
                    "d2h_bytes_per_step": hout.numel() * 2, "ms_per_step": round(e2e_ms, 4),
                    "api": ("fni8.linear x3 captured in a CUDA graph per input slot" if world == 1 else
-                           "ColumnParallelLinearW8A8 (eager, NCCL all-gather)") +
+                           "ColumnParallelLinearW8A8 x3 (GEMM with the all-gather stores over NVLink) captured in "
+                           "a CUDA graph per input slot") +
                           "; pinned host buffers; H2D, linears and D2H on three streams, steps pipelined"}
-    line["gpu_launches"] = 6 * args.steps
+    # per linear a quantiser and a GEMM; under p2p the decode-size (M=16) GEMM adds the copy out
+    line["gpu_launches"] = (7 if cp is not None else 6) * args.steps
     line["clocks"] = clk.summary()
+    if cp is not None:
+        cp.close()
     return line, None
 
 
@@ -935,8 +954,15 @@ def reference_arm(args, world, rank, config=None):
             "e2e": {"value": round(v, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-SUB_BLOCKS = {"decode": 1, "prefill": 2}
+# keyed sub-blocks of the default line: every dense config at N=1; at N>1 the column-parallel
+# sweep (config 4), the one dense config whose work is sharded over the ranks
+SUB_BLOCKS = {"decode": 1, "prefill": 2, "linear": 0, "sweep": 4}
+SUB_BLOCKS_MULTI = {"sweep": 4}
 _RUN_KEYS = ("n_gpus", "steps", "warmup", "vs_baseline", "data", "impl")
+
+
+def _sub_blocks(world):
+    return SUB_BLOCKS if world == 1 else SUB_BLOCKS_MULTI
 
 
 def _sub_block(line):
@@ -946,35 +972,34 @@ def _sub_block(line):
 
 def headline(args, world, rank, dev):
     """The default line: the MoE layer (config 3, expert-parallel at N>1) at the top level;
-    at N=1 the decode (config 1) and prefill (config 2) lines as keyed sub-blocks."""
+    the dense configs as keyed sub-blocks (all of them at N=1, the column-parallel sweep at
+    N>1)."""
+    runners = {0: run_config0, 1: run_config1, 2: run_config2, 4: run_config4}
     line, _ = run_config3(args, world, rank, dev)
-    line["config"]["sub_blocks"] = (
-        {k: f"BASELINE config {c}" for k, c in SUB_BLOCKS.items()} if world == 1 else
-        "none at N>1 (the dense configs run replicas only; BENCH at N=1 carries them)")
-    if world == 1:
-        if rank == 0 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_sample(3)
+    blocks = _sub_blocks(world)
+    line["config"]["sub_blocks"] = {k: f"BASELINE config {c}" for k, c in blocks.items()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample(3)
+    torch.cuda.empty_cache()
+    for key, c in blocks.items():
+        sub, keep = runners[c](args, world, rank, dev)
+        del keep
         torch.cuda.empty_cache()
-        for key, c in SUB_BLOCKS.items():
-            sub, keep = (run_config1 if c == 1 else run_config2)(args, world, rank, dev)
-            del keep
-            torch.cuda.empty_cache()
-            if not args.no_cpu_baseline:
-                sub["cpu_baseline"] = cpu_baseline_sample(c)
-            line[key] = _sub_block(sub)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            sub["cpu_baseline"] = cpu_baseline_sample(c)
+        line[key] = _sub_block(sub)
     return line
 
 
 def reference_headline(args, world, rank):
-    """The reference arm of the default line: the same three workloads on the host cores."""
+    """The reference arm of the default line: the same workloads on the host cores."""
     line = reference_arm(args, world, rank, config=3)
     if line is None:
         return None
-    line["config"]["sub_blocks"] = ({k: f"BASELINE config {c}" for k, c in SUB_BLOCKS.items()} if world == 1
-                                    else "none at N>1")
-    if world == 1:
-        for key, c in SUB_BLOCKS.items():
-            line[key] = _sub_block(reference_arm(args, world, rank, config=c))
+    blocks = _sub_blocks(world)
+    line["config"]["sub_blocks"] = {k: f"BASELINE config {c}" for k, c in blocks.items()}
+    for key, c in blocks.items():
+        line[key] = _sub_block(reference_arm(args, world, rank, config=c))
     return line
 
 

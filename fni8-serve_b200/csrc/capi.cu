@@ -294,6 +294,44 @@ extern "C" int fni8_gemm_w8a8_act(const int8_t* a, const float* a_scale, const i
                        out_dtype == FNI8_F16 ? 0 : 1, tile_pair_enabled() && M >= 256, static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int fni8_gemm_w8a8_peer_cols(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                                        const void* bias, int out_dtype, int64_t M, int64_t N, int64_t K,
+                                        void* const* peer_out, int n_peers, int64_t ld, int64_t col_off, void* tmp,
+                                        size_t tmp_bytes, void* ws, size_t ws_bytes, void* stream) {
+  if (int s = check_gemm(a, w, peer_out, M, N, K)) return s;
+  if (out_dtype != FNI8_F16 && out_dtype != FNI8_BF16)
+    return fail(FNI8_ERR_INVALID, "out_dtype %d: expected F16 or BF16", out_dtype);
+  if (n_peers < 1 || n_peers > 8) return fail(FNI8_ERR_INVALID, "peer_cols: 1 to 8 destination buffers (got %d)", n_peers);
+  if (N % 32 != 0) return fail(FNI8_ERR_UNSUPPORTED, "peer_cols: N=%lld must be a multiple of 32", (long long)N);
+  if (col_off < 0 || ld < col_off + N) return fail(FNI8_ERR_INVALID, "peer_cols: columns [%lld, %lld) exceed ld=%lld",
+                                                   (long long)col_off, (long long)(col_off + N), (long long)ld);
+  if (ld % 8 != 0 || col_off % 8 != 0 || ld >= (1LL << 31))
+    return fail(FNI8_ERR_ALIGN, "peer_cols: ld and col_off must be multiples of 8 (16 bytes)");
+  if (M > 0 && (a_scale == nullptr || w_scale == nullptr)) return fail(FNI8_ERR_INVALID, "null scale");
+  if (M == 0) return FNI8_OK;
+  for (int i = 0; i < n_peers; ++i) {
+    if (peer_out[i] == nullptr) return fail(FNI8_ERR_INVALID, "peer_cols: null destination %d", i);
+    if (reinterpret_cast<uintptr_t>(peer_out[i]) & 15u)
+      return fail(FNI8_ERR_ALIGN, "peer_cols: destination %d must be 16-byte aligned", i);
+  }
+  if ((reinterpret_cast<uintptr_t>(w_scale) & 15u) || (bias != nullptr && (reinterpret_cast<uintptr_t>(bias) & 15u)))
+    return fail(FNI8_ERR_ALIGN, "peer_cols: w_scale and bias must be 16-byte aligned");
+  const int mode = out_dtype == FNI8_F16 ? 0 : 1;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int p = pick_path(FNI8_PATH_AUTO, M, ws_bytes, N, K);
+  if (p == FNI8_PATH_TILE) {
+    const bool pair = tile_pair_enabled() && M >= 256;
+    return tile_gemm_peer_cols(a, a_scale, w, w_scale, bias, mode, M, N, K, peer_out, n_peers, ld, col_off,
+                               pair ? 256 : pick_bn(M, N), pair, st);
+  }
+  // decode sizes: the split-K (or stream-K) GEMM into tmp, then the copy to every buffer
+  if (tmp == nullptr || tmp_bytes < (size_t)(M * N * 2))
+    return fail(FNI8_ERR_WORKSPACE, "peer_cols: tmp needs %lld bytes", (long long)(M * N * 2));
+  if (reinterpret_cast<uintptr_t>(tmp) & 15u) return fail(FNI8_ERR_ALIGN, "peer_cols: tmp must be 16-byte aligned");
+  if (int s = gemm_any(a, a_scale, w, w_scale, bias, nullptr, tmp, mode, M, N, K, p, ws, ws_bytes, st)) return s;
+  return push_cols(tmp, M, N, peer_out, n_peers, ld, col_off, st);
+}
+
 extern "C" int fni8_gemm_w8a8_i32(const int8_t* a, const int8_t* w, int32_t* acc, int64_t M, int64_t N, int64_t K,
                                   int path, void* workspace, size_t workspace_bytes, void* stream) {
   if (int s = check_gemm(a, w, acc, M, N, K)) return s;

@@ -103,6 +103,23 @@ __global__ void return_kernel(const T* __restrict__ y, const int32_t* __restrict
   __threadfence_system();
 }
 
+// Column all-gather step: 16-byte piece i of src [M, N] (16-bit, row stride N) to every
+// destination's row at column col_off (row stride ld). Grid-stride over the M * N / 8 pieces.
+__global__ void push_cols_kernel(const uint4* __restrict__ src, int64_t M, int64_t pieces_per_row, Peers dst, int P,
+                                 int64_t ld, int64_t col_off) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t total = M * pieces_per_row;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = i / pieces_per_row, c = i - m * pieces_per_row;
+    const uint4 v = __ldg(src + i);
+    const int64_t off = (m * ld + col_off + 8 * c) * 2;
+    for (int p = 0; p < P; ++p) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(dst.p[p]) + off) = v;
+  }
+  __threadfence_system();
+}
+
 }  // namespace ep
 }  // namespace fni8b
 
@@ -117,6 +134,20 @@ int ep_status_read_and_clear(int* code) {
   e = cudaMemcpyToSymbol(ep::g_status, &z, sizeof(int));
   if (e != cudaSuccess) return cuda_status(e, "clear expert-exchange status");
   *code = v;
+  return FNI8_OK;
+}
+
+int push_cols(const void* src, int64_t M, int64_t N, void* const* peer_out, int n_peers, int64_t ld, int64_t col_off,
+              cudaStream_t st) {
+  if (M <= 0 || N <= 0) return FNI8_OK;
+  if (n_peers < 1 || n_peers > ep::kMaxPeers) return fail(FNI8_ERR_INVALID, "push_cols: 1 to %d destinations", ep::kMaxPeers);
+  ep::Peers d;
+  for (int i = 0; i < n_peers; ++i) d.p[i] = peer_out[i];
+  const int64_t pieces = M * (N / 8);
+  const int64_t blocks = (pieces + 255) / 256;
+  launch_pdl(ep::push_cols_kernel, dim3((int)(blocks < 148 * 8 ? blocks : 148 * 8)), dim3(256), 0, st,
+             static_cast<const uint4*>(src), M, N / 8, d, n_peers, ld, col_off);
+  FNI8_CHECK_LAUNCH("push_cols");
   return FNI8_OK;
 }
 }  // namespace fni8h

@@ -19,8 +19,15 @@ int tile_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const floa
 int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w, const float* w_scale,
                       int64_t E, int64_t N, int64_t K, const int32_t* seg_expert, const int32_t* seg_off,
                       const int32_t* seg_cnt, int64_t S, void* out, int out_mode, int bn, bool pair,
-                      cudaStream_t st, const int32_t* row_tag = nullptr,
-                      void* const* peer_out = nullptr, int n_peers = 0, int64_t peer_rows = 0);
+                      cudaStream_t st);
+// Dense tile GEMM whose epilogue writes output element (m, n) to element
+// (m, col_off + n) of each of the n_peers (<= 8) buffers peer_out[p] (row stride ld
+// elements; this GPU's memory or an NVLink peer's mapped into this process): a column
+// shard's part of an all-gather. 16-bit out_mode, no residual; the caller validates
+// alignment (buffers, ld and col_off 16-byte multiples, N % 32 == 0).
+int tile_gemm_peer_cols(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
+                        int out_mode, int64_t M, int64_t N, int64_t K, void* const* peer_out, int n_peers, int64_t ld,
+                        int64_t col_off, int bn, bool pair, cudaStream_t st);
 // Tile GEMM over a merged gate_up weight (gate rows [0, I), up rows [I, 2I)) whose
 // epilogue applies act_and_mul: out[M, I] in fp16/bf16 (out_mode 0/1), I % 128 == 0.
 // Dense when seg_expert is null; grouped over S segments of a [E, 2I, K] stack otherwise.
@@ -70,5 +77,10 @@ int w4a8_status_read_and_clear(int* code);
 
 // Expert-parallel exchange kernels (ep_p2p.cu): capacity-overflow status word.
 int ep_status_read_and_clear(int* code);
+// src [M, N] 16-bit rows (row stride N) to columns [col_off, col_off + N) of each of the
+// n_peers buffers peer_out[p] (row stride ld elements): the all-gather step of a column
+// shard whose GEMM wrote a local buffer. Same alignment rules as tile_gemm_peer_cols.
+int push_cols(const void* src, int64_t M, int64_t N, void* const* peer_out, int n_peers, int64_t ld, int64_t col_off,
+              cudaStream_t st);
 
 }  // namespace fni8h

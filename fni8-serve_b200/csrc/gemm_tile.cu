@@ -36,6 +36,7 @@
 #include "gemm_internal.h"
 
 #include <stdlib.h>
+#include <string.h>
 
 namespace fni8b {
 namespace tile {
@@ -54,8 +55,8 @@ constexpr int kL2AheadUnits = 0;
 
 static __device__ int g_status;  // watchdog word of this file
 
-enum : int { kCodeProducer = 0x101, kCodeMma = 0x102, kCodeEpilogue = 0x103, kCodeDrain = 0x104, kCodeScatter = 0x105 };
-constexpr int kMaxScatterPeers = 8;
+enum : int { kCodeProducer = 0x101, kCodeMma = 0x102, kCodeEpilogue = 0x103, kCodeDrain = 0x104 };
+constexpr int kMaxPeers = 8;
 enum : int { kOutF16 = 0, kOutBF16 = 1, kOutI32 = 2 };
 
 struct Epi {
@@ -67,13 +68,13 @@ struct Epi {
   int mode;              // kOutF16 / kOutBF16 / kOutI32
   int l2ahead;           // weight k-blocks pulled into L2 (beyond the ring) before the PDL wait
   int trigger;           // next kernel released at entry (0) or after this CTA's last load (1)
-  // Row scatter (grouped, 16-bit out): output row r goes to row (row_tag[r] & 0xFFFFFF) of
-  // peer_out[row_tag[r] >> 24] ([peer_rows, N] each; a peer's memory mapped into this
-  // process), instead of out[r]. null row_tag: plain rows of `out`.
-  const int32_t* row_tag;
-  void* peer_out[kMaxScatterPeers];
+  // Column all-gather (dense, 16-bit out, n_peers > 0): output element (m, n) goes to
+  // element (m, peer_col + n) of every peer_out[p] ([rows, peer_ld] each; buffers of this
+  // GPU or of its NVLink peers mapped into this process), instead of out.
+  void* peer_out[kMaxPeers];
   int n_peers;
-  int64_t peer_rows;
+  int peer_col;
+  int64_t peer_ld;
   // ACTMUL kernels (gate_up with act_and_mul in the epilogue): the weight holds the gate
   // rows [0, act_i) and the up rows [act_i, 2 act_i); tile n covers gate rows
   // [128 n, 128 n + 128) in accumulator columns 0-127 and the matching up rows in columns
@@ -270,6 +271,30 @@ __device__ __forceinline__ void store_slab(uint8_t* buf, const uint4 (&o)[4], in
   if (lane == 0) {
     tma_store_2d(tmOut, buf, n0, row_base);
     bulk_commit_group();
+  }
+}
+
+// The same chunk to columns [peer_col + n0, peer_col + n0 + 32) of rows
+// [row_base, row_base + nrows) of every peer_out buffer (the column all-gather): staged in
+// the warp's buffer with the same swizzle, then read back so that each store instruction
+// writes 8 rows x 64 contiguous bytes, once per destination (plain stores: the
+// destinations may be other GPUs' memory).
+__device__ __forceinline__ void store_slab_peers(uint8_t* buf, const uint4 (&o)[4], int lane, const Epi& epi, int n0,
+                                                 int row_base, int nrows) {
+  __syncwarp();  // every lane has read the previous chunk out of the buffer
+#pragma unroll
+  for (int j8 = 0; j8 < 4; ++j8)
+    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = o[j8];
+  __syncwarp();
+  const int g = lane & 3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = (lane >> 2) + 8 * i;
+    if (r < nrows) {
+      const uint4 v = *reinterpret_cast<const uint4*>(buf + r * 64 + ((g ^ ((r >> 1) & 3)) << 4));
+      const int64_t off = (static_cast<int64_t>(row_base + r) * epi.peer_ld + epi.peer_col + n0 + 8 * g) * 2;
+      for (int p = 0; p < epi.n_peers; ++p) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(epi.peer_out[p]) + off) = v;
+    }
   }
 }
 
@@ -565,25 +590,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // this CTA's rows of the tile
       const int row0 = tc.row0 + static_cast<int>(half) * BM;
       const int rows_here = tc.rows_valid - static_cast<int>(half) * BM;
-      bool valid = row_local < rows_here;
+      const bool valid = row_local < rows_here;
       const int64_t row = static_cast<int64_t>(row0) + row_local;
-      // this thread's output row: out[row], or a peer's row under the row scatter
+      // this thread's output row (per-thread store path)
       uint8_t* orow = nullptr;
-      if (valid && epi.mode != kOutI32) {
-        if (epi.row_tag != nullptr) {
-          const uint32_t tg = static_cast<uint32_t>(__ldg(epi.row_tag + row));
-          const int src = static_cast<int>(tg >> 24);
-          const int64_t slot = static_cast<int64_t>(tg & 0xFFFFFFu);
-          if (src < epi.n_peers && slot < epi.peer_rows) {
-            orow = static_cast<uint8_t*>(epi.peer_out[src]) + slot * static_cast<int64_t>(N) * 2;
-          } else {
-            atomicExch(&g_status, kCodeScatter);
-            valid = false;
-          }
-        } else {
-          orow = static_cast<uint8_t*>(epi.out) + row * static_cast<int64_t>(ACTMUL ? epi.act_i : N) * 2;
-        }
-      }
+      if (valid && epi.mode != kOutI32 && epi.n_peers == 0)
+        orow = static_cast<uint8_t*>(epi.out) + row * static_cast<int64_t>(ACTMUL ? epi.act_i : N) * 2;
       const int nb0 = tc.n_blk * BN;
       const float* wsc = epi.w_scale + static_cast<int64_t>(tc.expert) * N;
       static_assert(BN <= kEpiThreads, "one column scale per epilogue thread");
@@ -616,9 +628,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       // TMA store of whole 32-row slabs; a slab cut by a segment end (grouped) or any
-      // residual add takes the per-thread path
-      const bool slab_tma = tma_store && epi.residual == nullptr && epi.row_tag == nullptr &&
-                            (!GROUPED || rows_here - q * 32 >= 32) && q * 32 < rows_here;
+      // residual add takes the per-thread path. Column all-gather: every slab with rows.
+      const bool slab_tma = tma_store && epi.residual == nullptr && (!GROUPED || rows_here - q * 32 >= 32) &&
+                            q * 32 < rows_here;
+      const bool slab_peer = !GROUPED && !ACTMUL && epi.n_peers > 0 && q * 32 < rows_here;
       if constexpr (ACTMUL) {
         // this warp's 64 of the tile's 128 product columns: gate accumulators at c, up at
         // 128 + c; outputs at column 128 n + c of the [rows, act_i] product
@@ -670,6 +683,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             dequant_chunk(epi.mode, r, a_s, s_ws + c, s_bias + c, epi.bias != nullptr, o);
             if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
             store_slab(stg + ew * C::STG_BUF, o, lane, &tmOut, n0, row0 + q * 32);
+          } else if (slab_peer && n0 < N) {
+            uint4 o[4];
+            dequant_chunk(epi.mode, r, a_s, s_ws + c, s_bias + c, epi.bias != nullptr, o);
+            if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
+            store_slab_peers(stg + ew * C::STG_BUF, o, lane, epi, n0, row0 + q * 32, min(32, rows_here - q * 32));
           } else {
             if (n0 < N && valid) {
               if (epi.mode == kOutI32) store_chunk_i32(epi, r, row, n0, N, vec_ok != 0);
@@ -698,6 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (acc == 0) aph ^= 1u;
     }
     if (tma_store && lane == 0) bulk_wait_group<0>();  // stores complete before the CTA exits
+    if (epi.n_peers > 0) __threadfence_system();  // peer stores performed before the kernel ends
     __syncwarp();
   }
 
@@ -827,11 +846,41 @@ int tile_gemm(const int8_t* a, const float* a_scale, const int8_t* w, const floa
   return tile::launch<128, false, false>(ta, tb, to, tma_store, epi, grp, (int)M, (int)N, (int)K, grid, vec_ok, st);
 }
 
+int tile_gemm_peer_cols(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
+                        int out_mode, int64_t M, int64_t N, int64_t K, void* const* peer_out, int n_peers, int64_t ld,
+                        int64_t col_off, int bn, bool pair, cudaStream_t st) {
+  if (M <= 0 || N <= 0) return FNI8_OK;
+  if (n_peers < 1 || n_peers > tile::kMaxPeers) return fail(FNI8_ERR_INVALID, "1 to %d destinations", tile::kMaxPeers);
+  CUtensorMap ta, tb, to;
+  if (int s = encode_tmap_2d_i8(&ta, a, (uint64_t)K, (uint64_t)M, (uint64_t)K, 128, 128)) return s;
+  if (int s = encode_tmap_2d_i8(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)K, 128, (uint32_t)(pair ? bn / 2 : bn)))
+    return s;
+  memset(&to, 0, sizeof(to));
+  tile::Epi epi{a_scale, w_scale, bias, nullptr, nullptr, out_mode, tile_l2ahead(), tile_trigger()};
+  epi.n_peers = n_peers;
+  epi.peer_col = (int)col_off;
+  epi.peer_ld = ld;
+  for (int i = 0; i < n_peers; ++i) epi.peer_out[i] = peer_out[i];
+  tile::Groups grp{nullptr, nullptr, nullptr, 0};
+  const int bmt = pair ? 256 : 128;
+  const int64_t tiles = ((M + bmt - 1) / bmt) * ((N + bn - 1) / bn);
+  const int64_t ctas = pair ? 2 * tiles : tiles;
+  const int sms = num_sms(current_device());
+  const int cap = pair ? (sms & ~1) : sms;
+  const int grid = (int)(ctas < cap ? ctas : cap);
+  const int Mi = (int)M, Ni = (int)N, Ki = (int)K;
+  if (pair) {
+    if (bn == 256) return tile::launch<256, false, true>(ta, tb, to, false, epi, grp, Mi, Ni, Ki, grid, true, st);
+    return tile::launch<128, false, true>(ta, tb, to, false, epi, grp, Mi, Ni, Ki, grid, true, st);
+  }
+  if (bn == 256) return tile::launch<256, false, false>(ta, tb, to, false, epi, grp, Mi, Ni, Ki, grid, true, st);
+  return tile::launch<128, false, false>(ta, tb, to, false, epi, grp, Mi, Ni, Ki, grid, true, st);
+}
+
 int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w, const float* w_scale,
                       int64_t E, int64_t N, int64_t K, const int32_t* seg_expert, const int32_t* seg_off,
                       const int32_t* seg_cnt, int64_t S, void* out, int out_mode, int bn, bool pair,
-                      cudaStream_t st, const int32_t* row_tag, void* const* peer_out, int n_peers,
-                      int64_t peer_rows) {
+                      cudaStream_t st) {
   if (R <= 0 || N <= 0 || S <= 0) return FNI8_OK;
   if (S > tile::kMaxSeg) return fail(FNI8_ERR_UNSUPPORTED, "at most %d segments (got %lld)", tile::kMaxSeg, (long long)S);
   CUtensorMap ta, tb;
@@ -844,20 +893,11 @@ int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const in
   const int sms = num_sms(current_device());
   const int grid = pair ? (sms & ~1) : sms;
   const size_t esz = out_mode == tile::kOutI32 ? 4 : 2;
-  bool aligned = ((uintptr_t)out & 15u) == 0;
-  if (row_tag != nullptr) {  // rows scattered into peers' buffers (validated by the caller)
-    epi.row_tag = row_tag;
-    epi.n_peers = n_peers;
-    epi.peer_rows = peer_rows;
-    for (int i = 0; i < n_peers; ++i) {
-      epi.peer_out[i] = peer_out[i];
-      aligned = aligned && ((uintptr_t)peer_out[i] & 15u) == 0;
-    }
-  }
+  const bool aligned = ((uintptr_t)out & 15u) == 0;
   const bool vec_ok = ((N * (int64_t)esz) % 16 == 0) && aligned && (((uintptr_t)w_scale & 15u) == 0) &&
                       ((N % 4) == 0);
   CUtensorMap to;
-  const bool tma_store = row_tag == nullptr && out_tma_map(&to, out, out_mode, R, N);
+  const bool tma_store = out_tma_map(&to, out, out_mode, R, N);
   if (pair) {
     if (bn == 256)
       return tile::launch<256, true, true>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);

@@ -49,6 +49,8 @@ SIGNATURES: dict[str, tuple] = {
     "fni8_gemm_w8a8_i32": (_i, [_p, _p, _p, _i64, _i64, _i64, _i, _p, _sz, _p]),
     "fni8_gemm_w8a8_act": (_i, [_p, _p, _p, _p, _i, _p, _i, _i64, _i64, _i64, _p]),
     "fni8_grouped_gemm_w8a8_act": (_i, [_p, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _i, _p, _i, _p]),
+    "fni8_gemm_w8a8_peer_cols": (_i, [_p, _p, _p, _p, _p, _i, _i64, _i64, _i64, _p, _i, _i64, _i64, _p, _sz, _p, _sz,
+                                      _p]),
     "fni8_gemm_w8a8_noalloc": (_i, [_p, _p, _p, _p, _p, _p, _p, _i, _i64, _i64, _i64, _p]),
     "fni8_linear_w8a8": (_i, [_p, _i, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p, _sz, _p]),
     "fni8_linear_w8a8_ex": (_i, [_p, _i, _p, _p, _p, _p, _i64, _i64, _i64, _p, _p, _i, _p, _sz, _p]),
@@ -58,8 +60,6 @@ SIGNATURES: dict[str, tuple] = {
     "fni8_moe_gather_rows_i8": (_i, [_p, _p, _p, _i64, _i64, _i64, _p, _p, _p]),
     "fni8_moe_quantize_scatter_i8": (_i, [_p, _i, _i64, _i64, _p, _i64, _p, _p, _p]),
     "fni8_grouped_gemm_w8a8": (_i, [_p, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _i, _p]),
-    "fni8_grouped_gemm_w8a8_scatter": (_i, [_p, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p, _i64,
-                                            _i64, _i, _p]),
     "fni8_moe_combine": (_i, [_p, _i, _p, _p, _i64, _i64, _i64, _p, _p]),
     "fni8_moe_experts_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "fni8_moe_experts_w8a8": (_i, [_p, _i, _i64, _i64, _p, _p, _i64, _p, _p, _p, _p, _i64, _i64, _i, _p, _p, _sz,

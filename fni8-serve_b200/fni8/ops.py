@@ -309,6 +309,31 @@ def linear_act_q(q: torch.Tensor, scale: torch.Tensor, gate_up: QTensor, act: st
     return out.reshape(*q.shape[:-1], I)
 
 
+def linear_q_peer_cols(q: torch.Tensor, scale: torch.Tensor, shard: QTensor, peers, n_peers: int, ld: int,
+                       col_off: int, bias: torch.Tensor | None = None, out_dtype: torch.dtype = torch.float16) -> None:
+    """W8A8 GEMM of a column shard on pre-quantised rows q[M, K] whose output element (m, n)
+    is stored to element (m, col_off + n) of each of the n_peers buffers in `peers` (a ctypes
+    array of device pointers; row stride ld elements; this GPU's own or NVLink peers' memory):
+    the shard's part of a column all-gather, computed and sent in one call
+    (C: fni8_gemm_w8a8_peer_cols). Nothing is returned."""
+    _need_cuda(q, "linear_q_peer_cols")
+    K = q.shape[-1]
+    _check_weight(shard, q.device, K, "linear_q_peer_cols")
+    w, Kp = _k16_weight(shard, K)
+    q2 = q.reshape(-1, K).contiguous()
+    if Kp != K:
+        q2 = torch.nn.functional.pad(q2, (0, Kp - K))
+    s2 = scale.reshape(-1).to(torch.float32).contiguous()
+    M, N = q2.shape[0], shard.data.shape[0]
+    b = bias.to(out_dtype).contiguous() if bias is not None else None
+    # decode sizes run the split-K GEMM into a local [M, N] buffer before the copy out
+    tmp = torch.empty((M, N), dtype=out_dtype, device=q.device) if M <= 256 else None
+    ws, wsb = _ws(q.device)
+    nat.call("fni8_gemm_w8a8_peer_cols", _vp(q2), _vp(s2), _vp(w), _vp(shard.scale), _vp(b), _DT[out_dtype], M, N, Kp,
+             peers, n_peers, ld, col_off, _vp(tmp), tmp.numel() * 2 if tmp is not None else 0, ws, wsb,
+             _stream(q.device))
+
+
 def _linear_w4a8(x: torch.Tensor, qt: QTensor, bias: torch.Tensor | None) -> torch.Tensor:
     """per_group_i4 / int4 weights (W4A8): packed data [N, K/2] uint8, scale [N, K/g] fp32."""
     if qt.codebook not in (None, "int4"):

@@ -19,10 +19,15 @@ Expert parallel (rank r owns experts [r*E/P, (r+1)*E/P)), two transports:
     sizes visit the host (one small copy per layer).
 Activations cross NVLink as int8 (half the bytes of fp16).
 
-Column parallel: rank r holds rows [r*N/P, (r+1)*N/P) of W and its scales, computes
-y[:, slice] with the local GEMM and all_gathers the slices. Large batches go in row chunks
-whose all_gathers run asynchronously, so chunk c's exchange over NVLink overlaps the GEMM
-of chunk c+1; rows are independent, so the result is the same bit for bit.
+Column parallel: rank r holds rows [r*N/P, (r+1)*N/P) of W and its scales and computes
+y[:, slice]; every rank needs all of y. Two transports:
+  p2p (CUDA, one node): the GEMM stores its slice straight into every rank's output buffer
+    (CUDA IPC peer memory over NVLink): at prefill sizes from the tile GEMM's epilogue, so
+    each tile crosses NVLink while later tiles compute; at decode sizes by a copy kernel
+    after the split-K GEMM. One NCCL all_reduce of one element then orders the ranks.
+  nccl (any backend): the local GEMM and all_gather_into_tensor, in row chunks whose
+    exchanges run asynchronously.
+Rows and columns are independent, so every form gives the single-GPU result bit for bit.
 """
 from __future__ import annotations
 
@@ -33,7 +38,8 @@ import torch.distributed as dist
 
 from . import _native as nat
 from .moe import ExpertStack, combine, grouped_gemm, grouped_gemm_act, plan
-from .ops import _ACT, _DT, _need_cuda, _stream, _vp, act_and_mul_quant, linear, quantize_rows
+from .ops import (_ACT, _DT, _need_cuda, _stream, _vp, act_and_mul_quant, linear, linear_q_peer_cols,
+                  quantize_rows)
 from .qtensor import QTensor
 
 
@@ -106,31 +112,18 @@ def _cuda_view(ptr: int, nbytes: int, device: torch.device) -> torch.Tensor:
     return torch.as_tensor(_Mem(), device=device)
 
 
-class PeerExchange:
-    """Receive and back buffers of one rank in one CUDA IPC allocation, mapped into every
-    peer of `group`: rows [cap] of int8 [H] + fp32 scale + int32 tag received from any rank,
-    and back rows [max_tokens * top_k] of `dtype` [H] returned to this rank's slots.
-    cap = world * max_tokens * top_k covers any routing."""
+class PeerBuffer:
+    """One zeroed CUDA IPC allocation of `nbytes` on every rank of `group`, mapped into every
+    rank: bases[r] is rank r's allocation as this process addresses it (bases[rank] is this
+    rank's own, also viewed as the uint8 tensor `mem`)."""
 
-    def __init__(self, max_tokens: int, top_k: int, hidden: int, dtype: torch.dtype, device: torch.device,
-                 group=None):
+    def __init__(self, nbytes: int, device: torch.device, group=None):
         self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
         if self.world > 8:
-            raise ValueError("the peer-memory exchange spans at most 8 ranks")
-        self.max_tokens, self.top_k, self.hidden, self.dtype = max_tokens, top_k, hidden, dtype
-        self.cap = self.world * max_tokens * top_k
-        self.back_rows = max_tokens * top_k
-        esz = torch.tensor([], dtype=dtype).element_size()
-        parts = [("q", self.cap * hidden), ("s", self.cap * 4), ("tag", self.cap * 4),
-                 ("back", self.back_rows * hidden * esz)]
-        self.off, total = {}, 0
-        for name, nbytes in parts:
-            self.off[name] = total
-            total += (nbytes + 255) // 256 * 256
-        self.nbytes = total
+            raise ValueError("peer memory spans at most 8 ranks")
         ptr = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(64)
-        nat.call("fni8_ipc_alloc", total, ctypes.byref(ptr), ctypes.cast(handle, ctypes.c_void_p))
+        nat.call("fni8_ipc_alloc", nbytes, ctypes.byref(ptr), ctypes.cast(handle, ctypes.c_void_p))
         self._own = ptr.value
         handles = [None] * self.world
         dist.all_gather_object(handles, handle.raw, group=group)
@@ -153,23 +146,17 @@ class PeerExchange:
             nat.lib().fni8_ipc_free(ctypes.c_void_p(self._own))
             self._opened, self._own = [], None
             raise
-        arr = ctypes.c_void_p * self.world
-        self._arrays = {name: arr(*[b + self.off[name] for b in bases]) for name, _ in parts}
-        self.peer = {name: ctypes.cast(a, ctypes.c_void_p) for name, a in self._arrays.items()}
-        mem = _cuda_view(self._own, total, device)
-        self.rq = mem[self.off["q"]:self.off["q"] + self.cap * hidden].view(self.cap, hidden).view(torch.int8)
-        self.rs = mem[self.off["s"]:self.off["s"] + self.cap * 4].view(torch.float32)
-        self.tag = mem[self.off["tag"]:self.off["tag"] + self.cap * 4].view(torch.int32)
-        self.back = mem[self.off["back"]:self.off["back"] + self.back_rows * hidden * esz].view(dtype).view(
-            self.back_rows, hidden)
-        self._mem = mem
+        self.bases = bases
+        self.nbytes = nbytes
+        self.mem = _cuda_view(self._own, nbytes, device)
 
-    def fits(self, T: int, top_k: int, hidden: int, dtype: torch.dtype) -> bool:
-        return T <= self.max_tokens and top_k == self.top_k and hidden == self.hidden and dtype == self.dtype
+    def pointers(self, offset: int = 0):
+        """Every rank's base + offset, as the ctypes pointer array the kernels take."""
+        return (ctypes.c_void_p * self.world)(*[b + offset for b in self.bases])
 
     def close(self, group=None):
-        """Unmap the peers' buffers and free this rank's (after a barrier: no rank still
-        stores into them)."""
+        """Unmap the peers' allocations and free this rank's (every rank calls it; after a
+        barrier, so no rank still stores into them)."""
         if self._own is None:
             return
         torch.cuda.synchronize()
@@ -178,9 +165,50 @@ class PeerExchange:
             nat.call("fni8_ipc_close", p)
         self._opened = []
         dist.barrier(group=group)
-        self._mem = self.rq = self.rs = self.tag = self.back = None
+        self.mem = None
         nat.call("fni8_ipc_free", self._own)
         self._own = None
+
+
+class PeerExchange:
+    """Receive and back buffers of one rank in one PeerBuffer, mapped into every peer of
+    `group`: rows [cap] of int8 [H] + fp32 scale + int32 tag received from any rank, and back
+    rows [max_tokens * top_k] of `dtype` [H] returned to this rank's slots.
+    cap = world * max_tokens * top_k covers any routing."""
+
+    def __init__(self, max_tokens: int, top_k: int, hidden: int, dtype: torch.dtype, device: torch.device,
+                 group=None):
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the peer-memory exchange spans at most 8 ranks")
+        self.max_tokens, self.top_k, self.hidden, self.dtype = max_tokens, top_k, hidden, dtype
+        self.cap = self.world * max_tokens * top_k
+        self.back_rows = max_tokens * top_k
+        esz = torch.tensor([], dtype=dtype).element_size()
+        parts = [("q", self.cap * hidden), ("s", self.cap * 4), ("tag", self.cap * 4),
+                 ("back", self.back_rows * hidden * esz)]
+        self.off, total = {}, 0
+        for name, nbytes in parts:
+            self.off[name] = total
+            total += (nbytes + 255) // 256 * 256
+        self.nbytes = total
+        self.buf = PeerBuffer(total, device, group)
+        self._arrays = {name: self.buf.pointers(self.off[name]) for name, _ in parts}
+        self.peer = {name: ctypes.cast(a, ctypes.c_void_p) for name, a in self._arrays.items()}
+        mem = self.buf.mem
+        self.rq = mem[self.off["q"]:self.off["q"] + self.cap * hidden].view(self.cap, hidden).view(torch.int8)
+        self.rs = mem[self.off["s"]:self.off["s"] + self.cap * 4].view(torch.float32)
+        self.tag = mem[self.off["tag"]:self.off["tag"] + self.cap * 4].view(torch.int32)
+        self.back = mem[self.off["back"]:self.off["back"] + self.back_rows * hidden * esz].view(dtype).view(
+            self.back_rows, hidden)
+
+    def fits(self, T: int, top_k: int, hidden: int, dtype: torch.dtype) -> bool:
+        return T <= self.max_tokens and top_k == self.top_k and hidden == self.hidden and dtype == self.dtype
+
+    def close(self, group=None):
+        """Unmap the peers' buffers and free this rank's (every rank calls it)."""
+        self.rq = self.rs = self.tag = self.back = None
+        self.buf.close(group)
 
 
 def ep_dispatch(xq, xs, slot_of_row, offsets, E, rank, top_k, dst_base, xchg: PeerExchange, max_rows):
@@ -192,20 +220,6 @@ def ep_dispatch(xq, xs, slot_of_row, offsets, E, rank, top_k, dst_base, xchg: Pe
 def ep_return(y, n_recv, xchg: PeerExchange):
     nat.call("fni8_ep_return", _vp(y), _DT[y.dtype], _vp(n_recv), xchg.cap, _vp(xchg.tag), xchg.hidden, xchg.world,
              xchg.peer["back"], xchg.back_rows, _stream(y.device))
-
-
-def grouped_gemm_scatter(a, a_scale, w, w_scale, seg_expert, seg_off, seg_cnt, row_tag, peers, world, peer_rows,
-                         out_dtype=torch.float16):
-    """Grouped W8A8 GEMM whose output row r lands in row (row_tag[r] & 0xFFFFFF) of
-    buffer peers[row_tag[r] >> 24] (a ctypes array of `world` device pointers to
-    [peer_rows, N] buffers of out_dtype): the expert-parallel return fused into the down
-    projection's epilogue."""
-    _need_cuda(a, "grouped_gemm_scatter")
-    R, K = a.shape
-    E, N, _ = w.shape
-    nat.call("fni8_grouped_gemm_w8a8_scatter", _vp(a), _vp(a_scale), R, _vp(w), _vp(w_scale), E, N, K, _vp(seg_expert),
-             _vp(seg_off), _vp(seg_cnt), seg_expert.numel(), _vp(row_tag), peers, world, peer_rows, _DT[out_dtype],
-             _stream(a.device))
 
 
 def quantize_rows_dev(x: torch.Tensor, rows_dev: torch.Tensor):
@@ -247,16 +261,12 @@ class ExpertParallelMoE:
     around them is what this class owns."""
 
     def __init__(self, local: ExpertStack, num_experts: int, group=None, act: str = "silu", ops=KernelOps,
-                 transport: str = "auto", max_tokens: int | None = None, fuse_return: bool = False):
+                 transport: str = "auto", max_tokens: int | None = None):
         """transport: "p2p" (peer-memory exchange, CUDA, at most 8 ranks on one node),
         "nccl" (all_to_all_single, any backend) or "auto" (p2p for the NCCL backend with the
         sm_100a kernels, nccl otherwise). max_tokens: the most tokens one rank passes per
         call (p2p buffers are sized for it; default: the first call's, as a maximum over the
-        ranks). fuse_return (p2p): the down projection's epilogue stores each expert output
-        straight into its source's slot instead of a separate return kernel copying whole
-        rows afterwards (off by default: measured on 2 B200s, 0.97 vs 0.64 ms per layer, the
-        epilogue's 64-byte per-thread stores over NVLink hold up the tile pipeline)."""
-        self.fuse_return = fuse_return
+        ranks)."""
         self.local = local
         self.E = num_experts
         self.group = group
@@ -339,12 +349,8 @@ class ExpertParallelMoE:
         else:
             h = grouped_gemm(X.rq, X.rs, L.w_gu, L.s_gu, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
             hq, hs = act_and_mul_quant_rows(h, n_recv, self.act)
-        if self.fuse_return:  # each output row goes straight to its source's slot
-            grouped_gemm_scatter(hq, hs, L.w_dn, L.s_dn, self._iota, seg_off, seg_cnt, X.tag, X.peer["back"],
-                                 X.world, X.back_rows, out_dtype=x.dtype)
-        else:
-            y = grouped_gemm(hq, hs, L.w_dn, L.s_dn, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
-            ep_return(y, n_recv, X)
+        y = grouped_gemm(hq, hs, L.w_dn, L.s_dn, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
+        ep_return(y, n_recv, X)
         dist.all_reduce(self._tick, op=dist.ReduceOp.MAX, group=self.group)  # every output is back at its source
         ros_slot = torch.where(ros >= 0, self._slots[: T * k], torch.full_like(ros, -1))
         return combine(X.back[: T * k], ros_slot, topw)
@@ -360,23 +366,62 @@ def shard_rows(qt: QTensor, world: int, rank: int) -> QTensor:
 
 
 class ColumnParallelLinearW8A8:
-    """y = x W^T with W's output channels sharded over the ranks of `group`."""
+    """y = x W^T with W's output channels sharded over the ranks of `group`.
 
-    def __init__(self, shard: QTensor, group=None, matmul=linear, chunk_rows: int = 1024):
+    transport "p2p" (the sm_100a kernels, NCCL group of at most 8 ranks on one node): the
+    GEMM stores this rank's columns straight into every rank's output buffer over NVLink
+    (fni8.ops.linear_q_peer_cols), then a one-element NCCL all_reduce on the same stream
+    orders the ranks; no host synchronisation, so a decode runner can capture it. The
+    output buffers are the layer's own: `ring` buffers of [max_rows, world * n] in CUDA IPC
+    memory (max_rows default: the first call's rows, as a maximum over the ranks), used in
+    turn. A call returns a view of its buffer, valid until `ring` more calls of this layer
+    (copy=True returns a tensor of its own). close() releases them (every rank, before
+    destroy_process_group).
+    transport "nccl" (any backend): the local GEMM (`matmul`) and all_gather_into_tensor;
+    batches of at least 2 * chunk_rows rows go in row chunks whose exchanges run
+    asynchronously.
+    "auto": p2p for the NCCL backend with the sm_100a kernels and per_row_i8 shards, else nccl.
+    """
+
+    def __init__(self, shard: QTensor, group=None, matmul=linear, chunk_rows: int = 1024, transport: str = "auto",
+                 max_rows: int | None = None, ring: int = 2):
         self.shard = shard
         self.group = group
         self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
         self.matmul = matmul  # fni8.linear (the sm_100a kernels) unless a test swaps it
-        # batches of at least 2 x chunk_rows rows are computed and exchanged in chunks
         self.chunk_rows = chunk_rows
+        if transport == "auto":
+            transport = ("p2p" if (matmul is linear and 1 < self.world <= 8 and shard.scheme == "per_row_i8" and
+                                   shard.data.is_cuda and dist.get_backend(group) == "nccl") else "nccl")
+        if transport not in ("p2p", "nccl"):
+            raise ValueError(f"unknown transport {transport!r}")
+        if transport == "p2p" and shard.data.shape[0] % 32:
+            raise ValueError(f"p2p column all-gather takes shards of a multiple of 32 columns "
+                             f"(got {shard.data.shape[0]})")
+        if ring < 1:
+            raise ValueError("ring must be at least 1")
+        self.transport = transport
+        self.max_rows = max_rows
+        self.ring = ring
+        self.buf: PeerBuffer | None = None
 
-    def __call__(self, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    def close(self):
+        """Release the p2p output buffers (every rank calls it)."""
+        if self.buf is not None:
+            self.buf.close(self.group)
+            self.buf = None
+
+    def __call__(self, x: torch.Tensor, bias: torch.Tensor | None = None, copy: bool = False) -> torch.Tensor:
         K = x.shape[-1]
         x2 = x.reshape(-1, K)
         M = x2.shape[0]
         n = self.shard.data.shape[0]
         if self.world == 1:
             return self.matmul(x2, self.shard, bias).reshape(*x.shape[:-1], n)
+        if self.transport == "p2p":
+            y = self._p2p(x2, bias)
+            return (y.clone() if copy else y).reshape(*x.shape[:-1], self.world * n)
         step = self.chunk_rows if M >= 2 * self.chunk_rows else max(M, 1)
         pending = []
         for r0 in range(0, M, step):
@@ -390,3 +435,32 @@ class ColumnParallelLinearW8A8:
             work.wait()  # the current stream waits for this chunk's exchange
             out[r0:r1].view(r1 - r0, self.world, n).copy_(parts.view(self.world, r1 - r0, n).permute(1, 0, 2))
         return out.reshape(*x.shape[:-1], self.world * n)
+
+    def _p2p(self, x2: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+        _need_cuda(x2, "ColumnParallelLinearW8A8")
+        M, K = x2.shape
+        n = self.shard.data.shape[0]
+        Nt = self.world * n
+        if self.buf is None:
+            rows = self.max_rows
+            if rows is None:
+                m = torch.tensor([M], dtype=torch.int64, device=x2.device)
+                dist.all_reduce(m, op=dist.ReduceOp.MAX, group=self.group)
+                rows = int(m.item())
+            self._rows = max(rows, 1)
+            self._slot = (self._rows * Nt * 2 + 255) // 256 * 256  # 16-bit outputs
+            self.buf = PeerBuffer(self.ring * self._slot, x2.device, self.group)
+            self._arrays = [self.buf.pointers(i * self._slot) for i in range(self.ring)]
+            self._ptrs = [ctypes.cast(a, ctypes.c_void_p) for a in self._arrays]
+            self._tick = torch.zeros(1, dtype=torch.int32, device=x2.device)
+            self._next = 0
+        if M > self._rows:
+            raise ValueError(f"ColumnParallelLinearW8A8: {M} rows exceed the output buffers ({self._rows}); "
+                             "pass max_rows")
+        i = self._next
+        self._next = (i + 1) % self.ring
+        q, s = quantize_rows(x2)
+        linear_q_peer_cols(q, s, self.shard, self._ptrs[i], self.world, Nt, self.rank * n, bias=bias,
+                           out_dtype=x2.dtype)
+        dist.all_reduce(self._tick, op=dist.ReduceOp.MAX, group=self.group)  # every rank's columns have landed
+        return self.buf.mem[i * self._slot:i * self._slot + M * Nt * 2].view(x2.dtype).view(M, Nt)

@@ -279,19 +279,6 @@ FNI8_API int fni8_grouped_gemm_w8a8_act(const int8_t* a, const float* a_scale, i
                                         const int32_t* seg_off, const int32_t* seg_cnt, int64_t S, int act, void* out,
                                         int out_dtype, void* stream);
 
-/* fni8_grouped_gemm_w8a8 whose output rows go elsewhere: row r (of a segment) is stored as
- * row (row_tag[r] & 0xFFFFFF) of peer_out[row_tag[r] >> 24], a [peer_rows, N] buffer of rank
- * row_tag[r] >> 24 mapped into this process (fni8_ipc_open). With the tags of
- * fni8_ep_dispatch_i8 the down projection of an expert-parallel layer stores each output
- * straight into its source rank's slot over NVLink, tile by tile, while later tiles
- * compute (the return step fused into the GEMM epilogue). out_dtype F16 or BF16. */
-FNI8_API int fni8_grouped_gemm_w8a8_scatter(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w,
-                                            const float* w_scale, int64_t E, int64_t N, int64_t K,
-                                            const int32_t* seg_expert, const int32_t* seg_off,
-                                            const int32_t* seg_cnt, int64_t S, const int32_t* row_tag,
-                                            void* const* peer_out, int64_t world, int64_t peer_rows, int out_dtype,
-                                            void* stream);
-
 /* out[t] = sum_j topw[t, j] * y[row_of_slot[t*k + j]] in fp32, rounded once: the
  * weighted index_add_ combine (fni8serve/models/moe.py:97,105). */
 FNI8_API int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,
@@ -340,6 +327,27 @@ FNI8_API int fni8_ep_dispatch_i8(const int8_t* q, const float* scale, const int3
  * buffers), where that rank combines its tokens with fni8_moe_combine. */
 FNI8_API int fni8_ep_return(const void* y, int dtype, const int32_t* n_recv, int64_t cap_rows, const int32_t* tag,
                             int64_t H, int64_t world, void* const* peer_back, int64_t back_rows, void* stream);
+
+/* ------------------------------------------------------------------ column-parallel linear
+ * New capability (the reference forbids tensor parallelism, fni8serve/config.py:40-45): a
+ * dense W8A8 linear with its output channels sharded over the ranks, each rank's slice
+ * all-gathered into every rank's full output without a separate collective.
+ *
+ * y = dequant(a[M, K] . w[N, K]^T) for this rank's N output columns (the fni8_gemm_w8a8
+ * epilogue: a_scale [M], w_scale [N], optional bias [N]; out_dtype F16 or BF16), with element
+ * (m, n) stored to element (m, col_off + n) of every buffer peer_out[0 .. n_peers) (row stride
+ * ld elements; this rank's own buffer and its NVLink peers' buffers mapped with
+ * fni8_ipc_open, n_peers <= 8). Prefill sizes run the tile GEMM with these stores in its
+ * epilogue, so the slices cross NVLink tile by tile while later tiles compute; decode sizes
+ * run the split-K GEMM into tmp [M, N] (tmp_bytes >= M * N * 2) and then one kernel that
+ * copies it into the buffers. ws / ws_bytes: the GEMM workspace (fni8_gemm_workspace_bytes,
+ * zeroed once). Buffers 16-byte aligned, ld and col_off multiples of 8, N a multiple of 32,
+ * K of 16. No rank is waited for: the caller orders the ranks (a collective on the same
+ * stream) before any of them reads its buffer. */
+FNI8_API int fni8_gemm_w8a8_peer_cols(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,
+                                      const void* bias, int out_dtype, int64_t M, int64_t N, int64_t K,
+                                      void* const* peer_out, int n_peers, int64_t ld, int64_t col_off, void* tmp,
+                                      size_t tmp_bytes, void* ws, size_t ws_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -105,6 +105,15 @@ def test_argument_validation_without_launch(lib):
     assert lib.fni8_ep_dispatch_i8(p, p, p, p, 16, 2, 2, 4, 512, p, pp, pp, pp, 100, 100, None) == n.ERR_INVALID
     assert lib.fni8_ep_return(p, n.F32, p, 100, p, 512, 2, pp, 100, None) == n.ERR_INVALID
     assert lib.fni8_ep_return(p, n.F16, p, 100, p, 12, 2, pp, 100, None) == n.ERR_UNSUPPORTED
+    # column all-gather GEMM: destination count, shard width, column range, alignment
+    pc = lib.fni8_gemm_w8a8_peer_cols
+    assert pc(p, p, p, p, None, n.F16, 4, 64, 256, pp, 0, 256, 0, None, 0, None, 0, None) == n.ERR_INVALID
+    assert pc(p, p, p, p, None, n.F16, 4, 64, 256, pp, 9, 256, 0, None, 0, None, 0, None) == n.ERR_INVALID
+    assert pc(p, p, p, p, None, n.F16, 4, 48, 256, pp, 2, 256, 0, None, 0, None, 0, None) == n.ERR_UNSUPPORTED
+    assert pc(p, p, p, p, None, n.F16, 4, 64, 256, pp, 2, 256, 200, None, 0, None, 0, None) == n.ERR_INVALID
+    assert pc(p, p, p, p, None, n.F16, 4, 64, 256, pp, 2, 260, 4, None, 0, None, 0, None) == n.ERR_ALIGN
+    assert pc(p, p, p, p, None, n.F32, 4, 64, 256, pp, 2, 256, 0, None, 0, None, 0, None) == n.ERR_INVALID
+    assert pc(p, p, p, p, None, n.F16, 0, 64, 256, pp, 2, 256, 0, None, 0, None, 0, None) == n.OK
     assert lib.fni8_ipc_alloc(0, ctypes.byref(ctypes.c_void_p()), p) == n.ERR_INVALID
     assert lib.fni8_ipc_open(None, ctypes.byref(ctypes.c_void_p())) == n.ERR_INVALID
     assert lib.fni8_act_and_mul_quant_i8_rows(p, n.F16, 0, 4, 32, None, p, p, None) == n.ERR_INVALID

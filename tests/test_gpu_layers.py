@@ -169,44 +169,63 @@ def test_grouped_gemm_int32_exact():
             assert torch.equal(got[o:o + c], O.int_mm_fast(a[o:o + c], w[int(perm[s])])), s
 
 
+@pytest.mark.parametrize("M", [1, 40, 256, 300, 1000])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_grouped_gemm_row_scatter(dtype):
-    """The scatter epilogue (expert-parallel return fused into the down projection): every
-    output row lands in row (tag & 0xFFFFFF) of buffer tag >> 24 and equals the plain grouped
-    GEMM's row bit for bit. Two local buffers stand in for two ranks' back buffers."""
+def test_linear_peer_cols_all_gather(M, dtype):
+    """The column all-gather GEMM (fni8_gemm_w8a8_peer_cols): a shard's outputs land at its
+    column offset in every destination buffer, bit-exact against the plain GEMM, and nothing
+    outside those columns and rows is written. Three local buffers stand in for three ranks'
+    output buffers; the sizes cover the split-K + copy path (M <= 256) and the tile GEMM with
+    the stores in its epilogue (CTA pairs from 256 rows, a partial last tile at 300/1000)."""
     import ctypes
 
-    import fni8.moe as M
-    from fni8.parallel import grouped_gemm_scatter
+    import fni8
+    from fni8 import QTensor
+    from fni8.ops import linear_q_peer_cols
 
-    E, N, K = 6, 2048, 768
-    cnt = torch.tensor([40, 0, 130, 1, 300, 57], dtype=torch.int32)
-    off = torch.zeros(E, dtype=torch.int32)
-    off[1:] = torch.cumsum(cnt, 0)[:-1]
-    R = int(cnt.sum())
-    a = torch.randint(-127, 128, (R, K), generator=gen(20), dtype=torch.int8).to(DEV)
-    a_s = (torch.rand(R, generator=gen(21)) * 1e-2).to(DEV)
-    w = torch.randint(-127, 128, (E, N, K), generator=gen(22), dtype=torch.int8).to(DEV)
-    w_s = (torch.rand(E, N, generator=gen(23)) * 1e-2).to(DEV)
-    seg = torch.arange(E, dtype=torch.int32).to(DEV)
-    ref = M.grouped_gemm(a, a_s, w, w_s, seg, off.to(DEV), cnt.to(DEV), out_dtype=dtype)
-    rows = 400  # per buffer
-    dest = torch.randint(0, 2, (R,), generator=gen(24))
-    slot = torch.empty(R, dtype=torch.int64)
-    for b in range(2):  # distinct slots within each buffer
-        idx = (dest == b).nonzero().flatten()
-        slot[idx] = torch.randperm(rows, generator=gen(25 + b))[: idx.numel()]
-    tag = ((dest << 24) | slot).to(torch.int32).to(DEV)
-    bufs = [torch.zeros(rows, N, dtype=dtype, device=DEV) for _ in range(2)]
-    peers = (ctypes.c_void_p * 2)(*[b.data_ptr() for b in bufs])
-    grouped_gemm_scatter(a, a_s, w, w_s, seg, off.to(DEV), cnt.to(DEV), tag, ctypes.cast(peers, ctypes.c_void_p), 2,
-                         rows, out_dtype=dtype)
+    K, n, P, rank = 1024, 768, 3, 1
+    Nt, rows = P * n, M + 5
+    x = (torch.randn(M, K, generator=gen(30)) * 2).to(dtype).to(DEV)
+    w = torch.randint(-127, 128, (n, K), generator=gen(31), dtype=torch.int8).to(DEV)
+    ws = (torch.rand(n, generator=gen(32)) * 1e-3).to(DEV)
+    bias = (torch.randn(n, generator=gen(33)) * 0.1).to(dtype).to(DEV)
+    shard = QTensor(w, ws)
+    q, s = fni8.quantize_rows(x)
+    ref = fni8.linear_q(q, s, shard, bias=bias, out_dtype=dtype)
+    sentinel = torch.tensor(-7.0, dtype=dtype)
+    bufs = [torch.full((rows, Nt), -7.0, dtype=dtype, device=DEV) for _ in range(P)]
+    peers = (ctypes.c_void_p * P)(*[b.data_ptr() for b in bufs])
+    linear_q_peer_cols(q, s, shard, ctypes.cast(peers, ctypes.c_void_p), P, Nt, rank * n, bias=bias, out_dtype=dtype)
     torch.cuda.synchronize()
-    for r in range(0, R, 7):
-        got = bufs[int(dest[r])][int(slot[r])]
-        assert torch.equal(got, ref[r]), r
-    got_all = torch.stack([bufs[int(dest[r])][int(slot[r])] for r in range(R)])
-    assert torch.equal(got_all, ref)
+    for b in bufs:
+        got = b.cpu()
+        assert torch.equal(got[:M, rank * n:(rank + 1) * n], ref.cpu())
+        untouched = torch.ones(rows, Nt, dtype=torch.bool)
+        untouched[:M, rank * n:(rank + 1) * n] = False
+        assert bool((got[untouched] == sentinel).all())
+
+
+def test_linear_peer_cols_rejects_bad_layouts():
+    """Host-side checks of the all-gather GEMM: columns past ld, misaligned column offset,
+    a shard width that is not a multiple of 32."""
+    import ctypes
+
+    import fni8
+    from fni8 import QTensor
+    from fni8.ops import linear_q_peer_cols
+
+    K, n = 256, 64
+    q, s = fni8.quantize_rows(torch.randn(4, K, device=DEV).half())
+    buf = torch.zeros(4, 4 * n, dtype=torch.float16, device=DEV)
+    peers = ctypes.cast((ctypes.c_void_p * 1)(buf.data_ptr()), ctypes.c_void_p)
+    shard = QTensor(torch.zeros(n, K, dtype=torch.int8, device=DEV), torch.ones(n, device=DEV))
+    with pytest.raises(fni8.Fni8Error):
+        linear_q_peer_cols(q, s, shard, peers, 1, 4 * n, 3 * n + 8)  # past ld
+    with pytest.raises(fni8.Fni8Error):
+        linear_q_peer_cols(q, s, shard, peers, 1, 4 * n, 4)  # not a 16-byte column offset
+    odd = QTensor(torch.zeros(48, K, dtype=torch.int8, device=DEV), torch.ones(48, device=DEV))
+    with pytest.raises(fni8.Fni8Error):
+        linear_q_peer_cols(q, s, odd, peers, 1, 4 * n, 0)
 
 
 @pytest.mark.parametrize("scoring", ["softmax", "sigmoid"])

@@ -61,12 +61,12 @@ def _ep_worker(rank, world, port, errq):
         topi, topw = moe.route(torch.randn(T, E, generator=gx, device=dev) + bias, k)
         ref = moe.experts(x, topi, topw, full)
         # peer-memory exchange (the default on NCCL) and the all_to_all exchange
-        for transport, fuse in (("p2p", False), ("p2p", True), ("nccl", False)):
-            ep = ExpertParallelMoE(local, E, transport=transport, fuse_return=fuse)
+        for transport in ("p2p", "nccl"):
+            ep = ExpertParallelMoE(local, E, transport=transport)
             assert ep.transport == transport
             got = ep(x, topi, topw)
             torch.cuda.synchronize()
-            assert torch.equal(got, ref), (transport, fuse, (got.float() - ref.float()).abs().max().item())
+            assert torch.equal(got, ref), (transport, (got.float() - ref.float()).abs().max().item())
             # a rank with no tokens still takes every collective step
             got0 = ep(x[:0], topi[:0], topw[:0]) if rank == 1 else ep(x, topi, topw)
             assert got0.shape[0] == (0 if rank == 1 else T)
@@ -108,14 +108,37 @@ def _cp_worker(rank, world, port, errq):
         g = torch.Generator(device=dev).manual_seed(3)
         q, s = quantize_int8_rowwise(0.02 * torch.randn(N, K, generator=g, device=dev))
         full = QTensor(q, s.view(-1))
-        cp = ColumnParallelLinearW8A8(shard_rows(full, world, rank))
-        cpc = ColumnParallelLinearW8A8(shard_rows(full, world, rank), chunk_rows=128)  # 300 rows: 3 chunks
-        for M in (1, 16, 300):
+        shard = shard_rows(full, world, rank)
+        cp = ColumnParallelLinearW8A8(shard, max_rows=300)  # p2p: all-gather from the GEMM over NVLink
+        assert cp.transport == "p2p"
+        cpn = ColumnParallelLinearW8A8(shard, transport="nccl")
+        cpc = ColumnParallelLinearW8A8(shard, transport="nccl", chunk_rows=128)  # 300 rows: 3 chunks
+        outs = []
+        for M in (1, 16, 300):  # split-K + copy kernel, and the tile GEMM with the stores in its epilogue
             x = torch.randn(M, K, generator=g, device=dev).half()
             ref = fni8.linear(x, full)
-            for layer in (cp, cpc):
+            for layer in (cp, cpn, cpc):
                 got = layer(x)
-                assert torch.equal(got, ref), (M, (got.float() - ref.float()).abs().max().item())
+                assert torch.equal(got, ref), (M, layer.transport, (got.float() - ref.float()).abs().max().item())
+            outs.append((cp(x, copy=True), ref))
+        for got, ref in outs:  # copies stay valid after later calls reuse the ring
+            assert torch.equal(got, ref)
+        # no host synchronisation: the p2p layer replays from a CUDA graph
+        x = torch.randn(300, K, generator=g, device=dev).half()
+        ref = fni8.linear(x, full)
+        st = torch.cuda.Stream()
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            cp(x)
+        torch.cuda.current_stream().wait_stream(st)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = cp(x)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+        del graph, out
+        cp.close()
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:

@@ -55,7 +55,7 @@ constexpr int kL2AheadUnits = 0;
 
 static __device__ int g_status;  // watchdog word of this file
 
-enum : int { kCodeProducer = 0x101, kCodeMma = 0x102, kCodeEpilogue = 0x103, kCodeDrain = 0x104 };
+enum : int { kCodeProducer = 0x101, kCodeMma = 0x102, kCodeEpilogue = 0x103, kCodeDrain = 0x104, kCodeScatter = 0x105 };
 constexpr int kMaxPeers = 8;
 enum : int { kOutF16 = 0, kOutBF16 = 1, kOutI32 = 2 };
 
@@ -68,13 +68,18 @@ struct Epi {
   int mode;              // kOutF16 / kOutBF16 / kOutI32
   int l2ahead;           // weight k-blocks pulled into L2 (beyond the ring) before the PDL wait
   int trigger;           // next kernel released at entry (0) or after this CTA's last load (1)
-  // Column all-gather (dense, 16-bit out, n_peers > 0): output element (m, n) goes to
-  // element (m, peer_col + n) of every peer_out[p] ([rows, peer_ld] each; buffers of this
-  // GPU or of its NVLink peers mapped into this process), instead of out.
+  // Peer outputs (16-bit out, n_peers > 0; buffers of this GPU or of its NVLink peers
+  // mapped into this process), instead of out:
+  //  * column all-gather (dense, row_tag null): element (m, n) goes to element
+  //    (m, peer_col + n) of every peer_out[p] ([rows, peer_ld] each);
+  //  * row scatter (grouped, row_tag set): row r goes to row (row_tag[r] & 0xFFFFFF) of
+  //    peer_out[row_tag[r] >> 24] ([peer_rows, N] each).
   void* peer_out[kMaxPeers];
   int n_peers;
   int peer_col;
   int64_t peer_ld;
+  const int32_t* row_tag;
+  int64_t peer_rows;
   // ACTMUL kernels (gate_up with act_and_mul in the epilogue): the weight holds the gate
   // rows [0, act_i) and the up rows [act_i, 2 act_i); tile n covers gate rows
   // [128 n, 128 n + 128) in accumulator columns 0-127 and the matching up rows in columns
@@ -294,6 +299,35 @@ __device__ __forceinline__ void store_slab_peers(uint8_t* buf, const uint4 (&o)[
       const uint4 v = *reinterpret_cast<const uint4*>(buf + r * 64 + ((g ^ ((r >> 1) & 3)) << 4));
       const int64_t off = (static_cast<int64_t>(row_base + r) * epi.peer_ld + epi.peer_col + n0 + 8 * g) * 2;
       for (int p = 0; p < epi.n_peers; ++p) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(epi.peer_out[p]) + off) = v;
+    }
+  }
+}
+
+// The same chunk to the rows its tags name (the row scatter): row r of the slab (tag: lane
+// r's `tag`) goes to row (tag & 0xFFFFFF) of peer_out[tag >> 24], columns [n0, n0 + 32),
+// 8 rows x 64 contiguous bytes per store instruction. A tag outside the buffers is
+// skipped and recorded in the status word.
+__device__ __forceinline__ void store_slab_rows(uint8_t* buf, const uint4 (&o)[4], int lane, const Epi& epi, int n0,
+                                                int N, uint32_t tag, int nrows, int* status) {
+  __syncwarp();  // every lane has read the previous chunk out of the buffer
+#pragma unroll
+  for (int j8 = 0; j8 < 4; ++j8)
+    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = o[j8];
+  __syncwarp();
+  const int g = lane & 3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = (lane >> 2) + 8 * i;
+    const uint32_t tg = __shfl_sync(0xffffffffu, tag, r);
+    if (r < nrows) {
+      const int src = static_cast<int>(tg >> 24);
+      const int64_t slot = static_cast<int64_t>(tg & 0xFFFFFFu);
+      if (src < epi.n_peers && slot < epi.peer_rows) {
+        const uint4 v = *reinterpret_cast<const uint4*>(buf + r * 64 + ((g ^ ((r >> 1) & 3)) << 4));
+        *reinterpret_cast<uint4*>(static_cast<uint8_t*>(epi.peer_out[src]) + (slot * N + n0 + 8 * g) * 2) = v;
+      } else if (g == 0) {
+        atomicExch(status, kCodeScatter);
+      }
     }
   }
 }
@@ -632,6 +666,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool slab_tma = tma_store && epi.residual == nullptr && (!GROUPED || rows_here - q * 32 >= 32) &&
                             q * 32 < rows_here;
       const bool slab_peer = !GROUPED && !ACTMUL && epi.n_peers > 0 && q * 32 < rows_here;
+      const bool slab_rows = GROUPED && !ACTMUL && epi.row_tag != nullptr && q * 32 < rows_here;
+      const uint32_t my_tag = (slab_rows && valid) ? static_cast<uint32_t>(__ldg(epi.row_tag + row)) : 0xFFFFFFFFu;
       if constexpr (ACTMUL) {
         // this warp's 64 of the tile's 128 product columns: gate accumulators at c, up at
         // 128 + c; outputs at column 128 n + c of the [rows, act_i] product
@@ -688,6 +724,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             dequant_chunk(epi.mode, r, a_s, s_ws + c, s_bias + c, epi.bias != nullptr, o);
             if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
             store_slab_peers(stg + ew * C::STG_BUF, o, lane, epi, n0, row0 + q * 32, min(32, rows_here - q * 32));
+          } else if (slab_rows && n0 < N) {
+            uint4 o[4];
+            dequant_chunk(epi.mode, r, a_s, s_ws + c, s_bias + c, epi.bias != nullptr, o);
+            if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
+            store_slab_rows(stg + ew * C::STG_BUF, o, lane, epi, n0, N, my_tag, min(32, rows_here - q * 32), &g_status);
           } else {
             if (n0 < N && valid) {
               if (epi.mode == kOutI32) store_chunk_i32(epi, r, row, n0, N, vec_ok != 0);
@@ -880,7 +921,8 @@ int tile_gemm_peer_cols(const int8_t* a, const float* a_scale, const int8_t* w, 
 int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w, const float* w_scale,
                       int64_t E, int64_t N, int64_t K, const int32_t* seg_expert, const int32_t* seg_off,
                       const int32_t* seg_cnt, int64_t S, void* out, int out_mode, int bn, bool pair,
-                      cudaStream_t st) {
+                      cudaStream_t st, const int32_t* row_tag, void* const* peer_out, int n_peers,
+                      int64_t peer_rows) {
   if (R <= 0 || N <= 0 || S <= 0) return FNI8_OK;
   if (S > tile::kMaxSeg) return fail(FNI8_ERR_UNSUPPORTED, "at most %d segments (got %lld)", tile::kMaxSeg, (long long)S);
   CUtensorMap ta, tb;
@@ -897,7 +939,16 @@ int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const in
   const bool vec_ok = ((N * (int64_t)esz) % 16 == 0) && aligned && (((uintptr_t)w_scale & 15u) == 0) &&
                       ((N % 4) == 0);
   CUtensorMap to;
-  const bool tma_store = out_tma_map(&to, out, out_mode, R, N);
+  bool tma_store = false;
+  if (row_tag != nullptr) {  // rows scattered into peers' buffers (validated by the caller)
+    memset(&to, 0, sizeof(to));
+    epi.row_tag = row_tag;
+    epi.n_peers = n_peers;
+    epi.peer_rows = peer_rows;
+    for (int i = 0; i < n_peers; ++i) epi.peer_out[i] = peer_out[i];
+  } else {
+    tma_store = out_tma_map(&to, out, out_mode, R, N);
+  }
   if (pair) {
     if (bn == 256)
       return tile::launch<256, true, true>(ta, tb, to, tma_store, epi, grp, (int)R, (int)N, (int)K, grid, vec_ok, st);

@@ -470,6 +470,32 @@ extern "C" int fni8_grouped_gemm_w8a8_act(const int8_t* a, const float* a_scale,
                        out_dtype == FNI8_F16 ? 0 : 1, grouped_pair_enabled(), static_cast<cudaStream_t>(stream));
 }
 
+extern "C" int fni8_grouped_gemm_w8a8_scatter(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w,
+                                              const float* w_scale, int64_t E, int64_t N, int64_t K,
+                                              const int32_t* seg_expert, const int32_t* seg_off,
+                                              const int32_t* seg_cnt, int64_t S, const int32_t* row_tag,
+                                              void* const* peer_out, int64_t world, int64_t peer_rows, int out_dtype,
+                                              void* stream) {
+  if (R < 0 || E <= 0 || N <= 0 || K <= 0 || S < 0 || peer_rows < 0) return fail(FNI8_ERR_INVALID, "scatter: bad sizes");
+  if (world < 1 || world > 8) return fail(FNI8_ERR_INVALID, "scatter: 1 <= world <= 8");
+  if (K % 16 != 0) return fail(FNI8_ERR_UNSUPPORTED, "scatter: K must be a multiple of 16");
+  if (N % 32 != 0) return fail(FNI8_ERR_UNSUPPORTED, "scatter: N must be a multiple of 32");
+  if (R >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31)) return fail(FNI8_ERR_UNSUPPORTED, "scatter: too large");
+  if (out_dtype != FNI8_F16 && out_dtype != FNI8_BF16) return fail(FNI8_ERR_INVALID, "scatter: out_dtype F16 or BF16");
+  if (R == 0 || S == 0) return FNI8_OK;
+  if (!a || !a_scale || !w || !w_scale || !seg_expert || !seg_off || !seg_cnt || !row_tag || !peer_out)
+    return fail(FNI8_ERR_INVALID, "scatter: null pointer");
+  for (int64_t i = 0; i < world; ++i) {
+    if (peer_out[i] == nullptr) return fail(FNI8_ERR_INVALID, "scatter: null peer buffer %lld", (long long)i);
+    if (reinterpret_cast<uintptr_t>(peer_out[i]) & 15u)
+      return fail(FNI8_ERR_ALIGN, "scatter: peer buffer %lld must be 16-byte aligned", (long long)i);
+  }
+  const int bn = (N % 256 == 0 || N > 1024) ? 256 : 128;
+  return tile_gemm_grouped(a, a_scale, R, w, w_scale, E, N, K, seg_expert, seg_off, seg_cnt, S, nullptr,
+                           out_dtype == FNI8_F16 ? 0 : 1, bn, grouped_pair_enabled(), static_cast<cudaStream_t>(stream),
+                           row_tag, peer_out, (int)world, peer_rows);
+}
+
 extern "C" int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,
                                 int64_t top_k, int64_t H, void* out, void* stream) {
   if (T < 0 || top_k <= 0 || H <= 0) return fail(FNI8_ERR_INVALID, "combine: bad sizes");

@@ -222,6 +222,20 @@ def ep_return(y, n_recv, xchg: PeerExchange):
              xchg.peer["back"], xchg.back_rows, _stream(y.device))
 
 
+def grouped_gemm_scatter(a, a_scale, w, w_scale, seg_expert, seg_off, seg_cnt, row_tag, peers, world, peer_rows,
+                         out_dtype=torch.float16):
+    """Grouped W8A8 GEMM whose output row r lands in row (row_tag[r] & 0xFFFFFF) of
+    buffer peers[row_tag[r] >> 24] (a ctypes array of `world` device pointers to
+    [peer_rows, N] buffers of out_dtype): the expert-parallel return fused into the down
+    projection's epilogue (C: fni8_grouped_gemm_w8a8_scatter)."""
+    _need_cuda(a, "grouped_gemm_scatter")
+    R, K = a.shape
+    E, N, _ = w.shape
+    nat.call("fni8_grouped_gemm_w8a8_scatter", _vp(a), _vp(a_scale), R, _vp(w), _vp(w_scale), E, N, K, _vp(seg_expert),
+             _vp(seg_off), _vp(seg_cnt), seg_expert.numel(), _vp(row_tag), peers, world, peer_rows, _DT[out_dtype],
+             _stream(a.device))
+
+
 def quantize_rows_dev(x: torch.Tensor, rows_dev: torch.Tensor):
     """fni8 quantize_rows over the first rows_dev[0] rows of x (the rest left as is)."""
     M, K = x.shape
@@ -261,12 +275,15 @@ class ExpertParallelMoE:
     around them is what this class owns."""
 
     def __init__(self, local: ExpertStack, num_experts: int, group=None, act: str = "silu", ops=KernelOps,
-                 transport: str = "auto", max_tokens: int | None = None):
+                 transport: str = "auto", max_tokens: int | None = None, fuse_return: bool = True):
         """transport: "p2p" (peer-memory exchange, CUDA, at most 8 ranks on one node),
         "nccl" (all_to_all_single, any backend) or "auto" (p2p for the NCCL backend with the
         sm_100a kernels, nccl otherwise). max_tokens: the most tokens one rank passes per
         call (p2p buffers are sized for it; default: the first call's, as a maximum over the
-        ranks)."""
+        ranks). fuse_return (p2p): the down projection's epilogue stores each expert output
+        straight into its source's slot over NVLink (fni8_grouped_gemm_w8a8_scatter), so the
+        return overlaps the GEMM; False runs the GEMM and then the return kernel."""
+        self.fuse_return = fuse_return
         self.local = local
         self.E = num_experts
         self.group = group
@@ -349,8 +366,12 @@ class ExpertParallelMoE:
         else:
             h = grouped_gemm(X.rq, X.rs, L.w_gu, L.s_gu, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
             hq, hs = act_and_mul_quant_rows(h, n_recv, self.act)
-        y = grouped_gemm(hq, hs, L.w_dn, L.s_dn, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
-        ep_return(y, n_recv, X)
+        if self.fuse_return:  # each output row goes straight to its source's slot
+            grouped_gemm_scatter(hq, hs, L.w_dn, L.s_dn, self._iota, seg_off, seg_cnt, X.tag, X.peer["back"],
+                                 X.world, X.back_rows, out_dtype=x.dtype)
+        else:
+            y = grouped_gemm(hq, hs, L.w_dn, L.s_dn, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
+            ep_return(y, n_recv, X)
         dist.all_reduce(self._tick, op=dist.ReduceOp.MAX, group=self.group)  # every output is back at its source
         ros_slot = torch.where(ros >= 0, self._slots[: T * k], torch.full_like(ros, -1))
         return combine(X.back[: T * k], ros_slot, topw)

@@ -279,6 +279,22 @@ FNI8_API int fni8_grouped_gemm_w8a8_act(const int8_t* a, const float* a_scale, i
                                         const int32_t* seg_off, const int32_t* seg_cnt, int64_t S, int act, void* out,
                                         int out_dtype, void* stream);
 
+/* fni8_grouped_gemm_w8a8 whose output rows go to other buffers: row r (of a segment) is
+ * stored as row (row_tag[r] & 0xFFFFFF) of peer_out[row_tag[r] >> 24], a [peer_rows, N]
+ * buffer of that rank mapped into this process (fni8_ipc_open; this rank's own at its
+ * index). With the tags of fni8_ep_dispatch_i8, the down projection of an expert-parallel
+ * layer stores each expert output straight into its source rank's slot over NVLink, tile
+ * by tile while later tiles compute: the return step of fni8_ep_return fused into the GEMM
+ * epilogue. Rows leave 8 rows x 64 contiguous bytes per store instruction; a tag outside
+ * the buffers is skipped and reported by fni8_device_status. out_dtype F16 or BF16,
+ * N % 32 == 0. */
+FNI8_API int fni8_grouped_gemm_w8a8_scatter(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w,
+                                            const float* w_scale, int64_t E, int64_t N, int64_t K,
+                                            const int32_t* seg_expert, const int32_t* seg_off,
+                                            const int32_t* seg_cnt, int64_t S, const int32_t* row_tag,
+                                            void* const* peer_out, int64_t world, int64_t peer_rows, int out_dtype,
+                                            void* stream);
+
 /* out[t] = sum_j topw[t, j] * y[row_of_slot[t*k + j]] in fp32, rounded once: the
  * weighted index_add_ combine (fni8serve/models/moe.py:97,105). */
 FNI8_API int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,

@@ -105,6 +105,13 @@ def test_argument_validation_without_launch(lib):
     assert lib.fni8_ep_dispatch_i8(p, p, p, p, 16, 2, 2, 4, 512, p, pp, pp, pp, 100, 100, None) == n.ERR_INVALID
     assert lib.fni8_ep_return(p, n.F32, p, 100, p, 512, 2, pp, 100, None) == n.ERR_INVALID
     assert lib.fni8_ep_return(p, n.F16, p, 100, p, 12, 2, pp, 100, None) == n.ERR_UNSUPPORTED
+    # fused expert return: world, row width
+    assert lib.fni8_grouped_gemm_w8a8_scatter(p, p, 16, p, p, 4, 64, 64, p, p, p, 4, p, pp, 9, 100, n.F16,
+                                              None) == n.ERR_INVALID
+    assert lib.fni8_grouped_gemm_w8a8_scatter(p, p, 16, p, p, 4, 48, 64, p, p, p, 4, p, pp, 2, 100, n.F16,
+                                              None) == n.ERR_UNSUPPORTED
+    assert lib.fni8_grouped_gemm_w8a8_scatter(p, p, 16, p, p, 4, 64, 64, p, p, p, 4, p, pp, 2, 100, n.I32,
+                                              None) == n.ERR_INVALID
     # column all-gather GEMM: destination count, shard width, column range, alignment
     pc = lib.fni8_gemm_w8a8_peer_cols
     assert pc(p, p, p, p, None, n.F16, 4, 64, 256, pp, 0, 256, 0, None, 0, None, 0, None) == n.ERR_INVALID

@@ -169,6 +169,48 @@ def test_grouped_gemm_int32_exact():
             assert torch.equal(got[o:o + c], O.int_mm_fast(a[o:o + c], w[int(perm[s])])), s
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_grouped_gemm_row_scatter(dtype):
+    """The scatter epilogue (expert-parallel return fused into the down projection): every
+    output row lands in row (tag & 0xFFFFFF) of buffer tag >> 24 and equals the plain grouped
+    GEMM's row bit for bit; no other row of the buffers is written. Two local buffers stand
+    in for two ranks' back buffers; segments of 0, 1 and ragged row counts."""
+    import ctypes
+
+    import fni8.moe as M
+    from fni8.parallel import grouped_gemm_scatter
+
+    E, N, K = 6, 2048, 768
+    cnt = torch.tensor([40, 0, 130, 1, 300, 57], dtype=torch.int32)
+    off = torch.zeros(E, dtype=torch.int32)
+    off[1:] = torch.cumsum(cnt, 0)[:-1]
+    R = int(cnt.sum())
+    a = torch.randint(-127, 128, (R, K), generator=gen(20), dtype=torch.int8).to(DEV)
+    a_s = (torch.rand(R, generator=gen(21)) * 1e-2).to(DEV)
+    w = torch.randint(-127, 128, (E, N, K), generator=gen(22), dtype=torch.int8).to(DEV)
+    w_s = (torch.rand(E, N, generator=gen(23)) * 1e-2).to(DEV)
+    seg = torch.arange(E, dtype=torch.int32).to(DEV)
+    ref = M.grouped_gemm(a, a_s, w, w_s, seg, off.to(DEV), cnt.to(DEV), out_dtype=dtype)
+    rows = 400  # per buffer
+    dest = torch.randint(0, 2, (R,), generator=gen(24))
+    slot = torch.empty(R, dtype=torch.int64)
+    for b in range(2):  # distinct slots within each buffer
+        idx = (dest == b).nonzero().flatten()
+        slot[idx] = torch.randperm(rows, generator=gen(25 + b))[: idx.numel()]
+    tag = ((dest << 24) | slot).to(torch.int32).to(DEV)
+    bufs = [torch.full((rows, N), -7.0, dtype=dtype, device=DEV) for _ in range(2)]
+    peers = (ctypes.c_void_p * 2)(*[b.data_ptr() for b in bufs])
+    grouped_gemm_scatter(a, a_s, w, w_s, seg, off.to(DEV), cnt.to(DEV), tag, ctypes.cast(peers, ctypes.c_void_p), 2,
+                         rows, out_dtype=dtype)
+    torch.cuda.synchronize()
+    got_all = torch.stack([bufs[int(dest[r])][int(slot[r])] for r in range(R)])
+    assert torch.equal(got_all, ref)
+    for b in range(2):
+        unused = torch.ones(rows, dtype=torch.bool)
+        unused[slot[dest == b]] = False
+        assert bool((bufs[b][unused.to(DEV)] == -7.0).all())
+
+
 @pytest.mark.parametrize("M", [1, 40, 256, 300, 1000])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_linear_peer_cols_all_gather(M, dtype):

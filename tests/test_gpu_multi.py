@@ -61,12 +61,12 @@ def _ep_worker(rank, world, port, errq):
         topi, topw = moe.route(torch.randn(T, E, generator=gx, device=dev) + bias, k)
         ref = moe.experts(x, topi, topw, full)
         # peer-memory exchange (the default on NCCL) and the all_to_all exchange
-        for transport in ("p2p", "nccl"):
-            ep = ExpertParallelMoE(local, E, transport=transport)
+        for transport, fuse in (("p2p", True), ("p2p", False), ("nccl", False)):
+            ep = ExpertParallelMoE(local, E, transport=transport, fuse_return=fuse)
             assert ep.transport == transport
             got = ep(x, topi, topw)
             torch.cuda.synchronize()
-            assert torch.equal(got, ref), (transport, (got.float() - ref.float()).abs().max().item())
+            assert torch.equal(got, ref), (transport, fuse, (got.float() - ref.float()).abs().max().item())
             # a rank with no tokens still takes every collective step
             got0 = ep(x[:0], topi[:0], topw[:0]) if rank == 1 else ep(x, topi, topw)
             assert got0.shape[0] == (0 if rank == 1 else T)

@@ -6,7 +6,8 @@ The reference has neither: its MoE runs every expert locally (fni8serve/models/m
 and its config forbids tensor parallelism on its PCIe fleet (fni8serve/config.py:40-45).
 Both are new capabilities sized for an 8 x B200 NVSwitch box.
 
-Expert parallel (rank r owns experts [r*E/P, (r+1)*E/P)), two transports:
+Expert parallel (rank r owns E/P experts: [r*E/P, (r+1)*E/P), or those a load-balanced
+placement gives it, balanced_placement), two transports:
   p2p (CUDA tensors, one node): quantise own tokens -> group (token, slot) pairs by expert
     -> all_gather of per-expert counts (device) -> placement computed on the device ->
     int8 rows + scales stored straight into the owners' receive buffers (CUDA IPC peer
@@ -59,6 +60,45 @@ def expert_shard(num_experts: int, world: int, rank: int) -> tuple[int, int]:
         raise ValueError(f"{num_experts} experts do not split over {world} ranks")
     per = num_experts // world
     return rank * per, (rank + 1) * per
+
+
+def balanced_placement(load, world: int) -> torch.Tensor:
+    """Expert placement for expert parallelism from per-expert loads (rows routed to each
+    expert, e.g. counted over recent batches on all ranks): every rank owns E/P experts and
+    the ranks' total loads are as even as a greedy longest-load-first assignment makes them
+    (the heaviest remaining expert goes to the least-loaded rank with room; ties by id, so
+    every rank computes the same placement). Returns place [E] int64: expert e runs on rank
+    place[e] // (E/P) as its local expert place[e] % (E/P). With skewed routing the
+    contiguous placement (place[e] = e) leaves one rank with several of the heaviest experts,
+    and every rank waits for it."""
+    c = [float(v) for v in torch.as_tensor(load).reshape(-1).tolist()]
+    E = len(c)
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    per = E // world
+    total = [0.0] * world
+    used = [0] * world
+    place = [0] * E
+    for e in sorted(range(E), key=lambda i: (-c[i], i)):
+        r = min((r for r in range(world) if used[r] < per), key=lambda r: (total[r], r))
+        place[e] = r * per + used[r]
+        used[r] += 1
+        total[r] += c[e]
+    return torch.tensor(place, dtype=torch.int64)
+
+
+def experts_of_rank(place: torch.Tensor, world: int, rank: int) -> list[int]:
+    """The expert ids rank `rank` holds under `place` (balanced_placement), in local order:
+    its local expert stack is these experts' weights, stacked in this order."""
+    p = [int(v) for v in place.tolist()]
+    per = len(p) // world
+    ids = [-1] * per
+    for e, v in enumerate(p):
+        if v // per == rank:
+            ids[v % per] = e
+    if min(ids) < 0:
+        raise ValueError("placement does not give every rank E/P experts")
+    return ids
 
 
 def exchange_plan(counts: torch.Tensor, world: int, group=None):
@@ -275,15 +315,26 @@ class ExpertParallelMoE:
     around them is what this class owns."""
 
     def __init__(self, local: ExpertStack, num_experts: int, group=None, act: str = "silu", ops=KernelOps,
-                 transport: str = "auto", max_tokens: int | None = None, fuse_return: bool = True):
+                 transport: str = "auto", max_tokens: int | None = None, fuse_return: bool = True,
+                 placement: torch.Tensor | None = None):
         """transport: "p2p" (peer-memory exchange, CUDA, at most 8 ranks on one node),
         "nccl" (all_to_all_single, any backend) or "auto" (p2p for the NCCL backend with the
         sm_100a kernels, nccl otherwise). max_tokens: the most tokens one rank passes per
         call (p2p buffers are sized for it; default: the first call's, as a maximum over the
         ranks). fuse_return (p2p): the down projection's epilogue stores each expert output
         straight into its source's slot over NVLink (fni8_grouped_gemm_w8a8_scatter), so the
-        return overlaps the GEMM; False runs the GEMM and then the return kernel."""
+        return overlaps the GEMM; False runs the GEMM and then the return kernel. placement:
+        which rank holds which expert (balanced_placement; `local` then holds
+        experts_of_rank(placement, world, rank) in that order); default: rank r holds experts
+        [r*E/P, (r+1)*E/P). Every rank passes the same placement."""
         self.fuse_return = fuse_return
+        if placement is not None:
+            placement = torch.as_tensor(placement, dtype=torch.int64).reshape(-1)
+            if placement.numel() != num_experts or not torch.equal(placement.sort().values,
+                                                                   torch.arange(num_experts)):
+                raise ValueError("placement must be a permutation of the expert ids")
+        self.placement = placement
+        self._place_dev = None
         self.local = local
         self.E = num_experts
         self.group = group
@@ -308,7 +359,18 @@ class ExpertParallelMoE:
             self.xchg.close(self.group)
             self.xchg = None
 
+    def _placed(self, topi: torch.Tensor) -> torch.Tensor:
+        """Expert ids -> placement slots (rank * E/P + local index); ids outside [0, E) stay
+        as they are (the plan drops them)."""
+        if self.placement is None:
+            return topi
+        if self._place_dev is None or self._place_dev.device != topi.device:
+            self._place_dev = self.placement.to(device=topi.device, dtype=topi.dtype)
+        ok = (topi >= 0) & (topi < self.E)
+        return torch.where(ok, self._place_dev[topi.clamp(0, self.E - 1).long()], topi)
+
     def __call__(self, x: torch.Tensor, topi: torch.Tensor, topw: torch.Tensor) -> torch.Tensor:
+        topi = self._placed(topi)
         if self.transport == "p2p":
             return self._p2p(x, topi, topw)
         T, H = x.shape

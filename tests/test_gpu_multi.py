@@ -37,7 +37,7 @@ def _ep_worker(rank, world, port, errq):
         import fni8.moe as moe
         from fni8 import QTensor
         from fni8.moe import ExpertStack
-        from fni8.parallel import ExpertParallelMoE, expert_shard
+        from fni8.parallel import ExpertParallelMoE, balanced_placement, expert_shard, experts_of_rank
         from fni8.quant.core import quantize_int8_rowwise
 
         dev = torch.device("cuda", rank)
@@ -61,6 +61,18 @@ def _ep_worker(rank, world, port, errq):
         topi, topw = moe.route(torch.randn(T, E, generator=gx, device=dev) + bias, k)
         ref = moe.experts(x, topi, topw, full)
         # peer-memory exchange (the default on NCCL) and the all_to_all exchange
+        # load-balanced placement: rank r holds the experts balanced_placement gives it
+        load = torch.bincount(topi.reshape(-1).long(), minlength=E)
+        dist.all_reduce(load)
+        place = balanced_placement(load.cpu(), world)
+        ids = experts_of_rank(place, world, rank)
+        placed = ExpertStack(w_gu[ids].contiguous(), s_gu[ids].contiguous(), w_dn[ids].contiguous(),
+                             s_dn[ids].contiguous())
+        epb = ExpertParallelMoE(placed, E, placement=place)
+        got = epb(x, topi, topw)
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref), ("placed", (got.float() - ref.float()).abs().max().item())
+        epb.close()
         for transport, fuse in (("p2p", True), ("p2p", False), ("nccl", False)):
             ep = ExpertParallelMoE(local, E, transport=transport, fuse_return=fuse)
             assert ep.transport == transport

@@ -86,7 +86,7 @@ def _ep_worker(rank, world, port, errq):
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world)
         from fni8.moe import ExpertStack
-        from fni8.parallel import ExpertParallelMoE, expert_shard
+        from fni8.parallel import ExpertParallelMoE, balanced_placement, expert_shard, experts_of_rank
         from oracle import w8a8_oracle as O
 
         E, k, H, I, T = 8, 2, 64, 32, 24 + 8 * rank  # ragged: ranks hold different token counts
@@ -101,6 +101,16 @@ def _ep_worker(rank, world, port, errq):
         got = ep(x, topi.int(), topw.float())
         ref = O.moe_experts_w8a8(x, topi, topw.float(), w_gu, s_gu, w_dn, s_dn, exact=False)
         assert torch.equal(got, ref), (got.float() - ref.float()).abs().max()
+        # load-balanced placement from the routed load of all ranks: the popular expert 0
+        # and its neighbours no longer share a rank; same result bit for bit
+        load = torch.bincount(topi.reshape(-1), minlength=E)
+        dist.all_reduce(load)
+        place = balanced_placement(load, world)
+        assert place.sort().values.tolist() == list(range(E))
+        ids = experts_of_rank(place, world, rank)
+        epb = ExpertParallelMoE(ExpertStack(w_gu[ids], s_gu[ids], w_dn[ids], s_dn[ids]), E, ops=OracleOps,
+                                placement=place)
+        assert torch.equal(epb(x, topi.int(), topw.float()), ref)
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # report to the parent, which fails the test
@@ -203,6 +213,25 @@ def _spawn(worker, world):
             p.kill()
             errs.append("rank timed out")
     assert not errs and all(p.exitcode == 0 for p in procs), errs
+
+
+def test_balanced_placement():
+    """Greedy longest-load-first placement: E/P experts per rank, every expert placed once,
+    the heaviest experts on different ranks, loads within one expert of even."""
+    from fni8.parallel import balanced_placement, experts_of_rank
+
+    load = torch.tensor([100, 90, 80, 5, 5, 5, 5, 5, 1, 1, 1, 1, 0, 0, 0, 0])
+    for P in (1, 2, 4, 8):
+        place = balanced_placement(load, P)
+        per = 16 // P
+        ranks = [experts_of_rank(place, P, r) for r in range(P)]
+        assert sorted(e for ids in ranks for e in ids) == list(range(16))
+        tot = [int(load[ids].sum()) for ids in ranks]
+        assert max(tot) - min(tot) <= int(load.max()), (P, tot)
+        if P >= 3:
+            assert len({int(place[e]) // per for e in (0, 1, 2)}) == 3
+    with pytest.raises(ValueError):
+        balanced_placement(load, 3)
 
 
 def test_peer_exchange_cleans_up_a_failed_mapping():

@@ -302,7 +302,7 @@ extern "C" int fni8_gemm_w8a8_peer_cols(const int8_t* a, const float* a_scale, c
   if (out_dtype != FNI8_F16 && out_dtype != FNI8_BF16)
     return fail(FNI8_ERR_INVALID, "out_dtype %d: expected F16 or BF16", out_dtype);
   if (n_peers < 1 || n_peers > 8) return fail(FNI8_ERR_INVALID, "peer_cols: 1 to 8 destination buffers (got %d)", n_peers);
-  if (N % 32 != 0) return fail(FNI8_ERR_UNSUPPORTED, "peer_cols: N=%lld must be a multiple of 32", (long long)N);
+  if (N % 64 != 0) return fail(FNI8_ERR_UNSUPPORTED, "peer_cols: N=%lld must be a multiple of 64", (long long)N);
   if (col_off < 0 || ld < col_off + N) return fail(FNI8_ERR_INVALID, "peer_cols: columns [%lld, %lld) exceed ld=%lld",
                                                    (long long)col_off, (long long)(col_off + N), (long long)ld);
   if (ld % 8 != 0 || col_off % 8 != 0 || ld >= (1LL << 31))

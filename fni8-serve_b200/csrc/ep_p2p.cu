@@ -35,6 +35,58 @@ struct Peers {
   void* p[kMaxPeers];
 };
 
+// Placement of one exchange from cnt_all[s * E + e] (rows source rank s sends to global
+// expert e; experts [d * El, (d + 1) * El) live on rank d). Rank d's receive buffer holds
+// its local experts one after another, each expert's rows ordered by source rank. Lane d
+// (< P) of the single warp walks owner d's local experts: dst_base[d * El + el] = where this
+// rank's rows of (d, el) start in d's buffer; for d == rank also this rank's received
+// segments (seg_off, seg_cnt) and their total (n_recv).
+__global__ void placement_kernel(const int32_t* __restrict__ cnt_all, int P, int E, int me, int32_t* dst_base,
+                                 int32_t* seg_off, int32_t* seg_cnt, int32_t* n_recv) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int d = threadIdx.x, El = E / P;
+  if (d >= P) return;
+  int base = 0;
+  for (int el = 0; el < El; ++el) {
+    const int e = d * El + el;
+    int tot = 0, before = 0;
+    for (int s = 0; s < P; ++s) {
+      const int c = cnt_all[s * E + e];
+      tot += c;
+      if (s < me) before += c;
+    }
+    dst_base[e] = base + before;
+    if (d == me) {
+      seg_off[el] = base;
+      seg_cnt[el] = tot;
+    }
+    base += tot;
+  }
+  if (d == me) *n_recv = base;
+}
+
+// A warp copies `pieces` 16-byte pieces src -> dst. Each lane issues up to eight loads
+// before it stores them: a store to a peer waits for its own load only, and more bytes
+// stay in flight over NVLink (measured on 2 B200s: the expert-parallel layer with the
+// dispatch and return kernels, 0.60 -> 0.57 ms per 4096-token step).
+__device__ __forceinline__ void warp_copy(uint4* dst, const uint4* __restrict__ src, int pieces, int lane) {
+  constexpr int kDepth = 8;
+  for (int c0 = 0; c0 < pieces; c0 += kDepth * 32) {
+    uint4 v[kDepth];
+#pragma unroll
+    for (int u = 0; u < kDepth; ++u) {
+      const int c = c0 + u * 32 + lane;
+      if (c < pieces) v[u] = __ldg(src + c);
+    }
+#pragma unroll
+    for (int u = 0; u < kDepth; ++u) {
+      const int c = c0 + u * 32 + lane;
+      if (c < pieces) dst[c] = v[u];
+    }
+  }
+}
+
 // One warp per sorted row. offsets[E + 1]: first sorted row of each expert (offsets[E] =
 // valid rows); dst_base[P * El]: where this rank's rows of (owner d, local expert el)
 // start in d's receive buffers.
@@ -67,7 +119,7 @@ __global__ void dispatch_kernel(const int8_t* __restrict__ q, const float* __res
     const int64_t t = slot / k;
     const uint4* src = reinterpret_cast<const uint4*>(q + t * H);
     uint4* dst = reinterpret_cast<uint4*>(static_cast<int8_t*>(pq.p[d]) + pos * H);
-    for (int c = lane; c < H / 16; c += 32) dst[c] = __ldg(src + c);
+    warp_copy(dst, src, H / 16, lane);
     if (lane == 0) {
       static_cast<float*>(ps.p[d])[pos] = __ldg(scale + t);
       static_cast<int32_t*>(ptag.p[d])[pos] = (me << 24) | slot;
@@ -98,7 +150,7 @@ __global__ void return_kernel(const T* __restrict__ y, const int32_t* __restrict
     }
     const uint4* s = reinterpret_cast<const uint4*>(y + i * H);
     uint4* d = reinterpret_cast<uint4*>(static_cast<T*>(pb.p[src]) + slot * H);
-    for (int c = lane; c < chunks; c += 32) d[c] = __ldg(s + c);
+    warp_copy(d, s, chunks, lane);
   }
   __threadfence_system();
 }
@@ -110,12 +162,22 @@ __global__ void push_cols_kernel(const uint4* __restrict__ src, int64_t M, int64
   pdl_launch_dependents();
   pdl_wait();
   const int64_t total = M * pieces_per_row;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t m = i / pieces_per_row, c = i - m * pieces_per_row;
-    const uint4 v = __ldg(src + i);
-    const int64_t off = (m * ld + col_off + 8 * c) * 2;
-    for (int p = 0; p < P; ++p) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(dst.p[p]) + off) = v;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  constexpr int kDepth = 4;  // loads in flight per thread before its stores
+  for (int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < total; i0 += kDepth * stride) {
+    uint4 v[kDepth];
+#pragma unroll
+    for (int u = 0; u < kDepth; ++u)
+      if (i0 + u * stride < total) v[u] = __ldg(src + i0 + u * stride);
+#pragma unroll
+    for (int u = 0; u < kDepth; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < total) {
+        const int64_t m = i / pieces_per_row, c = i - m * pieces_per_row;
+        const int64_t off = (m * ld + col_off + 8 * c) * 2;
+        for (int p = 0; p < P; ++p) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(dst.p[p]) + off) = v[u];
+      }
+    }
   }
   __threadfence_system();
 }
@@ -198,6 +260,18 @@ static int load_peers(ep::Peers* out, void* const* ptrs, int P, const char* what
     if (ptrs[i] == nullptr) return fail(FNI8_ERR_INVALID, "%s: null peer buffer %d", what, i);
     out->p[i] = ptrs[i];
   }
+  return FNI8_OK;
+}
+
+extern "C" int fni8_ep_placement(const int32_t* cnt_all, int64_t world, int64_t rank, int64_t E, int32_t* dst_base,
+                                 int32_t* seg_off, int32_t* seg_cnt, int32_t* n_recv, void* stream) {
+  if (world < 1 || world > ep::kMaxPeers || rank < 0 || rank >= world)
+    return fail(FNI8_ERR_INVALID, "ep_placement: 1 <= world <= %d, 0 <= rank < world", ep::kMaxPeers);
+  if (E <= 0 || E > ep::kMaxE || E % world != 0) return fail(FNI8_ERR_INVALID, "ep_placement: E must split over the ranks");
+  if (!cnt_all || !dst_base || !seg_off || !seg_cnt || !n_recv) return fail(FNI8_ERR_INVALID, "ep_placement: null pointer");
+  launch_pdl(ep::placement_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), cnt_all, (int)world, (int)E,
+             (int)rank, dst_base, seg_off, seg_cnt, n_recv);
+  FNI8_CHECK_LAUNCH("ep_placement");
   return FNI8_OK;
 }
 

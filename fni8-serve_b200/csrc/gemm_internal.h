@@ -22,13 +22,13 @@ int tile_gemm_grouped(const int8_t* a, const float* a_scale, int64_t R, const in
                       cudaStream_t st, const int32_t* row_tag = nullptr, void* const* peer_out = nullptr,
                       int n_peers = 0, int64_t peer_rows = 0);
 // (row_tag set: output row r goes to row (row_tag[r] & 0xFFFFFF) of the [peer_rows, N]
-// buffer peer_out[row_tag[r] >> 24] instead of out; 16-bit out_mode, N % 32 == 0, buffers
+// buffer peer_out[row_tag[r] >> 24] instead of out; 16-bit out_mode, N % 64 == 0, buffers
 // 16-byte aligned, checked by the caller.)
 // Dense tile GEMM whose epilogue writes output element (m, n) to element
 // (m, col_off + n) of each of the n_peers (<= 8) buffers peer_out[p] (row stride ld
 // elements; this GPU's memory or an NVLink peer's mapped into this process): a column
 // shard's part of an all-gather. 16-bit out_mode, no residual; the caller validates
-// alignment (buffers, ld and col_off 16-byte multiples, N % 32 == 0).
+// alignment (buffers, ld and col_off 16-byte multiples, N % 64 == 0).
 int tile_gemm_peer_cols(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale, const void* bias,
                         int out_mode, int64_t M, int64_t N, int64_t K, void* const* peer_out, int n_peers, int64_t ld,
                         int64_t col_off, int bn, bool pair, cudaStream_t st);

@@ -279,54 +279,77 @@ __device__ __forceinline__ void store_slab(uint8_t* buf, const uint4 (&o)[4], in
   }
 }
 
-// The same chunk to columns [peer_col + n0, peer_col + n0 + 32) of rows
-// [row_base, row_base + nrows) of every peer_out buffer (the column all-gather): staged in
-// the warp's buffer with the same swizzle, then read back so that each store instruction
-// writes 8 rows x 64 contiguous bytes, once per destination (plain stores: the
+// Two consecutive chunks (o0: columns [n0, n0 + 32), o1: [n0 + 32, n0 + 64)) of rows
+// [row_base, row_base + nrows) to columns [peer_col + n0, peer_col + n0 + 64) of every
+// peer_out buffer (the column all-gather). The rows pass through the warp's 2 KB buffer
+// sixteen at a time (128 bytes each, 16-byte pieces swizzled by row), so that each store
+// instruction writes 4 rows x 128 contiguous bytes per destination (plain stores: the
 // destinations may be other GPUs' memory).
-__device__ __forceinline__ void store_slab_peers(uint8_t* buf, const uint4 (&o)[4], int lane, const Epi& epi, int n0,
-                                                 int row_base, int nrows) {
-  __syncwarp();  // every lane has read the previous chunk out of the buffer
+__device__ __forceinline__ void store_cols_128(uint8_t* buf, const uint4 (&o0)[4], const uint4 (&o1)[4], int lane,
+                                               const Epi& epi, int n0, int row_base, int nrows) {
 #pragma unroll
-  for (int j8 = 0; j8 < 4; ++j8)
-    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = o[j8];
-  __syncwarp();
-  const int g = lane & 3;
+  for (int h = 0; h < 2; ++h) {  // slab rows [16h, 16h + 16)
+    __syncwarp();  // every lane has read the previous rows out of the buffer
+    if ((lane >> 4) == h) {
+      const int rr = lane & 15;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = (lane >> 2) + 8 * i;
-    if (r < nrows) {
-      const uint4 v = *reinterpret_cast<const uint4*>(buf + r * 64 + ((g ^ ((r >> 1) & 3)) << 4));
-      const int64_t off = (static_cast<int64_t>(row_base + r) * epi.peer_ld + epi.peer_col + n0 + 8 * g) * 2;
-      for (int p = 0; p < epi.n_peers; ++p) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(epi.peer_out[p]) + off) = v;
+      for (int j = 0; j < 4; ++j) {
+        *reinterpret_cast<uint4*>(buf + rr * 128 + ((j ^ (rr & 7)) << 4)) = o0[j];
+        *reinterpret_cast<uint4*>(buf + rr * 128 + (((j + 4) ^ (rr & 7)) << 4)) = o1[j];
+      }
+    }
+    __syncwarp();
+    const int g = lane & 7;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int rr = 4 * u + (lane >> 3);
+      const int r = 16 * h + rr;
+      if (r < nrows) {
+        const uint4 v = *reinterpret_cast<const uint4*>(buf + rr * 128 + ((g ^ (rr & 7)) << 4));
+        const int64_t off = (static_cast<int64_t>(row_base + r) * epi.peer_ld + epi.peer_col + n0 + 8 * g) * 2;
+        for (int p = 0; p < epi.n_peers; ++p)
+          *reinterpret_cast<uint4*>(static_cast<uint8_t*>(epi.peer_out[p]) + off) = v;
+      }
     }
   }
 }
 
-// The same chunk to the rows its tags name (the row scatter): row r of the slab (tag: lane
-// r's `tag`) goes to row (tag & 0xFFFFFF) of peer_out[tag >> 24], columns [n0, n0 + 32),
-// 8 rows x 64 contiguous bytes per store instruction. A tag outside the buffers is
-// skipped and recorded in the status word.
-__device__ __forceinline__ void store_slab_rows(uint8_t* buf, const uint4 (&o)[4], int lane, const Epi& epi, int n0,
-                                                int N, uint32_t tag, int nrows, int* status) {
-  __syncwarp();  // every lane has read the previous chunk out of the buffer
+// Two consecutive chunks (o0: columns [n0, n0 + 32), o1: [n0 + 32, n0 + 64)) of the slab's
+// rows to the rows their tags name (the row scatter): row r of the slab (tag: lane r's
+// `tag`) goes to row (tag & 0xFFFFFF) of peer_out[tag >> 24]. The rows pass through the
+// warp's 2 KB buffer sixteen at a time (128 bytes each, 16-byte pieces swizzled by row),
+// so that each store instruction writes 4 rows x 128 contiguous bytes, the NVLink write
+// granule, rather than 64-byte halves. A tag outside the buffers is skipped and recorded
+// in the status word.
+__device__ __forceinline__ void store_rows_128(uint8_t* buf, const uint4 (&o0)[4], const uint4 (&o1)[4], int lane,
+                                               const Epi& epi, int n0, int N, uint32_t tag, int nrows, int* status) {
 #pragma unroll
-  for (int j8 = 0; j8 < 4; ++j8)
-    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j8 ^ ((lane >> 1) & 3)) << 4)) = o[j8];
-  __syncwarp();
-  const int g = lane & 3;
+  for (int h = 0; h < 2; ++h) {  // slab rows [16h, 16h + 16)
+    __syncwarp();  // every lane has read the previous rows out of the buffer
+    if ((lane >> 4) == h) {
+      const int rr = lane & 15;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = (lane >> 2) + 8 * i;
-    const uint32_t tg = __shfl_sync(0xffffffffu, tag, r);
-    if (r < nrows) {
-      const int src = static_cast<int>(tg >> 24);
-      const int64_t slot = static_cast<int64_t>(tg & 0xFFFFFFu);
-      if (src < epi.n_peers && slot < epi.peer_rows) {
-        const uint4 v = *reinterpret_cast<const uint4*>(buf + r * 64 + ((g ^ ((r >> 1) & 3)) << 4));
-        *reinterpret_cast<uint4*>(static_cast<uint8_t*>(epi.peer_out[src]) + (slot * N + n0 + 8 * g) * 2) = v;
-      } else if (g == 0) {
-        atomicExch(status, kCodeScatter);
+      for (int j = 0; j < 4; ++j) {
+        *reinterpret_cast<uint4*>(buf + rr * 128 + ((j ^ (rr & 7)) << 4)) = o0[j];
+        *reinterpret_cast<uint4*>(buf + rr * 128 + (((j + 4) ^ (rr & 7)) << 4)) = o1[j];
+      }
+    }
+    __syncwarp();
+    const int g = lane & 7;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int rr = 4 * u + (lane >> 3);
+      const int r = 16 * h + rr;
+      const uint32_t tg = __shfl_sync(0xffffffffu, tag, r);
+      if (r < nrows) {
+        const int src = static_cast<int>(tg >> 24);
+        const int64_t slot = static_cast<int64_t>(tg & 0xFFFFFFu);
+        if (src < epi.n_peers && slot < epi.peer_rows) {
+          const uint4 v = *reinterpret_cast<const uint4*>(buf + rr * 128 + ((g ^ (rr & 7)) << 4));
+          *reinterpret_cast<uint4*>(static_cast<uint8_t*>(epi.peer_out[src]) + (slot * N + n0 + 8 * g) * 2) = v;
+        } else if (g == 0) {
+          atomicExch(status, kCodeScatter);
+        }
       }
     }
   }
@@ -703,47 +726,59 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else {
-        // Software-pipelined like the ACTMUL loop: dequantise a chunk into registers, issue
-        // the next chunk's TMEM load, then wait for the staging buffer and store.
         const int c_end = c_beg + BN / 2;
-        uint32_t r[32];
-        tmem_ld32(tbase + static_cast<uint32_t>(c_beg), r);
-        tmem_ld_wait();
-        tmem_regs_ready(r);
+        if (slab_rows || slab_peer) {
+          // peer outputs: two chunks (64 columns) per round, each row leaving as 128 bytes
 #pragma unroll 1
-        for (int c = c_beg; c < c_end; c += 32) {
-          const int n0 = nb0 + c;
-          const bool more = c + 32 < c_end;
-          if (slab_tma && n0 < N) {
-            uint4 o[4];
-            dequant_chunk(epi.mode, r, a_s, s_ws + c, s_bias + c, epi.bias != nullptr, o);
-            if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
-            store_slab(stg + ew * C::STG_BUF, o, lane, &tmOut, n0, row0 + q * 32);
-          } else if (slab_peer && n0 < N) {
-            uint4 o[4];
-            dequant_chunk(epi.mode, r, a_s, s_ws + c, s_bias + c, epi.bias != nullptr, o);
-            if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
-            store_slab_peers(stg + ew * C::STG_BUF, o, lane, epi, n0, row0 + q * 32, min(32, rows_here - q * 32));
-          } else if (slab_rows && n0 < N) {
-            uint4 o[4];
-            dequant_chunk(epi.mode, r, a_s, s_ws + c, s_bias + c, epi.bias != nullptr, o);
-            if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
-            store_slab_rows(stg + ew * C::STG_BUF, o, lane, epi, n0, N, my_tag, min(32, rows_here - q * 32), &g_status);
-          } else {
-            if (n0 < N && valid) {
-              if (epi.mode == kOutI32) store_chunk_i32(epi, r, row, n0, N, vec_ok != 0);
-              else if (epi.mode == kOutF16)
-                store_chunk<__half>(epi, r, row, reinterpret_cast<__half*>(orow), n0, N, a_s, s_ws + c, s_bias + c,
-                                    vec_ok != 0);
-              else
-                store_chunk<__nv_bfloat16>(epi, r, row, reinterpret_cast<__nv_bfloat16*>(orow), n0, N, a_s,
-                                           s_ws + c, s_bias + c, vec_ok != 0);
-            }
-            if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
-          }
-          if (more) {
+          for (int c = c_beg; c < c_end && nb0 + c < N; c += 64) {
+            uint32_t r0[32], r1[32];
+            tmem_ld32(tbase + static_cast<uint32_t>(c), r0);
+            tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r1);
             tmem_ld_wait();
-            tmem_regs_ready(r);
+            tmem_regs_ready(r0);
+            tmem_regs_ready(r1);
+            uint4 o0[4], o1[4];
+            dequant_chunk(epi.mode, r0, a_s, s_ws + c, s_bias + c, epi.bias != nullptr, o0);
+            dequant_chunk(epi.mode, r1, a_s, s_ws + c + 32, s_bias + c + 32, epi.bias != nullptr, o1);
+            if (slab_rows)
+              store_rows_128(stg + ew * C::STG_BUF, o0, o1, lane, epi, nb0 + c, N, my_tag,
+                             min(32, rows_here - q * 32), &g_status);
+            else
+              store_cols_128(stg + ew * C::STG_BUF, o0, o1, lane, epi, nb0 + c, row0 + q * 32,
+                             min(32, rows_here - q * 32));
+          }
+        } else {
+          // Software-pipelined like the ACTMUL loop: dequantise a chunk into registers, issue
+          // the next chunk's TMEM load, then wait for the staging buffer and store.
+          uint32_t r[32];
+          tmem_ld32(tbase + static_cast<uint32_t>(c_beg), r);
+          tmem_ld_wait();
+          tmem_regs_ready(r);
+#pragma unroll 1
+          for (int c = c_beg; c < c_end; c += 32) {
+            const int n0 = nb0 + c;
+            const bool more = c + 32 < c_end;
+            if (slab_tma && n0 < N) {
+              uint4 o[4];
+              dequant_chunk(epi.mode, r, a_s, s_ws + c, s_bias + c, epi.bias != nullptr, o);
+              if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
+              store_slab(stg + ew * C::STG_BUF, o, lane, &tmOut, n0, row0 + q * 32);
+            } else {
+              if (n0 < N && valid) {
+                if (epi.mode == kOutI32) store_chunk_i32(epi, r, row, n0, N, vec_ok != 0);
+                else if (epi.mode == kOutF16)
+                  store_chunk<__half>(epi, r, row, reinterpret_cast<__half*>(orow), n0, N, a_s, s_ws + c, s_bias + c,
+                                      vec_ok != 0);
+                else
+                  store_chunk<__nv_bfloat16>(epi, r, row, reinterpret_cast<__nv_bfloat16*>(orow), n0, N, a_s,
+                                             s_ws + c, s_bias + c, vec_ok != 0);
+              }
+              if (more) tmem_ld32(tbase + static_cast<uint32_t>(c + 32), r);
+            }
+            if (more) {
+              tmem_ld_wait();
+              tmem_regs_ready(r);
+            }
           }
         }
       }

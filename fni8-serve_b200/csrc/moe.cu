@@ -311,7 +311,9 @@ __global__ void gather_rows(const int8_t* __restrict__ q, const float* __restric
   }
 }
 
-template <typename T>
+// SLOTS: y is indexed by slot (row t*k + j holds slot j of token t, the expert-parallel back
+// buffer); row_of_slot only marks dropped slots (< 0).
+template <typename T, bool SLOTS = false>
 __global__ void combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ row_of_slot,
                                const float* __restrict__ topw, int64_t Tn, int k, int H, T* __restrict__ out) {
   pdl_launch_dependents();
@@ -321,8 +323,9 @@ __global__ void combine_kernel(const T* __restrict__ y, const int32_t* __restric
     for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       for (int j = 0; j < k; ++j) {
-        const int r = row_of_slot[t * k + j];
+        int r = row_of_slot[t * k + j];
         if (r < 0) continue;
+        if constexpr (SLOTS) r = static_cast<int>(t * k + j);
         const float w = topw[t * k + j];
         const uint4 u = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(r) * H) + c);
         const T* v = reinterpret_cast<const T*>(&u);
@@ -335,6 +338,18 @@ __global__ void combine_kernel(const T* __restrict__ y, const int32_t* __restric
       for (int e = 0; e < 8; ++e) oo[e] = from_f32<T>(acc[e]);
       reinterpret_cast<uint4*>(out + t * H)[c] = o;
     }
+  }
+}
+
+// out[i] = map[ids[i]] for ids in [0, E), else ids[i] (the plan drops those).
+__global__ void map_ids_kernel(const int32_t* __restrict__ ids, int64_t n, const int32_t* __restrict__ map, int E,
+                               int32_t* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int v = ids[i];
+    out[i] = (v >= 0 && v < E) ? __ldg(map + v) : v;
   }
 }
 
@@ -419,6 +434,18 @@ extern "C" int fni8_moe_plan(const int32_t* topi, int64_t n_slots, int64_t E, in
                   stream);
 }
 
+extern "C" int fni8_moe_map_ids(const int32_t* ids, int64_t n, const int32_t* map, int64_t E, int32_t* out,
+                                void* stream) {
+  if (n < 0 || E <= 0) return fail(FNI8_ERR_INVALID, "map_ids: bad sizes");
+  if (n == 0) return FNI8_OK;
+  if (!ids || !map || !out) return fail(FNI8_ERR_INVALID, "map_ids: null pointer");
+  const int64_t blocks = (n + 255) / 256;
+  launch_pdl(moe::map_ids_kernel, dim3((int)(blocks < 148 * 4 ? blocks : 148 * 4)), dim3(256), 0,
+             static_cast<cudaStream_t>(stream), ids, n, map, (int)E, out);
+  FNI8_CHECK_LAUNCH("moe_map_ids");
+  return FNI8_OK;
+}
+
 extern "C" int fni8_moe_gather_rows_i8(const int8_t* q, const float* scale, const int32_t* slot_of_row, int64_t R,
                                        int64_t K, int64_t top_k, int8_t* q_out, float* scale_out, void* stream) {
   if (R < 0 || K <= 0 || top_k <= 0) return fail(FNI8_ERR_INVALID, "gather: bad sizes");
@@ -479,7 +506,7 @@ extern "C" int fni8_grouped_gemm_w8a8_scatter(const int8_t* a, const float* a_sc
   if (R < 0 || E <= 0 || N <= 0 || K <= 0 || S < 0 || peer_rows < 0) return fail(FNI8_ERR_INVALID, "scatter: bad sizes");
   if (world < 1 || world > 8) return fail(FNI8_ERR_INVALID, "scatter: 1 <= world <= 8");
   if (K % 16 != 0) return fail(FNI8_ERR_UNSUPPORTED, "scatter: K must be a multiple of 16");
-  if (N % 32 != 0) return fail(FNI8_ERR_UNSUPPORTED, "scatter: N must be a multiple of 32");
+  if (N % 64 != 0) return fail(FNI8_ERR_UNSUPPORTED, "scatter: N must be a multiple of 64");
   if (R >= (1LL << 31) || N >= (1LL << 31) || K >= (1LL << 31)) return fail(FNI8_ERR_UNSUPPORTED, "scatter: too large");
   if (out_dtype != FNI8_F16 && out_dtype != FNI8_BF16) return fail(FNI8_ERR_INVALID, "scatter: out_dtype F16 or BF16");
   if (R == 0 || S == 0) return FNI8_OK;
@@ -496,8 +523,9 @@ extern "C" int fni8_grouped_gemm_w8a8_scatter(const int8_t* a, const float* a_sc
                            row_tag, peer_out, (int)world, peer_rows);
 }
 
-extern "C" int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,
-                                int64_t top_k, int64_t H, void* out, void* stream) {
+template <bool SLOTS>
+static int combine_any(const void* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,
+                       int64_t top_k, int64_t H, void* out, void* stream) {
   if (T < 0 || top_k <= 0 || H <= 0) return fail(FNI8_ERR_INVALID, "combine: bad sizes");
   if (H % 8 != 0) return fail(FNI8_ERR_UNSUPPORTED, "combine: H must be a multiple of 8");
   if (dtype != FNI8_F16 && dtype != FNI8_BF16) return fail(FNI8_ERR_INVALID, "combine: dtype");
@@ -509,14 +537,24 @@ extern "C" int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_
   const int grid = (int)(T < 148 * 8 ? T : 148 * 8);
   const int threads = (int)((H / 8) < 256 ? ((H / 8 + 31) / 32) * 32 : 256);
   if (dtype == FNI8_F16)
-    launch_pdl(moe::combine_kernel<__half>, dim3(grid), dim3(threads), 0, st, static_cast<const __half*>(y),
+    launch_pdl(moe::combine_kernel<__half, SLOTS>, dim3(grid), dim3(threads), 0, st, static_cast<const __half*>(y),
                row_of_slot, topw, T, (int)top_k, (int)H, static_cast<__half*>(out));
   else
-    launch_pdl(moe::combine_kernel<__nv_bfloat16>, dim3(grid), dim3(threads), 0, st,
+    launch_pdl(moe::combine_kernel<__nv_bfloat16, SLOTS>, dim3(grid), dim3(threads), 0, st,
                static_cast<const __nv_bfloat16*>(y), row_of_slot, topw, T, (int)top_k, (int)H,
                static_cast<__nv_bfloat16*>(out));
   FNI8_CHECK_LAUNCH("moe_combine");
   return FNI8_OK;
+}
+
+extern "C" int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,
+                                int64_t top_k, int64_t H, void* out, void* stream) {
+  return combine_any<false>(y, dtype, row_of_slot, topw, T, top_k, H, out, stream);
+}
+
+extern "C" int fni8_moe_combine_slots(const void* y, int dtype, const int32_t* row_of_slot, const float* topw,
+                                      int64_t T, int64_t top_k, int64_t H, void* out, void* stream) {
+  return combine_any<true>(y, dtype, row_of_slot, topw, T, top_k, H, out, stream);
 }
 
 // Workspace layout of fni8_moe_experts_w8a8 (each piece 256-byte aligned).

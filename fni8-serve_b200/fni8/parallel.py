@@ -38,7 +38,7 @@ import torch
 import torch.distributed as dist
 
 from . import _native as nat
-from .moe import ExpertStack, combine, grouped_gemm, grouped_gemm_act, plan
+from .moe import ExpertStack, combine, combine_slots, grouped_gemm, grouped_gemm_act, plan
 from .ops import (_ACT, _DT, _need_cuda, _stream, _vp, act_and_mul_quant, linear, linear_q_peer_cols,
                   quantize_rows)
 from .qtensor import QTensor
@@ -140,6 +140,20 @@ def p2p_placement(cnt_all: torch.Tensor, rank: int, world: int):
     before = torch.cumsum(c, 0, dtype=torch.int32) - c  # exclusive over sources
     dst_base = (base + before[rank]).contiguous()
     return dst_base, base[rank].contiguous(), tot[rank].contiguous(), tot[rank].sum(dtype=torch.int32).reshape(1)
+
+
+def ep_placement(cnt_all: torch.Tensor, rank: int, world: int):
+    """p2p_placement on the device in one kernel (C: fni8_ep_placement); same outputs, int32."""
+    P, E = cnt_all.shape
+    c = cnt_all.to(torch.int32).contiguous()
+    El = E // world
+    dst_base = torch.empty((world, El), dtype=torch.int32, device=c.device)
+    seg_off = torch.empty(El, dtype=torch.int32, device=c.device)
+    seg_cnt = torch.empty(El, dtype=torch.int32, device=c.device)
+    n_recv = torch.empty(1, dtype=torch.int32, device=c.device)
+    nat.call("fni8_ep_placement", _vp(c), world, rank, E, _vp(dst_base), _vp(seg_off), _vp(seg_cnt), _vp(n_recv),
+             _stream(c.device))
+    return dst_base, seg_off, seg_cnt, n_recv
 
 
 def _cuda_view(ptr: int, nbytes: int, device: torch.device) -> torch.Tensor:
@@ -365,9 +379,15 @@ class ExpertParallelMoE:
         if self.placement is None:
             return topi
         if self._place_dev is None or self._place_dev.device != topi.device:
-            self._place_dev = self.placement.to(device=topi.device, dtype=topi.dtype)
+            self._place_dev = self.placement.to(device=topi.device, dtype=torch.int32)
+        if topi.is_cuda and topi.dtype == torch.int32:  # one kernel (C: fni8_moe_map_ids)
+            t = topi.contiguous()
+            out = torch.empty_like(t)
+            nat.call("fni8_moe_map_ids", _vp(t), t.numel(), _vp(self._place_dev), self.E, _vp(out),
+                     _stream(t.device))
+            return out
         ok = (topi >= 0) & (topi < self.E)
-        return torch.where(ok, self._place_dev[topi.clamp(0, self.E - 1).long()], topi)
+        return torch.where(ok, self._place_dev.to(topi.dtype)[topi.clamp(0, self.E - 1).long()], topi)
 
     def __call__(self, x: torch.Tensor, topi: torch.Tensor, topw: torch.Tensor) -> torch.Tensor:
         topi = self._placed(topi)
@@ -407,7 +427,6 @@ class ExpertParallelMoE:
                 mt = int(m.item())
             self.xchg = PeerExchange(mt, k, H, x.dtype, x.device, self.group)
             self._iota = torch.arange(El, dtype=torch.int32, device=x.device)
-            self._slots = torch.arange(mt * k, dtype=torch.int32, device=x.device)
             self._tick = torch.zeros(1, dtype=torch.int32, device=x.device)
         X = self.xchg
         if not X.fits(T, k, H, x.dtype):
@@ -417,7 +436,7 @@ class ExpertParallelMoE:
         counts, offsets, ros, sor = plan(topi, E)
         cnt_all = torch.empty(P * E, dtype=torch.int32, device=x.device)
         dist.all_gather_into_tensor(cnt_all, counts.to(torch.int32).contiguous(), group=self.group)
-        dst_base, seg_off, seg_cnt, n_recv = p2p_placement(cnt_all.view(P, E), self.rank, P)
+        dst_base, seg_off, seg_cnt, n_recv = ep_placement(cnt_all.view(P, E), self.rank, P)
         ep_dispatch(xq, xs, sor, offsets, E, self.rank, k, dst_base, X, T * k)
         dist.all_reduce(self._tick, op=dist.ReduceOp.MAX, group=self.group)  # every rank's rows have landed
         L = self.local
@@ -435,8 +454,7 @@ class ExpertParallelMoE:
             y = grouped_gemm(hq, hs, L.w_dn, L.s_dn, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
             ep_return(y, n_recv, X)
         dist.all_reduce(self._tick, op=dist.ReduceOp.MAX, group=self.group)  # every output is back at its source
-        ros_slot = torch.where(ros >= 0, self._slots[: T * k], torch.full_like(ros, -1))
-        return combine(X.back[: T * k], ros_slot, topw)
+        return combine_slots(X.back[: T * k], ros, topw)
 
 
 def shard_rows(qt: QTensor, world: int, rank: int) -> QTensor:
@@ -479,8 +497,8 @@ class ColumnParallelLinearW8A8:
                                    shard.data.is_cuda and dist.get_backend(group) == "nccl") else "nccl")
         if transport not in ("p2p", "nccl"):
             raise ValueError(f"unknown transport {transport!r}")
-        if transport == "p2p" and shard.data.shape[0] % 32:
-            raise ValueError(f"p2p column all-gather takes shards of a multiple of 32 columns "
+        if transport == "p2p" and shard.data.shape[0] % 64:
+            raise ValueError(f"p2p column all-gather takes shards of a multiple of 64 columns "
                              f"(got {shard.data.shape[0]})")
         if ring < 1:
             raise ValueError("ring must be at least 1")

@@ -285,9 +285,9 @@ FNI8_API int fni8_grouped_gemm_w8a8_act(const int8_t* a, const float* a_scale, i
  * index). With the tags of fni8_ep_dispatch_i8, the down projection of an expert-parallel
  * layer stores each expert output straight into its source rank's slot over NVLink, tile
  * by tile while later tiles compute: the return step of fni8_ep_return fused into the GEMM
- * epilogue. Rows leave 8 rows x 64 contiguous bytes per store instruction; a tag outside
+ * epilogue. Rows leave 4 rows x 128 contiguous bytes per store instruction; a tag outside
  * the buffers is skipped and reported by fni8_device_status. out_dtype F16 or BF16,
- * N % 32 == 0. */
+ * N % 64 == 0. */
 FNI8_API int fni8_grouped_gemm_w8a8_scatter(const int8_t* a, const float* a_scale, int64_t R, const int8_t* w,
                                             const float* w_scale, int64_t E, int64_t N, int64_t K,
                                             const int32_t* seg_expert, const int32_t* seg_off,
@@ -299,6 +299,11 @@ FNI8_API int fni8_grouped_gemm_w8a8_scatter(const int8_t* a, const float* a_scal
  * weighted index_add_ combine (fni8serve/models/moe.py:97,105). */
 FNI8_API int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,
                      int64_t top_k, int64_t H, void* out, void* stream);
+/* fni8_moe_combine over a slot-indexed y (row t*k + j holds slot j of token t: the back
+ * buffer of an expert-parallel layer, fni8_ep_return / fni8_grouped_gemm_w8a8_scatter);
+ * row_of_slot only marks dropped slots (< 0), whose terms are skipped. */
+FNI8_API int fni8_moe_combine_slots(const void* y, int dtype, const int32_t* row_of_slot, const float* topw,
+                                    int64_t T, int64_t top_k, int64_t H, void* out, void* stream);
 
 /* Routed-expert block of SparseMoE on one GPU (fni8serve/models/moe.py:97-105) given
  * the routing: quantise x, group, gate_up grouped GEMM, act_and_mul + quant, down
@@ -325,6 +330,22 @@ FNI8_API int fni8_ipc_free(void* ptr);
  * fni8_ipc_close unmaps it. */
 FNI8_API int fni8_ipc_open(const void* handle, void** ptr);
 FNI8_API int fni8_ipc_close(void* ptr);
+
+/* Expert ids through a placement: out[i] = map[ids[i]] for ids[i] in [0, E), else ids[i]
+ * (n ids, map [E]). With map[e] = the slot (rank * E/world + local index) that a
+ * load-balanced placement gives expert e, the routing of every token addresses the ranks'
+ * local experts; out may equal ids. */
+FNI8_API int fni8_moe_map_ids(const int32_t* ids, int64_t n, const int32_t* map, int64_t E, int32_t* out,
+                              void* stream);
+
+/* Placement of one exchange on the device, from cnt_all [world, E] (rows each source rank
+ * sends to each expert; expert e lives on rank e / (E / world)): rank d's receive buffer
+ * holds its local experts one after another, each expert's rows ordered by source rank.
+ * Writes dst_base [world * E/world] (where this rank's rows of (owner d, local expert el)
+ * start in d's buffer, as fni8_ep_dispatch_i8 takes it), this rank's received segments
+ * seg_off / seg_cnt [E/world] and their total n_recv [1]. One small kernel. */
+FNI8_API int fni8_ep_placement(const int32_t* cnt_all, int64_t world, int64_t rank, int64_t E, int32_t* dst_base,
+                               int32_t* seg_off, int32_t* seg_cnt, int32_t* n_recv, void* stream);
 
 /* Dispatch: the sorted rows of fni8_moe_plan (slot_of_row, offsets[E + 1]) to the ranks
  * owning their experts (expert e lives on rank e / (E / world)). Row r of local expert el
@@ -357,7 +378,7 @@ FNI8_API int fni8_ep_return(const void* y, int dtype, const int32_t* n_recv, int
  * epilogue, so the slices cross NVLink tile by tile while later tiles compute; decode sizes
  * run the split-K GEMM into tmp [M, N] (tmp_bytes >= M * N * 2) and then one kernel that
  * copies it into the buffers. ws / ws_bytes: the GEMM workspace (fni8_gemm_workspace_bytes,
- * zeroed once). Buffers 16-byte aligned, ld and col_off multiples of 8, N a multiple of 32,
+ * zeroed once). Buffers 16-byte aligned, ld and col_off multiples of 8, N a multiple of 64,
  * K of 16. No rank is waited for: the caller orders the ranks (a collective on the same
  * stream) before any of them reads its buffer. */
 FNI8_API int fni8_gemm_w8a8_peer_cols(const int8_t* a, const float* a_scale, const int8_t* w, const float* w_scale,

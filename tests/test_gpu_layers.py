@@ -169,6 +169,49 @@ def test_grouped_gemm_int32_exact():
             assert torch.equal(got[o:o + c], O.int_mm_fast(a[o:o + c], w[int(perm[s])])), s
 
 
+def test_combine_slots_equals_combine_over_slot_rows():
+    """combine over a slot-indexed buffer (the expert-parallel back buffer) equals the
+    plain combine given row_of_slot = slot for kept slots, -1 for dropped ones."""
+    import fni8.moe as M
+
+    T, k, H = 300, 8, 2048
+    y = (torch.randn(T * k, H, generator=gen(50))).half().to(DEV)
+    ros = torch.randint(0, 5 * T, (T * k,), generator=gen(51), dtype=torch.int32)
+    ros[::7] = -1  # dropped slots
+    topw = torch.rand(T, k, generator=gen(52)).to(DEV)
+    slots = torch.arange(T * k, dtype=torch.int32)
+    want = M.combine(y, torch.where(ros >= 0, slots, -1).to(DEV), topw)
+    assert torch.equal(M.combine_slots(y, ros.to(DEV), topw), want)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_ep_placement_kernel_matches_restatement(world):
+    """The exchange placement kernel (fni8_ep_placement) equals parallel.p2p_placement, the
+    torch restatement the CPU tests pin, for every rank; the expert-id map kernel
+    (fni8_moe_map_ids) equals indexing, ids outside [0, E) passing through."""
+    import ctypes
+
+    from fni8 import _native as nat
+    from fni8.parallel import ep_placement, p2p_placement
+
+    E = 128
+    cnt = torch.randint(0, 300, (world, E), generator=gen(40), dtype=torch.int32)
+    cnt[0, 5] = 0
+    for rank in range(world):
+        want = p2p_placement(cnt, rank, world)
+        got = ep_placement(cnt.to(DEV), rank, world)
+        for w, g in zip(want, got):
+            assert torch.equal(w.reshape(-1).int(), g.cpu().reshape(-1)), rank
+    ids = torch.randint(-2, E + 3, (4096, 8), generator=gen(41), dtype=torch.int32)
+    perm = torch.randperm(E, generator=gen(42)).int()
+    ids_d, perm_d = ids.to(DEV), perm.to(DEV)
+    out = torch.empty_like(ids_d)
+    nat.call("fni8_moe_map_ids", ctypes.c_void_p(ids_d.data_ptr()), ids.numel(), ctypes.c_void_p(perm_d.data_ptr()),
+             E, ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    ok = (ids >= 0) & (ids < E)
+    assert torch.equal(out.cpu(), torch.where(ok, perm[ids.clamp(0, E - 1).long()], ids))
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_grouped_gemm_row_scatter(dtype):
     """The scatter epilogue (expert-parallel return fused into the down projection): every
@@ -249,7 +292,7 @@ def test_linear_peer_cols_all_gather(M, dtype):
 
 def test_linear_peer_cols_rejects_bad_layouts():
     """Host-side checks of the all-gather GEMM: columns past ld, misaligned column offset,
-    a shard width that is not a multiple of 32."""
+    a shard width that is not a multiple of 64."""
     import ctypes
 
     import fni8

@@ -27,13 +27,60 @@ namespace ep {
 
 constexpr int kMaxPeers = 8;
 constexpr int kMaxE = 1024;
-enum : int { kCodeDispatchOverflow = 0x701, kCodeReturnOverflow = 0x702 };
+enum : int { kCodeDispatchOverflow = 0x701, kCodeReturnOverflow = 0x702, kCodeBarrier = 0x703 };
 
 static __device__ int g_status;
 
 struct Peers {
   void* p[kMaxPeers];
 };
+
+// Barrier of the ranks of one node over peer memory, optionally carrying n int32 words
+// of this rank (the all-gather of an exchange's per-expert counts). Every rank holds a
+// flag word per source rank in its buffer `flags` (this rank's flags: flags[me]) and an
+// epoch counter in its own memory. The CTA (1) copies src[0 .. n) to words
+// [me * n, me * n + n) of every rank's dst, (2) takes the next epoch, (3) stores it with
+// release semantics into word `me` of every rank's flags, and (4) waits, with acquire
+// loads, until every word of its own flags has reached the epoch. A rank can run at most
+// one epoch ahead of another (it passes epoch e only after every rank has stored e), so
+// `>= e` (wrap-safe) is the test. The wait is bounded by budget_ns: a rank that never
+// arrives is recorded in the status word and the kernel returns, with no GPU waiting for
+// good. Data stored into peers by kernels before this one on the stream are visible to a
+// peer once it has passed the barrier (those kernels completed, then the release store).
+__global__ void __launch_bounds__(256) barrier_kernel(Peers flags, int P, int me, uint32_t* epoch,
+                                                      const int32_t* __restrict__ src, int n, Peers dst,
+                                                      uint64_t budget_ns) {
+  pdl_wait();  // every store of the previous kernel is done before the flags go out
+  for (int i = threadIdx.x; i < P * n; i += blockDim.x) {
+    const int p = i / n, j = i - p * n;
+    static_cast<int32_t*>(dst.p[p])[me * n + j] = src[j];
+  }
+  __shared__ uint32_t s_e;
+  if (threadIdx.x == 0) {
+    s_e = *epoch + 1u;
+    *epoch = s_e;
+  }
+  __threadfence_system();
+  __syncthreads();
+  const uint32_t e = s_e;
+  if (threadIdx.x < P) {
+    uint32_t* to = static_cast<uint32_t*>(flags.p[threadIdx.x]) + me;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(to), "r"(e) : "memory");
+    const uint32_t* mine = static_cast<const uint32_t*>(flags.p[me]) + threadIdx.x;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0;; ++i) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if (static_cast<int32_t>(v - e) >= 0) break;
+      if ((i & 63u) == 0u && globaltimer_ns() - t0 > budget_ns) {
+        atomicCAS(&g_status, 0, kCodeBarrier);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+}
 
 // Placement of one exchange from cnt_all[s * E + e] (rows source rank s sends to global
 // expert e; experts [d * El, (d + 1) * El) live on rank d). Rank d's receive buffer holds
@@ -260,6 +307,24 @@ static int load_peers(ep::Peers* out, void* const* ptrs, int P, const char* what
     if (ptrs[i] == nullptr) return fail(FNI8_ERR_INVALID, "%s: null peer buffer %d", what, i);
     out->p[i] = ptrs[i];
   }
+  return FNI8_OK;
+}
+
+extern "C" int fni8_peer_barrier(void* const* peer_flags, int64_t world, int64_t rank, uint32_t* epoch,
+                                 const int32_t* src, int64_t n, void* const* peer_dst, int64_t wait_us, void* stream) {
+  if (world < 1 || world > ep::kMaxPeers || rank < 0 || rank >= world)
+    return fail(FNI8_ERR_INVALID, "peer_barrier: 1 <= world <= %d, 0 <= rank < world", ep::kMaxPeers);
+  if (n < 0 || n > 4096 || (n > 0 && (src == nullptr || peer_dst == nullptr)))
+    return fail(FNI8_ERR_INVALID, "peer_barrier: 0 <= n <= 4096 words, src and peer_dst with n > 0");
+  if (wait_us < 1 || wait_us > 1000000) return fail(FNI8_ERR_INVALID, "peer_barrier: wait_us in [1, 1000000]");
+  if (peer_flags == nullptr || epoch == nullptr) return fail(FNI8_ERR_INVALID, "peer_barrier: null pointer");
+  ep::Peers fl, dst{};
+  if (int s = load_peers(&fl, peer_flags, (int)world, "peer_barrier")) return s;
+  if (n > 0)
+    if (int s = load_peers(&dst, peer_dst, (int)world, "peer_barrier")) return s;
+  launch_pdl(ep::barrier_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), fl, (int)world, (int)rank,
+             epoch, src, (int)n, dst, static_cast<uint64_t>(wait_us) * 1000ull);
+  FNI8_CHECK_LAUNCH("peer_barrier");
   return FNI8_OK;
 }
 

@@ -71,6 +71,7 @@ SIGNATURES: dict[str, tuple] = {
     "fni8_ipc_free": (_i, [_p]),
     "fni8_ipc_open": (_i, [_p, ctypes.POINTER(_p)]),
     "fni8_ipc_close": (_i, [_p]),
+    "fni8_peer_barrier": (_i, [_p, _i64, _i64, _p, _p, _i64, _p, _i64, _p]),
     "fni8_moe_map_ids": (_i, [_p, _i64, _p, _i64, _p, _p]),
     "fni8_ep_placement": (_i, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _p]),
     "fni8_ep_dispatch_i8": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64, _p]),

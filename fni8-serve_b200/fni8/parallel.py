@@ -9,13 +9,13 @@ Both are new capabilities sized for an 8 x B200 NVSwitch box.
 Expert parallel (rank r owns E/P experts: [r*E/P, (r+1)*E/P), or those a load-balanced
 placement gives it, balanced_placement), two transports:
   p2p (CUDA tensors, one node): quantise own tokens -> group (token, slot) pairs by expert
-    -> all_gather of per-expert counts (device) -> placement computed on the device ->
-    int8 rows + scales stored straight into the owners' receive buffers (CUDA IPC peer
-    memory over NVLink) -> grouped GEMMs, one segment per local expert -> expert outputs
-    stored straight back into the sources' slot-indexed buffers -> weighted combine. Each
-    exchange is followed by a one-element NCCL all_reduce on the same stream, so a rank
-    reads its buffers only after every rank's stores are done. Nothing visits the host: the
-    layer replays from a CUDA graph.
+    -> per-expert counts all-gathered through peer memory -> placement computed on the
+    device -> int8 rows + scales stored straight into the owners' receive buffers (CUDA
+    IPC peer memory over NVLink) -> grouped GEMMs, one segment per local expert, the down
+    projection's epilogue storing each expert output straight back into its source's
+    slot-indexed buffer -> weighted combine. Each exchange ends in a barrier kernel over
+    peer memory (PeerSync) on the same stream, so a rank reads its buffers only after every
+    rank's stores are done. Nothing visits the host: the layer replays from a CUDA graph.
   nccl (any backend, gloo included): the same steps with all_to_all_single; the split
     sizes visit the host (one small copy per layer).
 Activations cross NVLink as int8 (half the bytes of fp16).
@@ -25,7 +25,7 @@ y[:, slice]; every rank needs all of y. Two transports:
   p2p (CUDA, one node): the GEMM stores its slice straight into every rank's output buffer
     (CUDA IPC peer memory over NVLink): at prefill sizes from the tile GEMM's epilogue, so
     each tile crosses NVLink while later tiles compute; at decode sizes by a copy kernel
-    after the split-K GEMM. One NCCL all_reduce of one element then orders the ranks.
+    after the split-K GEMM. A barrier kernel over peer memory then orders the ranks.
   nccl (any backend): the local GEMM and all_gather_into_tensor, in row chunks whose
     exchanges run asynchronously.
 Rows and columns are independent, so every form gives the single-GPU result bit for bit.
@@ -224,14 +224,45 @@ class PeerBuffer:
         self._own = None
 
 
+class PeerSync:
+    """Barrier of the ranks over peer memory, on the current stream (C: fni8_peer_barrier):
+    the flag words live in a PeerBuffer region of `world` uint32 (zeroed at allocation), the
+    epoch counter in this rank's memory. A call passes once every rank has made the same
+    call, and then sees every store into its memory that the ranks' earlier kernels issued;
+    with `payload` (src [n] int32 on this rank, dst: the PeerBuffer offset of a [world, n]
+    int32 region) it also all-gathers src. Waits are bounded (1 s; fni8.device_status
+    reports a rank that never arrived). Every rank calls the same barriers in the same
+    order."""
+
+    def __init__(self, buf: PeerBuffer, offset: int, device: torch.device):
+        self.world, self.rank = buf.world, buf.rank
+        self._buf = buf
+        self._flags = buf.pointers(offset)
+        self._flags_p = ctypes.cast(self._flags, ctypes.c_void_p)
+        self._epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self._dst = {}
+
+    def __call__(self, src: torch.Tensor | None = None, dst_offset: int | None = None):
+        n = 0 if src is None else src.numel()
+        dst = None
+        if n:
+            if dst_offset not in self._dst:
+                a = self._buf.pointers(dst_offset)
+                self._dst[dst_offset] = (a, ctypes.cast(a, ctypes.c_void_p))
+            dst = self._dst[dst_offset][1]
+        nat.call("fni8_peer_barrier", self._flags_p, self.world, self.rank, _vp(self._epoch),
+                 _vp(src) if n else None, n, dst, 1000000, _stream(self._epoch.device))
+
+
 class PeerExchange:
     """Receive and back buffers of one rank in one PeerBuffer, mapped into every peer of
     `group`: rows [cap] of int8 [H] + fp32 scale + int32 tag received from any rank, and back
-    rows [max_tokens * top_k] of `dtype` [H] returned to this rank's slots.
-    cap = world * max_tokens * top_k covers any routing."""
+    rows [max_tokens * top_k] of `dtype` [H] returned to this rank's slots, plus the
+    per-expert counts of every rank [world, num_experts] and the flag words of the layer's
+    barrier (`sync`). cap = world * max_tokens * top_k covers any routing."""
 
     def __init__(self, max_tokens: int, top_k: int, hidden: int, dtype: torch.dtype, device: torch.device,
-                 group=None):
+                 group=None, num_experts: int = 0):
         self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
         if self.world > 8:
             raise ValueError("the peer-memory exchange spans at most 8 ranks")
@@ -240,7 +271,8 @@ class PeerExchange:
         self.back_rows = max_tokens * top_k
         esz = torch.tensor([], dtype=dtype).element_size()
         parts = [("q", self.cap * hidden), ("s", self.cap * 4), ("tag", self.cap * 4),
-                 ("back", self.back_rows * hidden * esz)]
+                 ("back", self.back_rows * hidden * esz), ("cnt", self.world * max(num_experts, 1) * 4),
+                 ("flags", self.world * 4)]
         self.off, total = {}, 0
         for name, nbytes in parts:
             self.off[name] = total
@@ -255,13 +287,16 @@ class PeerExchange:
         self.tag = mem[self.off["tag"]:self.off["tag"] + self.cap * 4].view(torch.int32)
         self.back = mem[self.off["back"]:self.off["back"] + self.back_rows * hidden * esz].view(dtype).view(
             self.back_rows, hidden)
+        self.num_experts = num_experts
+        self.cnt = mem[self.off["cnt"]:self.off["cnt"] + self.world * max(num_experts, 1) * 4].view(torch.int32)
+        self.sync = PeerSync(self.buf, self.off["flags"], device)
 
     def fits(self, T: int, top_k: int, hidden: int, dtype: torch.dtype) -> bool:
         return T <= self.max_tokens and top_k == self.top_k and hidden == self.hidden and dtype == self.dtype
 
     def close(self, group=None):
         """Unmap the peers' buffers and free this rank's (every rank calls it)."""
-        self.rq = self.rs = self.tag = self.back = None
+        self.rq = self.rs = self.tag = self.back = self.cnt = self.sync = None
         self.buf.close(group)
 
 
@@ -425,20 +460,18 @@ class ExpertParallelMoE:
                 m = torch.tensor([T], dtype=torch.int64, device=x.device)
                 dist.all_reduce(m, op=dist.ReduceOp.MAX, group=self.group)
                 mt = int(m.item())
-            self.xchg = PeerExchange(mt, k, H, x.dtype, x.device, self.group)
+            self.xchg = PeerExchange(mt, k, H, x.dtype, x.device, self.group, num_experts=E)
             self._iota = torch.arange(El, dtype=torch.int32, device=x.device)
-            self._tick = torch.zeros(1, dtype=torch.int32, device=x.device)
         X = self.xchg
         if not X.fits(T, k, H, x.dtype):
             raise ValueError(f"ExpertParallelMoE: {T} tokens x top-{k} x {H} {x.dtype} exceeds the exchange buffers "
                              f"({X.max_tokens} x top-{X.top_k} x {X.hidden} {X.dtype}); pass max_tokens")
         xq, xs = quantize_rows(x)
         counts, offsets, ros, sor = plan(topi, E)
-        cnt_all = torch.empty(P * E, dtype=torch.int32, device=x.device)
-        dist.all_gather_into_tensor(cnt_all, counts.to(torch.int32).contiguous(), group=self.group)
-        dst_base, seg_off, seg_cnt, n_recv = ep_placement(cnt_all.view(P, E), self.rank, P)
+        X.sync(counts.to(torch.int32).contiguous(), X.off["cnt"])  # every rank's counts, all-gathered
+        dst_base, seg_off, seg_cnt, n_recv = ep_placement(X.cnt.view(P, E), self.rank, P)
         ep_dispatch(xq, xs, sor, offsets, E, self.rank, k, dst_base, X, T * k)
-        dist.all_reduce(self._tick, op=dist.ReduceOp.MAX, group=self.group)  # every rank's rows have landed
+        X.sync()  # every rank's rows have landed
         L = self.local
         if L.intermediate % 128 == 0:  # gate_up with act_and_mul in its epilogue
             p = grouped_gemm_act(X.rq, X.rs, L.w_gu, L.s_gu, self._iota, seg_off, seg_cnt, act=self.act,
@@ -453,7 +486,7 @@ class ExpertParallelMoE:
         else:
             y = grouped_gemm(hq, hs, L.w_dn, L.s_dn, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
             ep_return(y, n_recv, X)
-        dist.all_reduce(self._tick, op=dist.ReduceOp.MAX, group=self.group)  # every output is back at its source
+        X.sync()  # every output is back at its source
         return combine_slots(X.back[: T * k], ros, topw)
 
 
@@ -471,8 +504,8 @@ class ColumnParallelLinearW8A8:
 
     transport "p2p" (the sm_100a kernels, NCCL group of at most 8 ranks on one node): the
     GEMM stores this rank's columns straight into every rank's output buffer over NVLink
-    (fni8.ops.linear_q_peer_cols), then a one-element NCCL all_reduce on the same stream
-    orders the ranks; no host synchronisation, so a decode runner can capture it. The
+    (fni8.ops.linear_q_peer_cols), then a barrier kernel over peer memory (PeerSync) on the
+    same stream orders the ranks; no host synchronisation, so a decode runner can capture it. The
     output buffers are the layer's own: `ring` buffers of [max_rows, world * n] in CUDA IPC
     memory (max_rows default: the first call's rows, as a maximum over the ranks), used in
     turn. A call returns a view of its buffer, valid until `ring` more calls of this layer
@@ -550,10 +583,10 @@ class ColumnParallelLinearW8A8:
                 rows = int(m.item())
             self._rows = max(rows, 1)
             self._slot = (self._rows * Nt * 2 + 255) // 256 * 256  # 16-bit outputs
-            self.buf = PeerBuffer(self.ring * self._slot, x2.device, self.group)
+            self.buf = PeerBuffer(self.ring * self._slot + 256, x2.device, self.group)  # + barrier flags
             self._arrays = [self.buf.pointers(i * self._slot) for i in range(self.ring)]
             self._ptrs = [ctypes.cast(a, ctypes.c_void_p) for a in self._arrays]
-            self._tick = torch.zeros(1, dtype=torch.int32, device=x2.device)
+            self._sync = PeerSync(self.buf, self.ring * self._slot, x2.device)
             self._next = 0
         if M > self._rows:
             raise ValueError(f"ColumnParallelLinearW8A8: {M} rows exceed the output buffers ({self._rows}); "
@@ -563,5 +596,5 @@ class ColumnParallelLinearW8A8:
         q, s = quantize_rows(x2)
         linear_q_peer_cols(q, s, self.shard, self._ptrs[i], self.world, Nt, self.rank * n, bias=bias,
                            out_dtype=x2.dtype)
-        dist.all_reduce(self._tick, op=dist.ReduceOp.MAX, group=self.group)  # every rank's columns have landed
+        self._sync()  # every rank's columns have landed
         return self.buf.mem[i * self._slot:i * self._slot + M * Nt * 2].view(x2.dtype).view(M, Nt)

@@ -331,6 +331,20 @@ FNI8_API int fni8_ipc_free(void* ptr);
 FNI8_API int fni8_ipc_open(const void* handle, void** ptr);
 FNI8_API int fni8_ipc_close(void* ptr);
 
+/* Barrier of the `world` ranks of one node over peer memory, on `stream` (no host wait):
+ * each rank passes it once every rank has reached it, and then sees every store into its
+ * memory that the other ranks' kernels issued before their barrier. peer_flags: `world`
+ * pointers to each rank's flag words (world uint32 in memory mapped with fni8_ipc_open,
+ * zeroed once; this rank's own at index rank); epoch: a uint32 counter in this rank's
+ * device memory, zeroed once (every rank runs the same sequence of barriers). With n > 0
+ * the barrier also all-gathers n int32 words: src [n] of this rank lands at words
+ * [rank * n, rank * n + n) of every rank's peer_dst buffer. A rank that has not arrived
+ * after wait_us microseconds (1 .. 1e6) is reported by fni8_device_status and the kernel
+ * returns; no GPU waits for good. Replaces an NCCL all_reduce / all_gather used only as a
+ * barrier between the kernels of an expert-parallel or column-parallel layer. */
+FNI8_API int fni8_peer_barrier(void* const* peer_flags, int64_t world, int64_t rank, uint32_t* epoch,
+                               const int32_t* src, int64_t n, void* const* peer_dst, int64_t wait_us, void* stream);
+
 /* Expert ids through a placement: out[i] = map[ids[i]] for ids[i] in [0, E), else ids[i]
  * (n ids, map [E]). With map[e] = the slot (rank * E/world + local index) that a
  * load-balanced placement gives expert e, the routing of every token addresses the ranks'

@@ -65,3 +65,44 @@ def test_bounded_wait_timeout_is_reported_once_and_scratch_recovered():
     assert torch.equal(out.cpu(), ref)
     assert fni8.device_status() == 0
 
+
+
+def test_peer_barrier_single_rank_and_timeout():
+    """The peer-memory barrier (fni8_peer_barrier) on one GPU: with one rank it passes at
+    once and all-gathers its payload; with a second "rank" whose flag nothing ever sets it
+    gives up after its bound, fni8_device_status reports it once, and the GPU then runs a
+    GEMM exactly (no rank waits for good)."""
+    import ctypes
+
+    import fni8
+    from fni8 import _native as nat
+
+    dev = torch.device("cuda", 0)
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    flags = torch.zeros(2, dtype=torch.int32, device=dev)
+    epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+    src = torch.arange(7, dtype=torch.int32, device=dev) + 100
+    dst = torch.zeros(2 * 7, dtype=torch.int32, device=dev)
+    pf = (ctypes.c_void_p * 1)(flags.data_ptr())
+    pd = (ctypes.c_void_p * 1)(dst.data_ptr())
+    for i in range(3):
+        nat.call("fni8_peer_barrier", ctypes.cast(pf, ctypes.c_void_p), 1, 0, ctypes.c_void_p(epoch.data_ptr()),
+                 ctypes.c_void_p(src.data_ptr()), 7, ctypes.cast(pd, ctypes.c_void_p), 1000000, st)
+    torch.cuda.synchronize()
+    assert int(epoch.item()) == 3 and int(flags[0].item()) == 3
+    assert torch.equal(dst[:7].cpu(), torch.arange(7, dtype=torch.int32) + 100)
+    assert fni8.device_status() == 0
+    # rank 0 of 2: flags[1] (rank 1's word in this rank's buffer) is never set
+    flags2 = torch.zeros(2, dtype=torch.int32, device=dev)
+    other = torch.zeros(2, dtype=torch.int32, device=dev)  # stands in for rank 1's buffer
+    pf2 = (ctypes.c_void_p * 2)(flags2.data_ptr(), other.data_ptr())
+    epoch2 = torch.zeros(1, dtype=torch.int32, device=dev)
+    nat.call("fni8_peer_barrier", ctypes.cast(pf2, ctypes.c_void_p), 2, 0, ctypes.c_void_p(epoch2.data_ptr()), None,
+             0, None, 2000, st)
+    torch.cuda.synchronize()
+    assert int(other[0].item()) == 1  # this rank's arrival was stored into the peer's buffer
+    assert fni8.device_status() == 0x703  # the barrier's code
+    assert fni8.device_status() == 0  # reported once
+    a = torch.randint(-127, 128, (64, 256), dtype=torch.int8, device=dev)
+    w = torch.randint(-127, 128, (128, 256), dtype=torch.int8, device=dev)
+    assert torch.equal(fni8.gemm_i32(a, w).cpu(), a.cpu().int() @ w.cpu().int().T)

@@ -279,50 +279,14 @@ __device__ __forceinline__ void store_slab(uint8_t* buf, const uint4 (&o)[4], in
   }
 }
 
-// Two consecutive chunks (o0: columns [n0, n0 + 32), o1: [n0 + 32, n0 + 64)) of rows
-// [row_base, row_base + nrows) to columns [peer_col + n0, peer_col + n0 + 64) of every
-// peer_out buffer (the column all-gather). The rows pass through the warp's 2 KB buffer
-// sixteen at a time (128 bytes each, 16-byte pieces swizzled by row), so that each store
-// instruction writes 4 rows x 128 contiguous bytes per destination (plain stores: the
-// destinations may be other GPUs' memory).
-__device__ __forceinline__ void store_cols_128(uint8_t* buf, const uint4 (&o0)[4], const uint4 (&o1)[4], int lane,
-                                               const Epi& epi, int n0, int row_base, int nrows) {
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {  // slab rows [16h, 16h + 16)
-    __syncwarp();  // every lane has read the previous rows out of the buffer
-    if ((lane >> 4) == h) {
-      const int rr = lane & 15;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        *reinterpret_cast<uint4*>(buf + rr * 128 + ((j ^ (rr & 7)) << 4)) = o0[j];
-        *reinterpret_cast<uint4*>(buf + rr * 128 + (((j + 4) ^ (rr & 7)) << 4)) = o1[j];
-      }
-    }
-    __syncwarp();
-    const int g = lane & 7;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int rr = 4 * u + (lane >> 3);
-      const int r = 16 * h + rr;
-      if (r < nrows) {
-        const uint4 v = *reinterpret_cast<const uint4*>(buf + rr * 128 + ((g ^ (rr & 7)) << 4));
-        const int64_t off = (static_cast<int64_t>(row_base + r) * epi.peer_ld + epi.peer_col + n0 + 8 * g) * 2;
-        for (int p = 0; p < epi.n_peers; ++p)
-          *reinterpret_cast<uint4*>(static_cast<uint8_t*>(epi.peer_out[p]) + off) = v;
-      }
-    }
-  }
-}
-
-// Two consecutive chunks (o0: columns [n0, n0 + 32), o1: [n0 + 32, n0 + 64)) of the slab's
-// rows to the rows their tags name (the row scatter): row r of the slab (tag: lane r's
-// `tag`) goes to row (tag & 0xFFFFFF) of peer_out[tag >> 24]. The rows pass through the
-// warp's 2 KB buffer sixteen at a time (128 bytes each, 16-byte pieces swizzled by row),
-// so that each store instruction writes 4 rows x 128 contiguous bytes, the NVLink write
-// granule, rather than 64-byte halves. A tag outside the buffers is skipped and recorded
-// in the status word.
-__device__ __forceinline__ void store_rows_128(uint8_t* buf, const uint4 (&o0)[4], const uint4 (&o1)[4], int lane,
-                                               const Epi& epi, int n0, int N, uint32_t tag, int nrows, int* status) {
+// Peer outputs leave 4 rows x 128 contiguous bytes per store instruction (measured on
+// B200: twice the NVLink rate of 64-byte row pieces). Two consecutive 32-column chunks of
+// the slab (o0, o1: this lane's row) pass through the warp's 2 KB buffer sixteen rows at a
+// time (128 bytes per row, 16-byte pieces swizzled by row); put(r, g, v, tag) then stores
+// piece g of slab row r (r < nrows) with lane r's tag.
+template <typename Put>
+__device__ __forceinline__ void stage_rows_128(uint8_t* buf, const uint4 (&o0)[4], const uint4 (&o1)[4], int lane,
+                                               uint32_t tag, int nrows, Put&& put) {
 #pragma unroll
   for (int h = 0; h < 2; ++h) {  // slab rows [16h, 16h + 16)
     __syncwarp();  // every lane has read the previous rows out of the buffer
@@ -341,18 +305,35 @@ __device__ __forceinline__ void store_rows_128(uint8_t* buf, const uint4 (&o0)[4
       const int rr = 4 * u + (lane >> 3);
       const int r = 16 * h + rr;
       const uint32_t tg = __shfl_sync(0xffffffffu, tag, r);
-      if (r < nrows) {
-        const int src = static_cast<int>(tg >> 24);
-        const int64_t slot = static_cast<int64_t>(tg & 0xFFFFFFu);
-        if (src < epi.n_peers && slot < epi.peer_rows) {
-          const uint4 v = *reinterpret_cast<const uint4*>(buf + rr * 128 + ((g ^ (rr & 7)) << 4));
-          *reinterpret_cast<uint4*>(static_cast<uint8_t*>(epi.peer_out[src]) + (slot * N + n0 + 8 * g) * 2) = v;
-        } else if (g == 0) {
-          atomicExch(status, kCodeScatter);
-        }
-      }
+      if (r < nrows) put(r, g, *reinterpret_cast<const uint4*>(buf + rr * 128 + ((g ^ (rr & 7)) << 4)), tg);
     }
   }
+}
+
+// Column all-gather: columns [n0, n0 + 64) of rows [row_base, row_base + nrows) to columns
+// [peer_col + n0, peer_col + n0 + 64) of every peer_out buffer (plain stores: the
+// destinations may be other GPUs' memory).
+__device__ __forceinline__ void store_cols_128(uint8_t* buf, const uint4 (&o0)[4], const uint4 (&o1)[4], int lane,
+                                               const Epi& epi, int n0, int row_base, int nrows) {
+  stage_rows_128(buf, o0, o1, lane, 0u, nrows, [&](int r, int g, const uint4& v, uint32_t) {
+    const int64_t off = (static_cast<int64_t>(row_base + r) * epi.peer_ld + epi.peer_col + n0 + 8 * g) * 2;
+    for (int p = 0; p < epi.n_peers; ++p) *reinterpret_cast<uint4*>(static_cast<uint8_t*>(epi.peer_out[p]) + off) = v;
+  });
+}
+
+// Row scatter: columns [n0, n0 + 64) of slab row r (tag: lane r's `tag`) to row
+// (tag & 0xFFFFFF) of peer_out[tag >> 24]. A tag outside the buffers is skipped and
+// recorded in the status word.
+__device__ __forceinline__ void store_rows_128(uint8_t* buf, const uint4 (&o0)[4], const uint4 (&o1)[4], int lane,
+                                               const Epi& epi, int n0, int N, uint32_t tag, int nrows, int* status) {
+  stage_rows_128(buf, o0, o1, lane, tag, nrows, [&](int, int g, const uint4& v, uint32_t tg) {
+    const int src = static_cast<int>(tg >> 24);
+    const int64_t slot = static_cast<int64_t>(tg & 0xFFFFFFu);
+    if (src < epi.n_peers && slot < epi.peer_rows)
+      *reinterpret_cast<uint4*>(static_cast<uint8_t*>(epi.peer_out[src]) + (slot * N + n0 + 8 * g) * 2) = v;
+    else if (g == 0)
+      atomicExch(status, kCodeScatter);
+  });
 }
 
 __device__ __forceinline__ void act_chunk_any(int mode, int act, const uint32_t (&rg)[32], const uint32_t (&ru)[32],

@@ -73,6 +73,14 @@ def _ep_worker(rank, world, port, errq):
         torch.cuda.synchronize()
         assert torch.equal(got, ref), ("placed", (got.float() - ref.float()).abs().max().item())
         epb.close()
+        # bf16 activations through the same exchange (fused return of bf16 rows)
+        xb = x.to(torch.bfloat16)
+        epf = ExpertParallelMoE(placed, E, placement=place)
+        got = epf(xb, topi, topw)
+        refb = moe.experts(xb, topi, topw, full)
+        torch.cuda.synchronize()
+        assert got.dtype == torch.bfloat16 and torch.equal(got, refb), ("bf16", (got.float() - refb.float()).abs().max().item())
+        epf.close()
         for transport, fuse in (("p2p", True), ("p2p", False), ("nccl", False)):
             ep = ExpertParallelMoE(local, E, transport=transport, fuse_return=fuse)
             assert ep.transport == transport
@@ -126,6 +134,8 @@ def _cp_worker(rank, world, port, errq):
         cpn = ColumnParallelLinearW8A8(shard, transport="nccl")
         cpc = ColumnParallelLinearW8A8(shard, transport="nccl", chunk_rows=128)  # 300 rows: 3 chunks
         outs = []
+        bias = (0.1 * torch.randn(N, generator=g, device=dev)).half()
+        bshard = bias.view(world, N // world)[rank].contiguous()
         for M in (1, 16, 300):  # split-K + copy kernel, and the tile GEMM with the stores in its epilogue
             x = torch.randn(M, K, generator=g, device=dev).half()
             ref = fni8.linear(x, full)
@@ -133,6 +143,8 @@ def _cp_worker(rank, world, port, errq):
                 got = layer(x)
                 assert torch.equal(got, ref), (M, layer.transport, (got.float() - ref.float()).abs().max().item())
             outs.append((cp(x, copy=True), ref))
+            got = cp(x, bias=bshard)  # each rank's bias slice, applied in its epilogue
+            assert torch.equal(got, fni8.linear(x, full, bias)), ("bias", M)
         for got, ref in outs:  # copies stay valid after later calls reuse the ring
             assert torch.equal(got, ref)
         # no host synchronisation: the p2p layer replays from a CUDA graph

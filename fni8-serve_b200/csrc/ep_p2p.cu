@@ -6,9 +6,13 @@
 //
 //   dispatch  local rows sorted by expert (the plan) -> the owner rank d of the expert, at
 //             dst_base[d][local expert] + the row's rank among this rank's rows of that
-//             expert: int8 row, fp32 scale and a tag (source rank << 24 | slot)
+//             expert: int8 row, fp32 scale and a tag (source rank << 24 | the row's
+//             index in the source's expert-sorted order)
 //   return    every received row's expert output -> the back buffer of its source rank at
-//             the slot index, where the source combines its tokens
+//             the tag's sorted-row index, where the source combines its tokens through
+//             its own row map (row_of_slot). An owner's rows of one expert and one source
+//             are consecutive sorted rows of that source, so the rows of a tile land in a
+//             few contiguous runs of the sources' buffers rather than at random slots
 //
 // Ordering between ranks is the caller's: after each exchange kernel every rank runs a
 // small NCCL all_reduce on the same stream, which a rank passes only once every rank's
@@ -169,14 +173,14 @@ __global__ void dispatch_kernel(const int8_t* __restrict__ q, const float* __res
     warp_copy(dst, src, H / 16, lane);
     if (lane == 0) {
       static_cast<float*>(ps.p[d])[pos] = __ldg(scale + t);
-      static_cast<int32_t*>(ptag.p[d])[pos] = (me << 24) | slot;
+      static_cast<int32_t*>(ptag.p[d])[pos] = (me << 24) | static_cast<int32_t>(r);
     }
   }
   __threadfence_system();
 }
 
 // One warp per received row i < *n_recv: y[i] -> back buffer of the tag's source rank at
-// the tag's slot.
+// the tag's sorted-row index.
 template <typename T>
 __global__ void return_kernel(const T* __restrict__ y, const int32_t* __restrict__ n_recv, int64_t cap_rows,
                               const int32_t* __restrict__ tag, int H, Peers pb, int P, int64_t back_rows) {

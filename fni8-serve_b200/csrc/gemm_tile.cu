@@ -80,6 +80,7 @@ struct Epi {
   int64_t peer_ld;
   const int32_t* row_tag;
   int64_t peer_rows;
+  int band;  // m-tiles per band of the dense tile order (0: kGroupM)
   // ACTMUL kernels (gate_up with act_and_mul in the epilogue): the weight holds the gate
   // rows [0, act_i) and the up rows [act_i, 2 act_i); tile n covers gate rows
   // [128 n, 128 n + 128) in accumulator columns 0-127 and the matching up rows in columns
@@ -122,10 +123,11 @@ struct TileCoord {
 };
 
 // Tile t -> rows [row0, row0 + rows_valid) (rows_valid <= BMT) and weight block n_blk.
+// Dense tiles are visited in bands of `band` m-tiles, m-tile fastest within a band.
 template <bool GROUPED, int BMT>
 __device__ __forceinline__ TileCoord decode_tile(int t, int M, int m_tiles, int n_tiles, const int32_t* prefix,
                                                  const int32_t* soff, const int32_t* scnt, const int32_t* sexp,
-                                                 int S) {
+                                                 int S, int band) {
   TileCoord tc;
   if constexpr (GROUPED) {
     const int mt = t / n_tiles;
@@ -141,11 +143,11 @@ __device__ __forceinline__ TileCoord decode_tile(int t, int M, int m_tiles, int 
     tc.rows_valid = min(BMT, scnt[lo] - ml * BMT);
     tc.expert = sexp[lo];
   } else {
-    const int band_tiles = kGroupM * n_tiles;
-    const int band = t / band_tiles;
-    const int first_m = band * kGroupM;
-    const int gm = min(kGroupM, m_tiles - first_m);
-    const int local = t - band * band_tiles;
+    const int band_tiles = band * n_tiles;
+    const int b = t / band_tiles;
+    const int first_m = b * band;
+    const int gm = min(band, m_tiles - first_m);
+    const int local = t - b * band_tiles;
     const int m_blk = first_m + local % gm;
     tc.n_blk = local / gm;
     tc.row0 = m_blk * BMT;
@@ -413,6 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int n_tiles = (N + BN - 1) / BN;
   const int m_tiles = (M + C::BMT - 1) / C::BMT;
+  const int band = epi.band > 0 ? epi.band : kGroupM;
   const int kb = (K + BK - 1) / BK;
   int S = 0;
   if constexpr (GROUPED) {
@@ -456,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int t = t0, k = 0;
       TileCoord tc{};
-      if (t < total) tc = decode_tile<GROUPED, C::BMT>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
+      if (t < total) tc = decode_tile<GROUPED, C::BMT>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S, band);
       // this CTA's A rows and weight rows of a tile; stage loads complete on the even CTA's
       // barrier under PAIR, which is armed with the bytes of both CTAs
       const int a_off = static_cast<int>(half) * BM;
@@ -500,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++k == kb) {
           k = 0;
           t += tstep;
-          if (t < total) tc = decode_tile<GROUPED, C::BMT>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
+          if (t < total) tc = decode_tile<GROUPED, C::BMT>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S, band);
         }
       };
       if constexpr (!GROUPED) {
@@ -519,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (++kk == kb) {
               kk = 0;
               tt += tstep;
-              if (tt < total) nb = decode_tile<GROUPED, C::BMT>(tt, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S).n_blk;
+              if (tt < total) nb = decode_tile<GROUPED, C::BMT>(tt, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S, band).n_blk;
             }
           }
         }
@@ -624,7 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t aph = 0;
     if (tma_store && lane == 0) tma_prefetch_desc(&tmOut);
     for (int t = t0; t < total; t += tstep) {
-      const TileCoord tc = decode_tile<GROUPED, C::BMT>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S);
+      const TileCoord tc = decode_tile<GROUPED, C::BMT>(t, M, m_tiles, n_tiles, prefix, soff, scnt, sexp, S, band);
       // this CTA's rows of the tile
       const int row0 = tc.row0 + static_cast<int>(half) * BM;
       const int rows_here = tc.rows_valid - static_cast<int>(half) * BM;
@@ -918,6 +921,16 @@ int tile_gemm_peer_cols(const int8_t* a, const float* a_scale, const int8_t* w, 
   epi.peer_col = (int)col_off;
   epi.peer_ld = ld;
   for (int i = 0; i < n_peers; ++i) epi.peer_out[i] = peer_out[i];
+  // The tiles in flight cover about `band` m-tiles of rows, and their peer stores touch
+  // n_peers * rows * ld * 2 bytes of destination memory. Bands are narrowed so that stays
+  // under 512 MB: measured at M=4096, ld=28672 on B200s, 0.9 GB in flight (4 ranks,
+  // bands of 16 m-tiles) stored at the NVLink rate, 1.9 GB (8 ranks) at ~60 GB/s. Narrower
+  // bands than needed cost L2 reuse of the weights (2 ranks, 1 m-tile per band: +16 %).
+  {
+    const int64_t rows = (512ll << 20) / ((int64_t)n_peers * ld * 2);
+    const int64_t b = rows / (pair ? 256 : 128);
+    epi.band = (int)(b < 1 ? 1 : (b > tile::kGroupM ? tile::kGroupM : b));
+  }
   tile::Groups grp{nullptr, nullptr, nullptr, 0};
   const int bmt = pair ? 256 : 128;
   const int64_t tiles = ((M + bmt - 1) / bmt) * ((N + bn - 1) / bn);

@@ -311,9 +311,7 @@ __global__ void gather_rows(const int8_t* __restrict__ q, const float* __restric
   }
 }
 
-// SLOTS: y is indexed by slot (row t*k + j holds slot j of token t, the expert-parallel back
-// buffer); row_of_slot only marks dropped slots (< 0).
-template <typename T, bool SLOTS = false>
+template <typename T>
 __global__ void combine_kernel(const T* __restrict__ y, const int32_t* __restrict__ row_of_slot,
                                const float* __restrict__ topw, int64_t Tn, int k, int H, T* __restrict__ out) {
   pdl_launch_dependents();
@@ -323,9 +321,8 @@ __global__ void combine_kernel(const T* __restrict__ y, const int32_t* __restric
     for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       for (int j = 0; j < k; ++j) {
-        int r = row_of_slot[t * k + j];
+        const int r = row_of_slot[t * k + j];
         if (r < 0) continue;
-        if constexpr (SLOTS) r = static_cast<int>(t * k + j);
         const float w = topw[t * k + j];
         const uint4 u = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(r) * H) + c);
         const T* v = reinterpret_cast<const T*>(&u);
@@ -523,9 +520,8 @@ extern "C" int fni8_grouped_gemm_w8a8_scatter(const int8_t* a, const float* a_sc
                            row_tag, peer_out, (int)world, peer_rows);
 }
 
-template <bool SLOTS>
-static int combine_any(const void* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,
-                       int64_t top_k, int64_t H, void* out, void* stream) {
+extern "C" int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,
+                                int64_t top_k, int64_t H, void* out, void* stream) {
   if (T < 0 || top_k <= 0 || H <= 0) return fail(FNI8_ERR_INVALID, "combine: bad sizes");
   if (H % 8 != 0) return fail(FNI8_ERR_UNSUPPORTED, "combine: H must be a multiple of 8");
   if (dtype != FNI8_F16 && dtype != FNI8_BF16) return fail(FNI8_ERR_INVALID, "combine: dtype");
@@ -537,24 +533,14 @@ static int combine_any(const void* y, int dtype, const int32_t* row_of_slot, con
   const int grid = (int)(T < 148 * 8 ? T : 148 * 8);
   const int threads = (int)((H / 8) < 256 ? ((H / 8 + 31) / 32) * 32 : 256);
   if (dtype == FNI8_F16)
-    launch_pdl(moe::combine_kernel<__half, SLOTS>, dim3(grid), dim3(threads), 0, st, static_cast<const __half*>(y),
+    launch_pdl(moe::combine_kernel<__half>, dim3(grid), dim3(threads), 0, st, static_cast<const __half*>(y),
                row_of_slot, topw, T, (int)top_k, (int)H, static_cast<__half*>(out));
   else
-    launch_pdl(moe::combine_kernel<__nv_bfloat16, SLOTS>, dim3(grid), dim3(threads), 0, st,
+    launch_pdl(moe::combine_kernel<__nv_bfloat16>, dim3(grid), dim3(threads), 0, st,
                static_cast<const __nv_bfloat16*>(y), row_of_slot, topw, T, (int)top_k, (int)H,
                static_cast<__nv_bfloat16*>(out));
   FNI8_CHECK_LAUNCH("moe_combine");
   return FNI8_OK;
-}
-
-extern "C" int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,
-                                int64_t top_k, int64_t H, void* out, void* stream) {
-  return combine_any<false>(y, dtype, row_of_slot, topw, T, top_k, H, out, stream);
-}
-
-extern "C" int fni8_moe_combine_slots(const void* y, int dtype, const int32_t* row_of_slot, const float* topw,
-                                      int64_t T, int64_t top_k, int64_t H, void* out, void* stream) {
-  return combine_any<true>(y, dtype, row_of_slot, topw, T, top_k, H, out, stream);
 }
 
 // Workspace layout of fni8_moe_experts_w8a8 (each piece 256-byte aligned).

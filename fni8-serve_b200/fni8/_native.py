@@ -62,7 +62,6 @@ SIGNATURES: dict[str, tuple] = {
     "fni8_grouped_gemm_w8a8": (_i, [_p, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _i, _p]),
     "fni8_grouped_gemm_w8a8_scatter": (_i, [_p, _p, _i64, _p, _p, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _p, _i64,
                                             _i64, _i, _p]),
-    "fni8_moe_combine_slots": (_i, [_p, _i, _p, _p, _i64, _i64, _i64, _p, _p]),
     "fni8_moe_combine": (_i, [_p, _i, _p, _p, _i64, _i64, _i64, _p, _p]),
     "fni8_moe_experts_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "fni8_moe_experts_w8a8": (_i, [_p, _i, _i64, _i64, _p, _p, _i64, _p, _p, _p, _p, _i64, _i64, _i, _p, _p, _sz,

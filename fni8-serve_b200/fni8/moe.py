@@ -142,18 +142,6 @@ def combine(y: torch.Tensor, row_of_slot: torch.Tensor, topw: torch.Tensor) -> t
     return out
 
 
-def combine_slots(y: torch.Tensor, row_of_slot: torch.Tensor, topw: torch.Tensor) -> torch.Tensor:
-    """combine over a slot-indexed y (y[t*k + j] is slot j of token t); slots with
-    row_of_slot < 0 were dropped (C: fni8_moe_combine_slots)."""
-    _need_cuda(y, "moe.combine_slots")
-    T, k = topw.shape
-    H = y.shape[-1]
-    out = torch.empty((T, H), dtype=y.dtype, device=y.device)
-    nat.call("fni8_moe_combine_slots", _vp(y.contiguous()), _DT[y.dtype], _vp(row_of_slot.int().contiguous()),
-             _vp(topw.float().contiguous()), T, k, H, _vp(out), _stream(y.device))
-    return out
-
-
 class ExpertStack:
     """All experts' int8 weights stacked for the grouped GEMM: gate_up [E, 2I, H],
     down [E, H, I] with per-row fp32 scales [E, 2I] / [E, H]."""

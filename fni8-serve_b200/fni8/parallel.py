@@ -38,7 +38,7 @@ import torch
 import torch.distributed as dist
 
 from . import _native as nat
-from .moe import ExpertStack, combine, combine_slots, grouped_gemm, grouped_gemm_act, plan
+from .moe import ExpertStack, combine, grouped_gemm, grouped_gemm_act, plan
 from .ops import (_ACT, _DT, _need_cuda, _stream, _vp, act_and_mul_quant, linear, linear_q_peer_cols,
                   quantize_rows)
 from .qtensor import QTensor
@@ -487,7 +487,7 @@ class ExpertParallelMoE:
             y = grouped_gemm(hq, hs, L.w_dn, L.s_dn, self._iota, seg_off, seg_cnt, out_dtype=x.dtype)
             ep_return(y, n_recv, X)
         X.sync()  # every output is back at its source
-        return combine_slots(X.back[: T * k], ros, topw)
+        return combine(X.back[: T * k], ros, topw)  # back rows in this rank's sorted order
 
 
 def shard_rows(qt: QTensor, world: int, rank: int) -> QTensor:

@@ -283,7 +283,7 @@ FNI8_API int fni8_grouped_gemm_w8a8_act(const int8_t* a, const float* a_scale, i
  * stored as row (row_tag[r] & 0xFFFFFF) of peer_out[row_tag[r] >> 24], a [peer_rows, N]
  * buffer of that rank mapped into this process (fni8_ipc_open; this rank's own at its
  * index). With the tags of fni8_ep_dispatch_i8, the down projection of an expert-parallel
- * layer stores each expert output straight into its source rank's slot over NVLink, tile
+ * layer stores each expert output straight into its source rank's back buffer over NVLink, tile
  * by tile while later tiles compute: the return step of fni8_ep_return fused into the GEMM
  * epilogue. Rows leave 4 rows x 128 contiguous bytes per store instruction; a tag outside
  * the buffers is skipped and reported by fni8_device_status. out_dtype F16 or BF16,
@@ -299,12 +299,6 @@ FNI8_API int fni8_grouped_gemm_w8a8_scatter(const int8_t* a, const float* a_scal
  * weighted index_add_ combine (fni8serve/models/moe.py:97,105). */
 FNI8_API int fni8_moe_combine(const void* y, int dtype, const int32_t* row_of_slot, const float* topw, int64_t T,
                      int64_t top_k, int64_t H, void* out, void* stream);
-/* fni8_moe_combine over a slot-indexed y (row t*k + j holds slot j of token t: the back
- * buffer of an expert-parallel layer, fni8_ep_return / fni8_grouped_gemm_w8a8_scatter);
- * row_of_slot only marks dropped slots (< 0), whose terms are skipped. */
-FNI8_API int fni8_moe_combine_slots(const void* y, int dtype, const int32_t* row_of_slot, const float* topw,
-                                    int64_t T, int64_t top_k, int64_t H, void* out, void* stream);
-
 /* Routed-expert block of SparseMoE on one GPU (fni8serve/models/moe.py:97-105) given
  * the routing: quantise x, group, gate_up grouped GEMM, act_and_mul + quant, down
  * grouped GEMM, weighted combine. w_gu [E, 2I, H], w_dn [E, H, I] int8 with per-row
@@ -365,7 +359,7 @@ FNI8_API int fni8_ep_placement(const int32_t* cnt_all, int64_t world, int64_t ra
  * owning their experts (expert e lives on rank e / (E / world)). Row r of local expert el
  * of rank d goes to position dst_base[d * (E / world) + el] + (r - offsets[e]) of rank d's
  * receive buffers: the int8 row q[slot / top_k] (H bytes) into peer_q[d], its scale into
- * peer_scale[d] and the tag (rank << 24 | slot) into peer_tag[d]. peer_* are `world` device
+ * peer_scale[d] and the tag (rank << 24 | r) into peer_tag[d]. peer_* are `world` device
  * pointers (this rank's own buffers at index rank); cap_rows is the rows each receive
  * buffer holds (a row past it is skipped and reported by fni8_device_status); max_rows
  * bounds the sorted rows (T * top_k, < 2^24). */
@@ -375,7 +369,8 @@ FNI8_API int fni8_ep_dispatch_i8(const int8_t* q, const float* scale, const int3
                                  void* const* peer_tag, int64_t cap_rows, int64_t max_rows, void* stream);
 /* Return: row i < *n_recv of y[cap_rows, H] (dtype) goes to row (tag[i] & 0xFFFFFF) of the
  * back buffer of rank tag[i] >> 24 (peer_back: `world` device pointers to [back_rows, H]
- * buffers), where that rank combines its tokens with fni8_moe_combine. */
+ * buffers): the source's sorted row r, so that rank combines its tokens with
+ * fni8_moe_combine over its own row_of_slot. */
 FNI8_API int fni8_ep_return(const void* y, int dtype, const int32_t* n_recv, int64_t cap_rows, const int32_t* tag,
                             int64_t H, int64_t world, void* const* peer_back, int64_t back_rows, void* stream);
 

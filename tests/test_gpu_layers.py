@@ -169,21 +169,6 @@ def test_grouped_gemm_int32_exact():
             assert torch.equal(got[o:o + c], O.int_mm_fast(a[o:o + c], w[int(perm[s])])), s
 
 
-def test_combine_slots_equals_combine_over_slot_rows():
-    """combine over a slot-indexed buffer (the expert-parallel back buffer) equals the
-    plain combine given row_of_slot = slot for kept slots, -1 for dropped ones."""
-    import fni8.moe as M
-
-    T, k, H = 300, 8, 2048
-    y = (torch.randn(T * k, H, generator=gen(50))).half().to(DEV)
-    ros = torch.randint(0, 5 * T, (T * k,), generator=gen(51), dtype=torch.int32)
-    ros[::7] = -1  # dropped slots
-    topw = torch.rand(T, k, generator=gen(52)).to(DEV)
-    slots = torch.arange(T * k, dtype=torch.int32)
-    want = M.combine(y, torch.where(ros >= 0, slots, -1).to(DEV), topw)
-    assert torch.equal(M.combine_slots(y, ros.to(DEV), topw), want)
-
-
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_ep_placement_kernel_matches_restatement(world):
     """The exchange placement kernel (fni8_ep_placement) equals parallel.p2p_placement, the

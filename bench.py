@@ -805,7 +805,7 @@ def run_config4(args, world, rank, dev):
                               "GB/s": round((n * K + 2 * M * K + 2 * M * n) / (t * 1e-3) / 1e9, 1)}
         if cp is not None:
             # the whole column-parallel call: quantise, GEMM with the all-gather stores, the
-            # ordering all_reduce. Bound: the slower of the shard's int8 work at the nominal
+            # ordering barrier. Bound: the slower of the shard's int8 work at the nominal
             # peak and the (world-1)/world of the output each rank receives over NVLink at the
             # measured 770 GB/s per direction.
             tg = per_launch_ms(lambda x=x: cp(x), reps=10)

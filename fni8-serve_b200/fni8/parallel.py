@@ -13,7 +13,7 @@ placement gives it, balanced_placement), two transports:
     device -> int8 rows + scales stored straight into the owners' receive buffers (CUDA
     IPC peer memory over NVLink) -> grouped GEMMs, one segment per local expert, the down
     projection's epilogue storing each expert output straight back into its source's
-    slot-indexed buffer -> weighted combine. Each exchange ends in a barrier kernel over
+    buffer, at the row's index in the source's expert-sorted order -> weighted combine. Each exchange ends in a barrier kernel over
     peer memory (PeerSync) on the same stream, so a rank reads its buffers only after every
     rank's stores are done. Nothing visits the host: the layer replays from a CUDA graph.
   nccl (any backend, gloo included): the same steps with all_to_all_single; the split
@@ -229,7 +229,7 @@ class PeerSync:
     the flag words live in a PeerBuffer region of `world` uint32 (zeroed at allocation), the
     epoch counter in this rank's memory. A call passes once every rank has made the same
     call, and then sees every store into its memory that the ranks' earlier kernels issued;
-    with `payload` (src [n] int32 on this rank, dst: the PeerBuffer offset of a [world, n]
+    given src (n int32 on this rank) and dst_offset (the PeerBuffer offset of a [world, n]
     int32 region) it also all-gathers src. Waits are bounded (1 s; fni8.device_status
     reports a rank that never arrived). Every rank calls the same barriers in the same
     order."""
@@ -257,7 +257,8 @@ class PeerSync:
 class PeerExchange:
     """Receive and back buffers of one rank in one PeerBuffer, mapped into every peer of
     `group`: rows [cap] of int8 [H] + fp32 scale + int32 tag received from any rank, and back
-    rows [max_tokens * top_k] of `dtype` [H] returned to this rank's slots, plus the
+    rows [max_tokens * top_k] of `dtype` [H] returned in this rank's expert-sorted row order,
+    plus the
     per-expert counts of every rank [world, num_experts] and the flag words of the layer's
     barrier (`sync`). cap = world * max_tokens * top_k covers any routing."""
 

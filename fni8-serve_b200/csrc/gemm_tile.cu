@@ -921,16 +921,12 @@ int tile_gemm_peer_cols(const int8_t* a, const float* a_scale, const int8_t* w, 
   epi.peer_col = (int)col_off;
   epi.peer_ld = ld;
   for (int i = 0; i < n_peers; ++i) epi.peer_out[i] = peer_out[i];
-  // The tiles in flight cover about `band` m-tiles of rows, and their peer stores touch
-  // n_peers * rows * ld * 2 bytes of destination memory. Bands are narrowed so that stays
-  // under 512 MB: measured at M=4096, ld=28672 on B200s, 0.9 GB in flight (4 ranks,
-  // bands of 16 m-tiles) stored at the NVLink rate, 1.9 GB (8 ranks) at ~60 GB/s. Narrower
-  // bands than needed cost L2 reuse of the weights (2 ranks, 1 m-tile per band: +16 %).
-  {
-    const int64_t rows = (512ll << 20) / ((int64_t)n_peers * ld * 2);
-    const int64_t b = rows / (pair ? 256 : 128);
-    epi.band = (int)(b < 1 ? 1 : (b > tile::kGroupM ? tile::kGroupM : b));
-  }
+  // Tile bands (m-tiles per band): measured on B200s at M=4096, ld=28672 (K=8192), 2 and 4
+  // ranks run fastest with the prefill's bands of 16 m-tiles, whose waves reuse the
+  // weights from L2 (373 and 362 us per call; bands of 1 and 9 m-tiles: 425 and 513 us);
+  // on 8 ranks those bands, with all 4096 rows in flight towards eight destinations, store
+  // at ~60 GB/s (3.4 ms per call) and bands of 4 m-tiles (~1400 rows in flight) take 1.0 ms.
+  epi.band = n_peers > 4 ? 4 : tile::kGroupM;
   tile::Groups grp{nullptr, nullptr, nullptr, 0};
   const int bmt = pair ? 256 : 128;
   const int64_t tiles = ((M + bmt - 1) / bmt) * ((N + bn - 1) / bn);

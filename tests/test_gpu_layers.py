@@ -239,21 +239,22 @@ def test_grouped_gemm_row_scatter(dtype):
         assert bool((bufs[b][unused.to(DEV)] == -7.0).all())
 
 
-@pytest.mark.parametrize("M", [1, 40, 256, 300, 1000])
+@pytest.mark.parametrize("M,P", [(1, 3), (40, 3), (256, 3), (300, 3), (1000, 3), (1000, 6), (4100, 8)])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_linear_peer_cols_all_gather(M, dtype):
+def test_linear_peer_cols_all_gather(M, P, dtype):
     """The column all-gather GEMM (fni8_gemm_w8a8_peer_cols): a shard's outputs land at its
     column offset in every destination buffer, bit-exact against the plain GEMM, and nothing
     outside those columns and rows is written. Three local buffers stand in for three ranks'
-    output buffers; the sizes cover the split-K + copy path (M <= 256) and the tile GEMM with
-    the stores in its epilogue (CTA pairs from 256 rows, a partial last tile at 300/1000)."""
+    output buffers (six and eight for the narrower tile bands used beyond four ranks); the
+    sizes cover the split-K + copy path (M <= 256) and the tile GEMM with the stores in its
+    epilogue (CTA pairs from 256 rows, a partial last tile at 300/1000/4100)."""
     import ctypes
 
     import fni8
     from fni8 import QTensor
     from fni8.ops import linear_q_peer_cols
 
-    K, n, P, rank = 1024, 768, 3, 1
+    K, n, rank = 1024, 768, 1
     Nt, rows = P * n, M + 5
     x = (torch.randn(M, K, generator=gen(30)) * 2).to(dtype).to(DEV)
     w = torch.randint(-127, 128, (n, K), generator=gen(31), dtype=torch.int8).to(DEV)
